@@ -1,0 +1,362 @@
+#!/usr/bin/env python
+"""bench.py -- FRNN throughput on the benchmark workload.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl engine|reference]
+                    [--config C]
+
+Workload (default ``--config 2``): D=3, N=1,000,000
+points from a 64-component Gaussian mixture (sigma=0.02), K=32, radius
+calibrated for 24 mean in-radius neighbours, self-query.  One step = one full
+search (grid build + neighbour search + results in the reference layout) of
+one cloud.
+
+Multi-GPU (one process per GPU under torchrun): every rank searches its own
+independent cloud (seed 1234+rank, same radius); no data-path collective, so
+scaling is weak.  ``value`` = all ranks' queries / max-over-ranks step time.
+
+Timing: W untimed warm-up steps, then exactly K timed steps, bracketed by a
+barrier and torch.cuda.synchronize; each step is timed with CUDA events on the
+engine's stream (the legacy default stream, which is also torch's current
+stream); the L2 is flushed (a 512 MB buffer is overwritten) before every timed
+step.  ``e2e`` times the same search through the host-buffer entry point
+(pinned input copied in, all results copied out, every step).
+
+The reference arm (``--impl reference``) runs the reference engine compiled
+from its own sources for sm_100a (oracle/_ref/libfrnn_ref.so) through its
+FRNNEngine.search_gpu on the same cloud, on rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for p in (os.path.join(ROOT, "pure_cuda-c-_frnn_b200"), os.path.join(ROOT, "oracle")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import numpy as np  # noqa: E402
+
+from frnn_cuda import datagen  # noqa: E402
+
+L2_FLUSH_BYTES = 512 << 20
+METRIC = "FRNN queries/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["engine", "reference"], default="engine")
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), float(j.get("bf16_tflops", 1590.0)), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons of one GPU, sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", gpu_id], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                text=True)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def gpu_uuid(torch, dev: int) -> str:
+    try:
+        return "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        return str(dev)
+
+
+def time_steps(torch, fn, steps, flush):
+    """Per-step device time (ms) of fn with an L2 flush before each step."""
+    total = 0.0
+    for _ in range(steps):
+        flush.zero_()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        total += a.elapsed_time(b)
+    return total / steps
+
+
+def cpu_baseline(soa: np.ndarray, K: int, r: float, budget_s: float = 12.0) -> dict:
+    """The CPU oracle (exact grid search, OpenMP) on a bounded query sample,
+    extrapolated to the whole self-query."""
+    import oracle
+    D, N = soa.shape
+    rng = np.random.default_rng(99)
+    one = np.zeros(1, np.int32)
+    t0 = time.perf_counter()
+    oracle.search_subset(soa, one, K, r)
+    t_build = time.perf_counter() - t0            # grid build + one query
+    nq = min(N, 4096)
+    while True:
+        q = rng.choice(N, nq, replace=False).astype(np.int32)
+        t0 = time.perf_counter()
+        oracle.search_subset(soa, q, K, r)
+        t = time.perf_counter() - t0
+        if t >= 1.0 or nq == N:
+            break
+        nq = min(N, int(nq * max(2.0, min(budget_s, 5.0) / max(t, 1e-3))))
+    t_query = max(t - t_build, 1e-9) / nq
+    total = t_build + t_query * N
+    return {"value": N / total, "unit": "queries/s", "cores": oracle.max_threads(), "kind": "port",
+            "sample": f"oracle (C++/OpenMP exact grid search) on {nq} seeded queries of the same "
+                      f"cloud plus one grid build; extrapolated to all {N} queries"}
+
+
+def run_engine_arm(a, torch, dist, rank, world, dev):
+    import frnn_cuda
+    c = datagen.config(a.config)
+    N, D, K, r = c.N, c.D, c.K, c.radius
+    pts = datagen.generate(c.kind, N, D, seed=datagen.SEED + rank)
+    soa = datagen.soa(pts)
+    x = torch.from_numpy(soa).to(dev)
+    eng = frnn_cuda.FRNNEngine(max_points=N, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    step = lambda: eng.search_gpu(x.data_ptr(), N, D, K, r)  # noqa: E731
+
+    for _ in range(max(3, a.warmup)):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(gpu_uuid(torch, dev))
+    # keep the GPU loaded while nvidia-smi starts, so the clock samples
+    # describe the state the timed steps run in
+    t_end = time.perf_counter() + 1.5
+    while time.perf_counter() < t_end:
+        step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    n0 = eng.launch_count()
+    ms = time_steps(torch, step, a.steps, flush)
+    launches = eng.launch_count() - n0
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+
+    # per-stage device times, from separate instrumented steps
+    eng.set_timing(True)
+    stages = {}
+    for _ in range(5):
+        flush.zero_()
+        step()
+        for k, v in eng.stage_times().items():
+            stages.setdefault(k, []).append(v)
+    eng.set_timing(False)
+    stage_ms = {k: statistics.median(v) for k, v in stages.items()}
+    plan = eng.last_plan()
+
+    ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    value = world * N / (ms_max / 1e3)
+
+    # end-to-end through the host-buffer entry point (pinned buffers)
+    e2e = None
+    if not a.no_e2e:
+        h_in = torch.from_numpy(soa).pin_memory()
+        h_idx = torch.empty((K, N), dtype=torch.int32).pin_memory()
+        h_dst = torch.empty((K, N), dtype=torch.float32).pin_memory()
+        hi, hx, hd = h_in.numpy(), h_idx.numpy(), h_dst.numpy()
+        e2e_step = lambda: eng.search_soa_host(hi, K, r, hx, hd)  # noqa: E731
+        for _ in range(2):
+            e2e_step()
+        if world > 1:
+            dist.barrier()
+        e2e_ms = time_steps(torch, e2e_step, max(3, min(a.steps, 10)), flush)
+        et = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(et, op=dist.ReduceOp.MAX)
+        e2e = {"value": world * N / (float(et.item()) / 1e3), "unit": "queries/s",
+               "h2d_bytes_per_step": int(N * D * 4), "d2h_bytes_per_step": int(N * K * 8),
+               "ms_per_step": float(et.item())}
+
+    if rank != 0:
+        return None
+
+    hbm, bf16, peak_src = measured_peaks()
+    # dominant kernel: the stage with the largest device time
+    dom = max(stage_ms, key=stage_ms.get) if stage_ms else None
+    roofline = None
+    if dom is not None:
+        cells = plan["cells"]
+        row = 16 if D == 3 else ((D + 3) // 4 * 4 if D <= 16 else 32) * 4
+        alg = {
+            # rows read once + K results written + cell starts read
+            "search": N * row + N * K * 8 + 4 * (cells + 1),
+            "unpermute": N * K * 8 * 2 + 4 * N,
+            "scan": 12 * cells,
+            "hash": N * D * 4 + N * 8 + 4 * N,
+            "scatter": N * D * 4 + N * 8 + N * row + 4 * N,
+            "bbox": N * min(D, 4) * 4,
+            "brute": N * D * 4 + N * K * 8,
+        }[dom]
+        t = stage_ms[dom] / 1e3
+        achieved = alg / t / 1e9
+        traffic = None
+        tpath = os.path.join(ROOT, "profiles", "traffic.json")
+        if os.path.exists(tpath):
+            with open(tpath) as f:
+                traffic = json.load(f).get(f"cfg{a.config}", {}).get(dom)
+        roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm,
+                    "unit": "GB/s", "frac": achieved / hbm, "traffic": traffic,
+                    "peak_source": peak_src, "alg_bytes": int(alg), "kernel_ms": stage_ms[dom]}
+    b_alg = 4 * N * (3 * D + 4 + 2 * K) + 12 * plan["cells"]
+    line = {
+        "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_max,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded generator, rank r uses seed 1234+r)",
+        "config": {"workload": c.name, "describe": c.describe, "N": N, "D": D, "K": K,
+                   "radius": r, "queries_per_gpu": N, "l2": "flushed before every timed step",
+                   "parallelism": f"independent clouds x{world}"},
+        "latency_ms": ms_max,
+        "pipeline": {"b_alg_bytes": int(b_alg), "b_alg_gbs": b_alg / (ms_max / 1e3) / 1e9,
+                     "b_alg_frac": b_alg / (ms_max / 1e3) / 1e9 / hbm, "plan": plan,
+                     "stage_ms": stage_ms},
+        "roofline": roofline,
+        "e2e": e2e,
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+    }
+    if world == 1 and not a.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(soa, K, r)
+    return line
+
+
+def run_reference_arm(a, torch, dev):
+    import oracle
+    c = datagen.config(a.config)
+    N, D, K, r = c.N, c.D, c.K, c.radius
+    if not os.path.exists(oracle.REF_SO):
+        return {"impl": "reference", "unavailable": "oracle/_ref/libfrnn_ref.so was not built"}
+    pts = datagen.generate(c.kind, N, D, seed=datagen.SEED)
+    soa = datagen.soa(pts)
+    x = torch.from_numpy(soa).to(dev)
+    ref = oracle.RefEngine(N)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    step = lambda: ref.search_gpu(x.data_ptr(), N, D, K, r)  # noqa: E731
+    for _ in range(max(3, a.warmup)):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(gpu_uuid(torch, dev))
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < 1.0:
+        step()
+    torch.cuda.synchronize()
+    ms = time_steps(torch, step, a.steps, flush)
+    clocks = sampler.stop()
+    ref.close()
+    value = N / (ms / 1e3)
+    return {
+        "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": 1, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded generator, seed 1234)",
+        "impl": "reference",
+        "config": {"workload": c.name, "describe": c.describe, "N": N, "D": D, "K": K,
+                   "radius": r, "l2": "flushed before every timed step"},
+        "latency_ms": ms,
+        "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "cpu_baseline": {"value": value, "unit": "queries/s", "cores": 1, "kind": "reference",
+                         "sample": "the reference FRNNEngine.search_gpu, compiled from its own "
+                                   "sources for sm_100a (oracle/_ref), full workload on GPU 0 "
+                                   "(the reference has no CPU implementation of the path)"},
+        "clocks": clocks,
+    }
+
+
+def main():
+    a = parse()
+    import torch
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if a.impl == "reference":
+        if rank != 0:
+            return 0
+        line = run_reference_arm(a, torch, local)
+        print(json.dumps(line), flush=True)
+        return 0
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    try:
+        line = run_engine_arm(a, torch, dist, rank, world, local)
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+    if rank == 0 and line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

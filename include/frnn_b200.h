@@ -1,0 +1,138 @@
+/*
+ * frnn_b200.h -- C ABI of the B200 fixed-radius nearest-neighbour engine.
+ *
+ * Drop-in boundary for the reference engine DebuRatnam/Pure_CUDA-C-_FRNN:
+ * its Python class frnn_cuda.FRNNEngine (python_interface/nanobind_module.cu:8-21)
+ * is a thin binding over the C++ class FRNNEngine (python_interface/frnn_engine.h:9-55).
+ * Each entry point below replaces one member of that class; the Python module
+ * frnn_cuda in this repository binds these symbols with ctypes.
+ *
+ * Semantics kept from the reference:
+ *   - input points are float32, SoA p[d*N + i] on the device path (grid.h:26-30),
+ *     row-major AoS on the host path (frnn_engine.cu:108-116);
+ *   - self-query: every point is a query against all points (self included);
+ *   - a neighbour of q is any point with squared distance d2 < radius*radius
+ *     (strict), at most K of them, the K smallest;
+ *   - outputs are int32 indices padded with -1 and float32 squared distances
+ *     padded with radius*radius; device results are SoA out[k*N + q]
+ *     (find_nbrs.cu:206-213), host results of frnn_search row-major [q*K + k];
+ *   - limits K <= 128 and D <= 128 (grid.h:59-60);
+ *   - returned device pointers are engine-owned and stay valid until the next
+ *     search call on the same engine (frnn_engine.cu:248-249).
+ *
+ * Differences (all documented in DESIGN.md of this repository):
+ *   - the K slots of a query are returned in ascending (d2, index) order and
+ *     ties at equal d2 are broken by the smaller index, so results are a
+ *     deterministic function of the input (the reference returns heap order
+ *     and breaks ties by nondeterministic visit order);
+ *   - points need not lie in [0,1)^D: the grid is built on the data's bounding
+ *     box (the reference drops points outside [0,1), insert_points.cu:74-87);
+ *   - every entry returns an int status instead of failing silently.
+ *
+ * Threading: one engine is not re-entrant; use one engine per host thread.
+ */
+#ifndef FRNN_B200_H
+#define FRNN_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct frnn_engine frnn_engine;
+
+/* Status codes returned by every entry point. */
+enum frnn_status {
+    FRNN_OK = 0,
+    FRNN_ERR_INVALID_ARG = 1,  /* bad N / dim / K / radius / pointer            */
+    FRNN_ERR_OOM = 2,          /* device or pinned-host allocation failed        */
+    FRNN_ERR_CUDA = 3,         /* a CUDA runtime call or kernel launch failed    */
+    FRNN_ERR_TIMEOUT = 4,      /* a bounded device wait gave up (scan lookback)  */
+    FRNN_ERR_NO_DEVICE = 5,    /* no usable sm_100 device                        */
+    FRNN_ERR_STATE = 6         /* call order violated (e.g. results before search) */
+};
+
+/* Search paths (frnn_engine.cu:215-246 chooses among the reference's three). */
+enum frnn_path {
+    FRNN_PATH_AUTO = 0,        /* dispatcher decides                              */
+    FRNN_PATH_GRID = 1,        /* uniform grid on the leading min(D,4) axes,      *
+                                * full-D ranking (full-D grid when D <= 3)         */
+    FRNN_PATH_BRUTE = 2,       /* tiled brute force, SIMT fp32                    */
+    FRNN_PATH_BRUTE_TC = 3     /* brute force with a tcgen05 distance filter and  *
+                                * exact fp32 re-rank (D a multiple of 16)          */
+};
+
+/* Constructor.  Replaces FRNNEngine::FRNNEngine(int max_points)
+ * (python_interface/frnn_engine.h:11, frnn_engine.cu:23-46).  device = -1
+ * selects the current CUDA device.  Scratch grows lazily with N, D and K. */
+int frnn_create(int max_points, int device, frnn_engine** out);
+
+/* Destructor.  Replaces FRNNEngine::~FRNNEngine (frnn_engine.cu:48-55). */
+int frnn_destroy(frnn_engine* e);
+
+/* Device path.  Replaces FRNNEngine::search_gpu(uintptr_t dev_ptr, int N,
+ * int dim, int K, float radius) (frnn_engine.h:24-26, frnn_engine.cu:195-250).
+ * d_points_soa: caller-owned device memory, SoA [d*N + i], N <= max_points.
+ * On return *d_idxs / *d_dists point at engine-owned SoA results [k*N + q];
+ * the call is blocking like the reference's (its launchers synchronise). */
+int frnn_search_gpu(frnn_engine* e, const float* d_points_soa, int N, int dim, int K,
+                    float radius, int** d_idxs, float** d_dists);
+
+/* Host path.  Replaces FRNNEngine::search(std::vector<float> points_raw, int K,
+ * float radius) (frnn_engine.h:15-19, frnn_engine.cu:104-193).
+ * h_points_aos holds count floats, row-major (N, dim) with N = max_points and
+ * dim = count / max_points (frnn_engine.cu:108).  h_idxs / h_dists receive
+ * N*K values row-major [q*K + k]. */
+int frnn_search(frnn_engine* e, const float* h_points_aos, int64_t count, int K, float radius,
+                int* h_idxs, float* h_dists);
+
+/* Replaces FRNNEngine::get_results(int N, int K) (frnn_engine.h:30,
+ * frnn_engine.cu:252-258): copies the last results device->host in SoA order
+ * [k*N + q].  N and K must match the last search. */
+int frnn_get_results(frnn_engine* e, int N, int K, int* h_idxs, float* h_dists);
+
+/* ---- additions with no reference counterpart ---------------------------- */
+
+/* Human-readable text for a status code / the engine's last error. */
+const char* frnn_status_string(int status);
+const char* frnn_last_error(const frnn_engine* e);
+
+/* Run the engine's work on a caller stream (cudaStream_t; 0 = legacy default
+ * stream, the reference's behaviour and the default). */
+int frnn_set_stream(frnn_engine* e, void* stream);
+
+/* Force a search path (FRNN_PATH_*); FRNN_PATH_AUTO restores the dispatcher. */
+int frnn_set_path(frnn_engine* e, int path);
+
+/* Path taken by the last search and the grid it used (grid_dims = 0 for brute
+ * force; cells = number of dense cells). */
+int frnn_last_plan(const frnn_engine* e, int* path, int* grid_dims, int64_t* cells);
+
+/* Same as frnn_search_gpu but does not wait for the device: results are
+ * ready when the engine's stream reaches this point. */
+int frnn_search_gpu_async(frnn_engine* e, const float* d_points_soa, int N, int dim, int K,
+                          float radius, int** d_idxs, float** d_dists);
+
+/* Host path with caller-provided pinned or pageable buffers in the device
+ * layouts: h_points_soa [d*N + i] in, SoA results [k*N + q] out.  The copies
+ * run on the engine stream; used for end-to-end timing. */
+int frnn_search_host_soa(frnn_engine* e, const float* h_points_soa, int N, int dim, int K,
+                         float radius, int* h_idxs, float* h_dists);
+
+/* Per-stage device timing.  When enabled, each search records CUDA events
+ * around its stages on the engine stream; frnn_last_stage_times writes the
+ * last search's milliseconds for stages 0..n-1 (0 bounding box, 1 cell
+ * histogram, 2 prefix scan, 3 scatter, 4 neighbour search, 5 unpermute,
+ * 6 brute force), -1 for stages that did not run. */
+int frnn_set_timing(frnn_engine* e, int enable);
+int frnn_last_stage_times(frnn_engine* e, float* ms, int n);
+
+/* Number of kernels this engine has launched since it was created. */
+int frnn_launch_count(const frnn_engine* e, int64_t* n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FRNN_B200_H */

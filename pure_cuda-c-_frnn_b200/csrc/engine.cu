@@ -1,0 +1,656 @@
+// engine.cu -- host engine, dispatcher and the C ABI of include/frnn_b200.h.
+//
+// Replaces the reference's FRNNEngine (python_interface/frnn_engine.{h,cu}).
+// Differences by design:
+//   * scratch is allocated lazily from the sizes of each call and kept across
+//     calls (the reference allocates 32-dim / 128-slot buffers up front and
+//     overflows them for D > 32, frnn_engine.cu:26-27);
+//   * all work runs on one stream (the legacy default stream unless the
+//     caller sets another) with no device-wide synchronisation;
+//   * the dispatcher (frnn_engine.cu:215-246 in the reference) decides from
+//     N, D, K, r and the bounding box of the grid axes; no path drops points;
+//   * every CUDA call is checked and reported through the status codes.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "frnn_b200.h"
+#include "frnn_device.cuh"
+#include "frnn_internal.h"
+
+using namespace frnn;
+
+namespace {
+
+struct DevBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+    template <class T>
+    T* as() const { return static_cast<T*>(p); }
+};
+
+constexpr int kBoxMaxBlocks = 1024;
+#define FRNN_STAGES 7   // bbox, hash, scan, scatter, search, unpermute, brute force
+
+// Brute force is taken when the all-pairs work is small enough that the grid
+// build would dominate (the reference's own small-input rule is
+// N^2*D*ceil(K/8) <= 2e6, frnn_engine.cu:215-219; a B200 finishes far larger
+// all-pairs problems in the time of one grid build).
+constexpr double kBruteSmallWork = 4.0e8;   // N*N*D below this -> brute force
+
+}  // namespace
+
+struct frnn_engine {
+    int device = 0;
+    int max_points = 0;
+    int sms = 148;
+    cudaStream_t stream = 0;
+    int forced_path = FRNN_PATH_AUTO;
+    unsigned epoch = 0;
+
+    DevBuf box_partial, box_ticket, box_out;
+    DevBuf counts, starts, scan_status, scan_ticket, err_flag;
+    DevBuf cellrank, rows, ids;
+    DevBuf tmp_idx, tmp_dist, out_idx, out_dist;
+    DevBuf in_stage, in_soa, out_rm_idx, out_rm_dist;
+    float* h_box = nullptr;   // pinned, 9 floats
+    int* h_err = nullptr;     // pinned
+
+    int last_N = -1, last_K = -1;
+    int last_path = 0, last_g = 0;
+    long long last_cells = 0;
+    std::string last_error;
+
+    // per-stage device timing (frnn_set_timing); stage s spans events
+    // ev[2s] .. ev[2s+1] on the engine stream
+    bool timing = false;
+    cudaEvent_t ev[2 * FRNN_STAGES] = {};
+    bool stage_used[FRNN_STAGES] = {};
+    long long launches = 0;
+};
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+int fail(frnn_engine* e, int status, const std::string& msg) {
+    if (e) e->last_error = msg;
+    return status;
+}
+
+int cuda_fail(frnn_engine* e, cudaError_t err, const char* what) {
+    std::string m = std::string(what) + ": " + cudaGetErrorString(err);
+    cudaGetLastError();  // clear a sticky launch error so the engine stays usable
+    return fail(e, err == cudaErrorMemoryAllocation ? FRNN_ERR_OOM : FRNN_ERR_CUDA, m);
+}
+
+#define FRNN_CHECK(e, call, what)                          \
+    do {                                                   \
+        cudaError_t err__ = (call);                        \
+        if (err__ != cudaSuccess) return cuda_fail(e, err__, what); \
+    } while (0)
+
+int grow(frnn_engine* e, DevBuf& b, size_t bytes, const char* what) {
+    if (bytes == 0) bytes = 16;
+    if (b.bytes >= bytes) return FRNN_OK;
+    if (b.p) cudaFree(b.p);
+    b.p = nullptr;
+    b.bytes = 0;
+    // round up to limit regrowth
+    size_t want = bytes + bytes / 8;
+    want = (want + 255) & ~size_t(255);
+    cudaError_t err = cudaMalloc(&b.p, want);
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        b.p = nullptr;
+        return fail(e, FRNN_ERR_OOM, std::string("cudaMalloc failed for ") + what + " (" +
+                                         std::to_string(want) + " bytes)");
+    }
+    b.bytes = want;
+    return FRNN_OK;
+}
+
+#define FRNN_GROW(e, buf, bytes)                                   \
+    do {                                                           \
+        int st__ = grow(e, buf, bytes, #buf);                      \
+        if (st__ != FRNN_OK) return st__;                          \
+    } while (0)
+
+enum Stage { ST_BBOX = 0, ST_HASH, ST_SCAN, ST_SCATTER, ST_SEARCH, ST_UNPERMUTE, ST_BRUTE };
+
+void stage_begin(frnn_engine* e, int st) {
+    if (e->timing) cudaEventRecord(e->ev[2 * st], e->stream);
+}
+void stage_end(frnn_engine* e, int st) {
+    if (e->timing) {
+        cudaEventRecord(e->ev[2 * st + 1], e->stream);
+        e->stage_used[st] = true;
+    }
+}
+
+void free_buf(DevBuf& b) {
+    if (b.p) cudaFree(b.p);
+    b.p = nullptr;
+    b.bytes = 0;
+}
+
+int check_search_args(frnn_engine* e, const void* pts, int N, int dim, int K, float radius) {
+    if (!e) return FRNN_ERR_INVALID_ARG;
+    if (!pts) return fail(e, FRNN_ERR_INVALID_ARG, "points pointer is null");
+    if (N <= 0) return fail(e, FRNN_ERR_INVALID_ARG, "N must be positive");
+    if (N > e->max_points)
+        return fail(e, FRNN_ERR_INVALID_ARG,
+                    "N=" + std::to_string(N) + " exceeds max_points=" + std::to_string(e->max_points));
+    if (dim < 1 || dim > kMaxD) return fail(e, FRNN_ERR_INVALID_ARG, "dim must be in [1, 128]");
+    if (K < 1 || K > kMaxK) return fail(e, FRNN_ERR_INVALID_ARG, "K must be in [1, 128]");
+    if (!(radius > 0.0f) || !std::isfinite(radius) || !std::isfinite(radius * radius) ||
+        !(radius * radius > 0.0f))
+        return fail(e, FRNN_ERR_INVALID_ARG, "radius must be finite and positive");
+    return FRNN_OK;
+}
+
+int check_device_ptr(frnn_engine* e, const void* p) {
+    cudaPointerAttributes a{};
+    cudaError_t err = cudaPointerGetAttributes(&a, p);
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return fail(e, FRNN_ERR_INVALID_ARG, "points pointer is not CUDA memory");
+    }
+    if (a.type == cudaMemoryTypeDevice && a.device != e->device)
+        return fail(e, FRNN_ERR_INVALID_ARG, "points pointer lives on another device");
+    if (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged)
+        return fail(e, FRNN_ERR_INVALID_ARG, "points pointer is not device memory");
+    return FRNN_OK;
+}
+
+// ---- transposes for the host paths --------------------------------------------
+
+// out[c*rows + r] = in[r*cols + c]  (in: rows x cols row-major)
+__global__ void transpose32_kernel(const unsigned* __restrict__ in, unsigned* __restrict__ out,
+                                   int rows, int cols) {
+    __shared__ unsigned t[32][33];
+    // 1-D grid over 32x32 tiles (either extent may exceed the 65535 limit of gridDim.y)
+    const long long tiles_c = (cols + 31) / 32;
+    const int c0 = (int)(blockIdx.x % tiles_c) * 32, r0 = (int)(blockIdx.x / tiles_c) * 32;
+    for (int i = threadIdx.y; i < 32; i += 8) {
+        int r = r0 + i, c = c0 + threadIdx.x;
+        if (r < rows && c < cols) t[i][threadIdx.x] = in[(long long)r * cols + c];
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += 8) {
+        int c = c0 + i, r = r0 + threadIdx.x;
+        if (r < rows && c < cols) out[(long long)c * rows + r] = t[threadIdx.x][i];
+    }
+}
+
+cudaError_t launch_transpose(const void* in, void* out, int rows, int cols, cudaStream_t s) {
+    const long long tiles = (long long)((cols + 31) / 32) * ((rows + 31) / 32);
+    dim3 grid((unsigned)tiles), block(32, 8);
+    transpose32_kernel<<<grid, block, 0, s>>>(static_cast<const unsigned*>(in),
+                                              static_cast<unsigned*>(out), rows, cols);
+    return cudaGetLastError();
+}
+
+// ---- planning -------------------------------------------------------------------
+
+int grid_axes_for(int dim) { return dim <= 4 ? dim : 4; }
+
+int row_floats(int dim) {
+    if (dim == 3) return 4;
+    int r = (dim + 3) / 4 * 4;
+    if (r > 16 && r <= 32) r = 32;
+    return r;
+}
+
+// Build the grid plan from the box.  Returns false when a grid is useless
+// (every query would scan nearly everything) or cannot be formed.
+bool make_plan(const float* box, int N, int dim, float radius, GridPlan& P) {
+    const int g = grid_axes_for(dim);
+    double ext_max = 0.0, mag = 0.0;
+    for (int d = 0; d < g; ++d) {
+        double lo = box[2 * d], hi = box[2 * d + 1];
+        ext_max = std::max(ext_max, hi - lo);
+        mag = std::max(mag, std::max(std::fabs(lo), std::fabs(hi)));
+    }
+    // Cell edge slightly above r: a point within r of the query then lies in
+    // the query's 3^g shell despite float rounding of the cell assignment
+    // (|error| of (x-origin)*inv_cell is a few ulps of the cell index).
+    const double u = 1.0 / 16777216.0;
+    double cell = (double)radius * (1.0 + 1e-5 + 8.0 * u * (ext_max / radius + 2.0));
+    const long long budget = std::max<long long>(1LL << 22, 8LL * N);
+    long long res[kMaxGridAxes];
+    long long cells = 1;
+    for (int iter = 0; iter < 64; ++iter) {
+        cells = 1;
+        bool over = false;
+        for (int d = 0; d < g; ++d) {
+            double ext = (double)box[2 * d + 1] - (double)box[2 * d];
+            res[d] = (long long)std::floor(ext / cell) + 1;
+            if (res[d] > (1LL << 30)) { over = true; break; }
+            cells *= res[d];
+            if (cells > budget) { over = true; break; }
+        }
+        if (!over) break;
+        cell *= 1.25;  // coarser cells keep cr = 1 valid, only the work grows
+    }
+    if (cells > budget) return false;
+    bool useful = false;
+    for (int d = 0; d < g; ++d) useful |= res[d] > 3;
+    if (!useful) return false;
+    P.g = g;
+    P.n = N;
+    P.dim = dim;
+    P.row = row_floats(dim);
+    P.cell = (float)cell;
+    P.inv_cell = 1.0f / P.cell;
+    // Recompute resolutions with the float cell actually used by the kernels:
+    // the largest coordinate must map inside the grid.
+    long long s = 1;
+    for (int d = 0; d < kMaxGridAxes; ++d) {
+        if (d < g) {
+            P.origin[d] = box[2 * d];
+            int c = (int)std::floor((box[2 * d + 1] - P.origin[d]) * P.inv_cell);
+            res[d] = std::max<long long>(res[d], (long long)c + 1);
+            P.res[d] = (int)res[d];
+            P.stride[d] = s;
+            s *= res[d];
+        } else {
+            P.origin[d] = 0.0f;
+            P.res[d] = 1;
+            P.stride[d] = s;
+        }
+    }
+    P.cells = s;
+    if (P.cells > (1LL << 31) - 2) return false;
+    P.eps = (float)(std::ldexp(1.0, -20) * (mag + ext_max)) + 1e-30f;
+    return true;
+}
+
+// ---- the search core ------------------------------------------------------------
+
+int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2,
+             const GridPlan& P, int* out_idx, float* out_dist) {
+    cudaStream_t s = e->stream;
+    FRNN_GROW(e, e->counts, (size_t)P.cells * 4);
+    FRNN_GROW(e, e->starts, ((size_t)P.cells + 1) * 4);
+    const long long tiles = scan_tiles(P.cells);
+    FRNN_GROW(e, e->scan_status, (size_t)tiles * 8);
+    FRNN_GROW(e, e->cellrank, (size_t)N * 8);
+    FRNN_GROW(e, e->rows, (size_t)N * P.row * 4);
+    FRNN_GROW(e, e->ids, (size_t)N * 4);
+
+    FRNN_CHECK(e, cudaMemsetAsync(e->counts.p, 0, (size_t)P.cells * 4, s), "memset counts");
+    FRNN_CHECK(e, cudaMemsetAsync(e->scan_ticket.p, 0, 4, s), "memset scan ticket");
+    stage_begin(e, ST_HASH);
+    FRNN_CHECK(e, launch_hash_count(d_pts, P, e->counts.as<int>(), e->cellrank.as<int2>(), s),
+               "hash_count launch");
+    stage_end(e, ST_HASH);
+    e->launches++;
+    e->epoch = (e->epoch + 1) & 0x3fffffffu;
+    if (e->epoch == 0) {
+        // status words of every earlier epoch must read as "not ready"
+        FRNN_CHECK(e, cudaMemsetAsync(e->scan_status.p, 0, e->scan_status.bytes, s), "memset status");
+        e->epoch = 1;
+    }
+    stage_begin(e, ST_SCAN);
+    FRNN_CHECK(e, launch_scan(e->counts.as<int>(), e->starts.as<int>(), P.cells,
+                              e->scan_status.as<unsigned long long>(), e->scan_ticket.as<int>(),
+                              e->epoch, e->err_flag.as<int>(), s),
+               "scan launch");
+    stage_end(e, ST_SCAN);
+    stage_begin(e, ST_SCATTER);
+    FRNN_CHECK(e, launch_scatter(d_pts, P, e->cellrank.as<int2>(), e->starts.as<int>(),
+                                 e->rows.as<float>(), e->ids.as<int>(), s),
+               "scatter launch");
+    stage_end(e, ST_SCATTER);
+    e->launches += 2;
+    // Small result sets: write straight to the original query ids (the
+    // scattered stores stay in L2).  Large ones: write in cell order, then
+    // unpermute one output row at a time.
+    const size_t out_bytes = (size_t)N * K * 8;
+    if (out_bytes <= (size_t)48 << 20) {
+        stage_begin(e, ST_SEARCH);
+        FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(), P, K,
+                                         r2, 0, N, out_idx, out_dist, N, e->ids.as<int>(), s),
+                   "grid search launch");
+        stage_end(e, ST_SEARCH);
+        e->launches++;
+    } else {
+        FRNN_GROW(e, e->tmp_idx, (size_t)N * K * 4);
+        FRNN_GROW(e, e->tmp_dist, (size_t)N * K * 4);
+        stage_begin(e, ST_SEARCH);
+        FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(), P, K,
+                                         r2, 0, N, e->tmp_idx.as<int>(), e->tmp_dist.as<float>(), N,
+                                         nullptr, s),
+                   "grid search launch");
+        stage_end(e, ST_SEARCH);
+        stage_begin(e, ST_UNPERMUTE);
+        FRNN_CHECK(e, launch_unpermute(e->tmp_idx.as<int>(), e->tmp_dist.as<float>(), e->ids.as<int>(),
+                                       N, K, out_idx, out_dist, s),
+                   "unpermute launch");
+        stage_end(e, ST_UNPERMUTE);
+        e->launches += 2;
+    }
+    return FRNN_OK;
+}
+
+int search_core(frnn_engine* e, const float* d_pts, int N, int dim, int K, float radius,
+                bool blocking) {
+    cudaStream_t s = e->stream;
+    const float r2 = radius * radius;
+    FRNN_GROW(e, e->out_idx, (size_t)N * K * 4);
+    FRNN_GROW(e, e->out_dist, (size_t)N * K * 4);
+    int* out_idx = e->out_idx.as<int>();
+    float* out_dist = e->out_dist.as<float>();
+
+    for (int i = 0; i < FRNN_STAGES; ++i) e->stage_used[i] = false;
+    int path = e->forced_path;
+    if (path == FRNN_PATH_AUTO) {
+        const double work = (double)N * (double)N * dim;
+        if (dim > 32 || work <= kBruteSmallWork) path = FRNN_PATH_BRUTE;
+        else path = FRNN_PATH_GRID;
+    }
+    if (path == FRNN_PATH_BRUTE_TC) path = FRNN_PATH_BRUTE;  // until the tensor-core path lands
+    if (path == FRNN_PATH_GRID && dim > 32) path = FRNN_PATH_BRUTE;
+
+    GridPlan P{};
+    bool grid_ok = false;
+    if (path == FRNN_PATH_GRID) {
+        const int g = grid_axes_for(dim);
+        const int blocks = std::min(bbox_blocks(N, e->sms), kBoxMaxBlocks);
+        stage_begin(e, ST_BBOX);
+        FRNN_CHECK(e, launch_bbox(d_pts, N, g, e->box_partial.as<float>(), e->box_ticket.as<unsigned>(),
+                                  e->box_out.as<float>(), blocks, s),
+                   "bbox launch");
+        stage_end(e, ST_BBOX);
+        e->launches++;
+        FRNN_CHECK(e, cudaMemcpyAsync(e->h_box, e->box_out.p, 9 * sizeof(float), cudaMemcpyDeviceToHost, s),
+                   "bbox readback");
+        FRNN_CHECK(e, cudaStreamSynchronize(s), "bbox sync");
+        if (e->h_box[8] != 0.0f)
+            return fail(e, FRNN_ERR_INVALID_ARG, "points contain NaN or Inf coordinates");
+        grid_ok = make_plan(e->h_box, N, dim, radius, P);
+        if (!grid_ok) path = FRNN_PATH_BRUTE;
+    }
+
+    if (path == FRNN_PATH_GRID) {
+        int st = run_grid(e, d_pts, N, dim, K, r2, P, out_idx, out_dist);
+        if (st != FRNN_OK) return st;
+        e->last_g = P.g;
+        e->last_cells = P.cells;
+    } else {
+        stage_begin(e, ST_BRUTE);
+        FRNN_CHECK(e, launch_bruteforce(d_pts, N, dim, K, r2, 0, N, out_idx, out_dist, N, s),
+                   "bruteforce launch");
+        stage_end(e, ST_BRUTE);
+        e->launches++;
+        e->last_g = 0;
+        e->last_cells = 0;
+    }
+    e->last_path = path;
+    e->last_N = N;
+    e->last_K = K;
+    if (blocking) {
+        FRNN_CHECK(e, cudaMemcpyAsync(e->h_err, e->err_flag.p, sizeof(int), cudaMemcpyDeviceToHost, s),
+                   "error flag readback");
+        FRNN_CHECK(e, cudaStreamSynchronize(s), "search sync");
+        if (*e->h_err != 0) {
+            cudaMemsetAsync(e->err_flag.p, 0, sizeof(int), s);
+            cudaStreamSynchronize(s);
+            e->last_N = -1;
+            return fail(e, FRNN_ERR_TIMEOUT, "prefix-scan look-back wait gave up");
+        }
+    }
+    return FRNN_OK;
+}
+
+}  // namespace
+
+// ---- C ABI ------------------------------------------------------------------------
+
+extern "C" {
+
+const char* frnn_status_string(int status) {
+    switch (status) {
+        case FRNN_OK: return "ok";
+        case FRNN_ERR_INVALID_ARG: return "invalid argument";
+        case FRNN_ERR_OOM: return "out of memory";
+        case FRNN_ERR_CUDA: return "CUDA error";
+        case FRNN_ERR_TIMEOUT: return "device wait timed out";
+        case FRNN_ERR_NO_DEVICE: return "no usable CUDA device";
+        case FRNN_ERR_STATE: return "invalid call order";
+        default: return "unknown status";
+    }
+}
+
+const char* frnn_last_error(const frnn_engine* e) { return e ? e->last_error.c_str() : ""; }
+
+int frnn_create(int max_points, int device, frnn_engine** out) {
+    if (!out) return FRNN_ERR_INVALID_ARG;
+    *out = nullptr;
+    if (max_points <= 0) return FRNN_ERR_INVALID_ARG;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        return FRNN_ERR_NO_DEVICE;
+    }
+    if (device < 0 && cudaGetDevice(&device) != cudaSuccess) return FRNN_ERR_NO_DEVICE;
+    if (device >= ndev) return FRNN_ERR_INVALID_ARG;
+    cudaDeviceProp prop{};
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return FRNN_ERR_NO_DEVICE;
+    if (prop.major < 10) return FRNN_ERR_NO_DEVICE;  // kernels are built for sm_100a only
+    frnn_engine* e = new frnn_engine();
+    e->device = device;
+    e->max_points = max_points;
+    e->sms = prop.multiProcessorCount;
+    DeviceGuard g(device);
+    int st = FRNN_OK;
+    if ((st = grow(e, e->box_partial, (size_t)kBoxMaxBlocks * 9 * 4, "box_partial")) ||
+        (st = grow(e, e->box_ticket, 16, "box_ticket")) || (st = grow(e, e->box_out, 64, "box_out")) ||
+        (st = grow(e, e->scan_ticket, 16, "scan_ticket")) || (st = grow(e, e->err_flag, 16, "err_flag"))) {
+        frnn_destroy(e);
+        return st;
+    }
+    if (cudaMemset(e->box_ticket.p, 0, e->box_ticket.bytes) != cudaSuccess ||
+        cudaMemset(e->err_flag.p, 0, e->err_flag.bytes) != cudaSuccess ||
+        cudaMallocHost(&e->h_box, 64) != cudaSuccess || cudaMallocHost(&e->h_err, 64) != cudaSuccess) {
+        cudaGetLastError();
+        frnn_destroy(e);
+        return FRNN_ERR_OOM;
+    }
+    *e->h_err = 0;
+    *out = e;
+    return FRNN_OK;
+}
+
+int frnn_destroy(frnn_engine* e) {
+    if (!e) return FRNN_OK;
+    {
+        DeviceGuard g(e->device);
+        if (e->stream) cudaStreamSynchronize(e->stream);
+        DevBuf* bufs[] = {&e->box_partial, &e->box_ticket, &e->box_out, &e->counts, &e->starts,
+                          &e->scan_status, &e->scan_ticket, &e->err_flag, &e->cellrank, &e->rows,
+                          &e->ids, &e->tmp_idx, &e->tmp_dist, &e->out_idx, &e->out_dist,
+                          &e->in_stage, &e->in_soa, &e->out_rm_idx, &e->out_rm_dist};
+        for (DevBuf* b : bufs) free_buf(*b);
+        for (cudaEvent_t& ev : e->ev)
+            if (ev) cudaEventDestroy(ev);
+        if (e->h_box) cudaFreeHost(e->h_box);
+        if (e->h_err) cudaFreeHost(e->h_err);
+    }
+    delete e;
+    return FRNN_OK;
+}
+
+int frnn_set_stream(frnn_engine* e, void* stream) {
+    if (!e) return FRNN_ERR_INVALID_ARG;
+    e->stream = static_cast<cudaStream_t>(stream);
+    return FRNN_OK;
+}
+
+int frnn_set_path(frnn_engine* e, int path) {
+    if (!e) return FRNN_ERR_INVALID_ARG;
+    if (path < FRNN_PATH_AUTO || path > FRNN_PATH_BRUTE_TC)
+        return fail(e, FRNN_ERR_INVALID_ARG, "unknown path");
+    e->forced_path = path;
+    return FRNN_OK;
+}
+
+int frnn_last_plan(const frnn_engine* e, int* path, int* grid_dims, int64_t* cells) {
+    if (!e) return FRNN_ERR_INVALID_ARG;
+    if (path) *path = e->last_path;
+    if (grid_dims) *grid_dims = e->last_g;
+    if (cells) *cells = e->last_cells;
+    return FRNN_OK;
+}
+
+static int search_gpu_impl(frnn_engine* e, const float* d_points_soa, int N, int dim, int K,
+                           float radius, int** d_idxs, float** d_dists, bool blocking) {
+    int st = check_search_args(e, d_points_soa, N, dim, K, radius);
+    if (st != FRNN_OK) return st;
+    if (!d_idxs || !d_dists) return fail(e, FRNN_ERR_INVALID_ARG, "output pointers are null");
+    DeviceGuard g(e->device);
+    st = check_device_ptr(e, d_points_soa);
+    if (st != FRNN_OK) return st;
+    st = search_core(e, d_points_soa, N, dim, K, radius, blocking);
+    if (st != FRNN_OK) return st;
+    *d_idxs = e->out_idx.as<int>();
+    *d_dists = e->out_dist.as<float>();
+    return FRNN_OK;
+}
+
+int frnn_search_gpu(frnn_engine* e, const float* d_points_soa, int N, int dim, int K, float radius,
+                    int** d_idxs, float** d_dists) {
+    return search_gpu_impl(e, d_points_soa, N, dim, K, radius, d_idxs, d_dists, true);
+}
+
+int frnn_search_gpu_async(frnn_engine* e, const float* d_points_soa, int N, int dim, int K,
+                          float radius, int** d_idxs, float** d_dists) {
+    return search_gpu_impl(e, d_points_soa, N, dim, K, radius, d_idxs, d_dists, false);
+}
+
+int frnn_search(frnn_engine* e, const float* h_points_aos, int64_t count, int K, float radius,
+                int* h_idxs, float* h_dists) {
+    if (!e) return FRNN_ERR_INVALID_ARG;
+    if (!h_points_aos || !h_idxs || !h_dists) return fail(e, FRNN_ERR_INVALID_ARG, "null pointer");
+    const int N = e->max_points;
+    if (count <= 0 || count % N != 0)
+        return fail(e, FRNN_ERR_INVALID_ARG, "point count must be a positive multiple of max_points");
+    const int64_t dim64 = count / N;
+    if (dim64 > kMaxD) return fail(e, FRNN_ERR_INVALID_ARG, "dim must be in [1, 128]");
+    const int dim = (int)dim64;
+    int st = check_search_args(e, h_points_aos, N, dim, K, radius);
+    if (st != FRNN_OK) return st;
+    DeviceGuard g(e->device);
+    cudaStream_t s = e->stream;
+    const size_t in_bytes = (size_t)count * 4;
+    FRNN_GROW(e, e->in_stage, in_bytes);
+    FRNN_GROW(e, e->in_soa, in_bytes);
+    FRNN_CHECK(e, cudaMemcpyAsync(e->in_stage.p, h_points_aos, in_bytes, cudaMemcpyHostToDevice, s), "H2D points");
+    FRNN_CHECK(e, launch_transpose(e->in_stage.p, e->in_soa.p, N, dim, s), "transpose points");
+    e->launches++;
+    st = search_core(e, e->in_soa.as<float>(), N, dim, K, radius, false);
+    if (st != FRNN_OK) return st;
+    const size_t out_n = (size_t)N * K;
+    FRNN_GROW(e, e->out_rm_idx, out_n * 4);
+    FRNN_GROW(e, e->out_rm_dist, out_n * 4);
+    FRNN_CHECK(e, launch_transpose(e->out_idx.p, e->out_rm_idx.p, K, N, s), "transpose idx");
+    FRNN_CHECK(e, launch_transpose(e->out_dist.p, e->out_rm_dist.p, K, N, s), "transpose dist");
+    e->launches += 2;
+    FRNN_CHECK(e, cudaMemcpyAsync(h_idxs, e->out_rm_idx.p, out_n * 4, cudaMemcpyDeviceToHost, s), "D2H idx");
+    FRNN_CHECK(e, cudaMemcpyAsync(h_dists, e->out_rm_dist.p, out_n * 4, cudaMemcpyDeviceToHost, s), "D2H dist");
+    FRNN_CHECK(e, cudaMemcpyAsync(e->h_err, e->err_flag.p, sizeof(int), cudaMemcpyDeviceToHost, s), "flag");
+    FRNN_CHECK(e, cudaStreamSynchronize(s), "search sync");
+    if (*e->h_err != 0) {
+        cudaMemsetAsync(e->err_flag.p, 0, sizeof(int), s);
+        cudaStreamSynchronize(s);
+        e->last_N = -1;
+        return fail(e, FRNN_ERR_TIMEOUT, "prefix-scan look-back wait gave up");
+    }
+    return FRNN_OK;
+}
+
+int frnn_search_host_soa(frnn_engine* e, const float* h_points_soa, int N, int dim, int K,
+                         float radius, int* h_idxs, float* h_dists) {
+    int st = check_search_args(e, h_points_soa, N, dim, K, radius);
+    if (st != FRNN_OK) return st;
+    if (!h_idxs || !h_dists) return fail(e, FRNN_ERR_INVALID_ARG, "null output pointer");
+    DeviceGuard g(e->device);
+    cudaStream_t s = e->stream;
+    const size_t in_bytes = (size_t)N * dim * 4;
+    FRNN_GROW(e, e->in_soa, in_bytes);
+    FRNN_CHECK(e, cudaMemcpyAsync(e->in_soa.p, h_points_soa, in_bytes, cudaMemcpyHostToDevice, s), "H2D points");
+    st = search_core(e, e->in_soa.as<float>(), N, dim, K, radius, false);
+    if (st != FRNN_OK) return st;
+    const size_t out_n = (size_t)N * K;
+    FRNN_CHECK(e, cudaMemcpyAsync(h_idxs, e->out_idx.p, out_n * 4, cudaMemcpyDeviceToHost, s), "D2H idx");
+    FRNN_CHECK(e, cudaMemcpyAsync(h_dists, e->out_dist.p, out_n * 4, cudaMemcpyDeviceToHost, s), "D2H dist");
+    FRNN_CHECK(e, cudaMemcpyAsync(e->h_err, e->err_flag.p, sizeof(int), cudaMemcpyDeviceToHost, s), "flag");
+    FRNN_CHECK(e, cudaStreamSynchronize(s), "search sync");
+    if (*e->h_err != 0) {
+        cudaMemsetAsync(e->err_flag.p, 0, sizeof(int), s);
+        cudaStreamSynchronize(s);
+        e->last_N = -1;
+        return fail(e, FRNN_ERR_TIMEOUT, "prefix-scan look-back wait gave up");
+    }
+    return FRNN_OK;
+}
+
+int frnn_set_timing(frnn_engine* e, int enable) {
+    if (!e) return FRNN_ERR_INVALID_ARG;
+    DeviceGuard g(e->device);
+    if (enable && !e->ev[0]) {
+        for (cudaEvent_t& ev : e->ev)
+            FRNN_CHECK(e, cudaEventCreate(&ev), "event create");
+    }
+    e->timing = enable != 0;
+    return FRNN_OK;
+}
+
+int frnn_last_stage_times(frnn_engine* e, float* ms, int n) {
+    if (!e || !ms || n <= 0) return FRNN_ERR_INVALID_ARG;
+    DeviceGuard g(e->device);
+    for (int i = 0; i < n; ++i) {
+        ms[i] = -1.0f;
+        if (i < FRNN_STAGES && e->timing && e->stage_used[i]) {
+            FRNN_CHECK(e, cudaEventSynchronize(e->ev[2 * i + 1]), "event sync");
+            FRNN_CHECK(e, cudaEventElapsedTime(&ms[i], e->ev[2 * i], e->ev[2 * i + 1]), "event time");
+        }
+    }
+    return FRNN_OK;
+}
+
+int frnn_launch_count(const frnn_engine* e, int64_t* n) {
+    if (!e || !n) return FRNN_ERR_INVALID_ARG;
+    *n = e->launches;
+    return FRNN_OK;
+}
+
+int frnn_get_results(frnn_engine* e, int N, int K, int* h_idxs, float* h_dists) {
+    if (!e) return FRNN_ERR_INVALID_ARG;
+    if (!h_idxs || !h_dists) return fail(e, FRNN_ERR_INVALID_ARG, "null output pointer");
+    if (e->last_N < 0) return fail(e, FRNN_ERR_STATE, "no finished search to read");
+    if (N != e->last_N || K < 1 || K > e->last_K)
+        return fail(e, FRNN_ERR_INVALID_ARG, "N must equal the last search's N and K must not exceed its K");
+    DeviceGuard g(e->device);
+    cudaStream_t s = e->stream;
+    const size_t n = (size_t)N * K;
+    FRNN_CHECK(e, cudaMemcpyAsync(h_idxs, e->out_idx.p, n * 4, cudaMemcpyDeviceToHost, s), "D2H idx");
+    FRNN_CHECK(e, cudaMemcpyAsync(h_dists, e->out_dist.p, n * 4, cudaMemcpyDeviceToHost, s), "D2H dist");
+    FRNN_CHECK(e, cudaStreamSynchronize(s), "results sync");
+    return FRNN_OK;
+}
+
+}  // extern "C"

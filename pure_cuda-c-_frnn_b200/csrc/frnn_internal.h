@@ -1,0 +1,41 @@
+// frnn_internal.h -- kernel launchers shared between the engine's .cu files.
+// Not part of the public ABI (that is include/frnn_b200.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include "frnn_device.cuh"
+
+namespace frnn {
+
+// grid_build.cu
+int bbox_blocks(int n, int sms);
+cudaError_t launch_bbox(const float* pts, int n, int g, float* partial, unsigned int* ticket,
+                        float* out, int blocks, cudaStream_t s);
+cudaError_t launch_hash_count(const float* pts, const GridPlan& P, int* counts, int2* cellrank,
+                              cudaStream_t s);
+long long scan_tiles(long long cells);
+cudaError_t launch_scan(const int* counts, int* starts, long long cells,
+                        unsigned long long* status, int* ticket, unsigned epoch, int* err,
+                        cudaStream_t s);
+cudaError_t launch_scatter(const float* pts, const GridPlan& P, const int2* cellrank,
+                           const int* starts, float* rows, int* ids, cudaStream_t s);
+
+// grid_search.cu
+// Searches sorted query positions [q0, q1).  Results for sorted position sq go
+// to row (sq - q0) of the outputs: out[k*ostride + (sq - q0)], or, when
+// scatter_ids is non-null, straight to out[k*ostride + scatter_ids[sq]].
+cudaError_t launch_grid_search(const float* rows, const int* ids, const int* starts,
+                               const GridPlan& P, int K, float r2, int q0, int q1, int* oidx,
+                               float* odist, long long ostride, const int* scatter_ids,
+                               cudaStream_t s);
+// out[k*N + ids[sq]] = in[k*N + sq]
+cudaError_t launch_unpermute(const int* in_idx, const float* in_dist, const int* ids, int n,
+                             int K, int* out_idx, float* out_dist, cudaStream_t s);
+
+// bruteforce.cu
+// Queries [q0, q1) of the SoA cloud against all n points; results of query q
+// go to out[k*ostride + (q - q0)].
+cudaError_t launch_bruteforce(const float* pts, int n, int dim, int K, float r2, int q0, int q1,
+                              int* oidx, float* odist, long long ostride, cudaStream_t s);
+
+}  // namespace frnn

@@ -1,0 +1,173 @@
+"""Seeded synthetic point clouds for the five benchmark configurations.
+
+The reference benchmarks on synthetic clouds only (Tests/scripts/
+benchmark_vs_libfrnn.py:94-133 and Tests/scripts/validate_correctness.py:47-78):
+a generator, a radius chosen for an expected neighbour count, self-query.
+This module keeps that harness convention for the five configurations the
+engine is measured on; every cloud is a pure function of (config, N, seed).
+
+Arrays are returned row-major (N, D) float32; the engine's device input is the
+transposed SoA copy p[d*N + i] (the reference's layout, grid.h:26-30).
+
+Radii: configuration 1 uses the analytic radius for 16 expected neighbours of
+a uniform cloud.  Configurations 2-5 use a radius calibrated by bisection so
+that the mean in-radius count (d^2 <= r^2, self included) over a seeded
+4,096-query float64 brute-force sample equals the target; the values in
+CONFIGS were produced by ``calibrate_radius`` with the default arguments and
+are pinned so runs never recompute them.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+
+SEED = 1234
+
+
+@dataclass(frozen=True)
+class Config:
+    name: str
+    D: int
+    N: int
+    K: int
+    target: int          # expected mean in-radius count
+    radius: float        # pinned radius for the full-size cloud
+    kind: str
+    describe: str
+
+
+def _uniform(rng, N, D):
+    return rng.random((N, D), dtype=np.float64).astype(np.float32)
+
+
+def _mixture(rng, N, D, comps=64, sigma=0.02):
+    centres = rng.random((comps, D))
+    labels = rng.integers(0, comps, N)
+    pts = centres[labels] + sigma * rng.standard_normal((N, D))
+    return pts.astype(np.float32)
+
+
+def _lowrank_minmax(rng, N, D, rank, noise=0.01):
+    a, _ = np.linalg.qr(rng.standard_normal((D, rank)))    # D x rank, orthonormal columns
+    z = rng.standard_normal((N, rank))
+    pts = z @ a.T + noise * rng.standard_normal((N, D))
+    mn = pts.min(axis=0, keepdims=True)
+    mx = pts.max(axis=0, keepdims=True)
+    return ((pts - mn) / np.maximum(mx - mn, 1e-12)).astype(np.float32)
+
+
+def _sphere(rng, N, D):
+    x = rng.standard_normal((N, D))
+    x /= np.linalg.norm(x, axis=1, keepdims=True)
+    return x.astype(np.float32)
+
+
+def generate(kind: str, N: int, D: int, seed: int = SEED) -> np.ndarray:
+    """Row-major (N, D) float32 cloud of the given kind."""
+    rng = np.random.default_rng(seed)
+    if kind == "uniform":
+        return _uniform(rng, N, D)
+    if kind == "mixture":
+        return _mixture(rng, N, D)
+    if kind == "lowrank4":
+        return _lowrank_minmax(rng, N, D, 4)
+    if kind == "lowrank6":
+        return _lowrank_minmax(rng, N, D, 6)
+    if kind == "sphere":
+        return _sphere(rng, N, D)
+    raise ValueError(f"unknown cloud kind {kind!r}")
+
+
+def uniform_radius(N: int, D: int, k: int) -> float:
+    """Radius whose ball holds k expected points of a unit-cube uniform cloud."""
+    v = math.pi ** (D / 2) / math.gamma(D / 2 + 1)
+    return (k / (N * v)) ** (1.0 / D)
+
+
+def calibrate_radius(pts: np.ndarray, target: float, sample: int = 4096, seed: int = SEED,
+                     keep: int | None = None) -> float:
+    """Bisect r so the mean count of d^2 <= r^2 (self included) over a seeded
+    query sample equals ``target``; distances are float64.
+
+    Each sampled query keeps its ``keep`` smallest squared distances, which is
+    exact as long as no query has more than ``keep`` points inside the final
+    radius (checked)."""
+    N = pts.shape[0]
+    keep = keep or int(16 * target)
+    keep = min(keep, N)
+    rng = np.random.default_rng(seed + 1)
+    qi = rng.choice(N, size=min(sample, N), replace=False)
+    p64 = pts.astype(np.float64)
+    pn = (p64 * p64).sum(1)
+    best = np.empty((len(qi), keep), dtype=np.float64)
+    for s in range(0, len(qi), 32):
+        q = p64[qi[s:s + 32]]
+        d2 = (q * q).sum(1)[:, None] + pn[None, :] - 2.0 * (q @ p64.T)
+        np.maximum(d2, 0.0, out=d2)
+        part = np.partition(d2, keep - 1, axis=1)[:, :keep]
+        best[s:s + len(q)] = np.sort(part, axis=1)
+    flat = best.ravel()
+    lo, hi = 0.0, math.sqrt(float(flat.max()))
+    want = target * len(qi)
+    for _ in range(60):
+        mid = 0.5 * (lo + hi)
+        if int((flat <= mid * mid).sum()) < want:
+            lo = mid
+        else:
+            hi = mid
+    r = 0.5 * (lo + hi)
+    if np.any(best[:, -1] <= r * r):
+        raise RuntimeError("calibration sample saturated; raise keep")
+    return float(r)
+
+
+CONFIGS = {
+    1: Config("cfg1_uniform_d3", 3, 200_000, 16, 16, 0.0, "uniform",
+              "D=3, N=200,000 uniform in [0,1)^3, K=16, r=(3*16/(4*pi*N))^(1/3)"),
+    2: Config("cfg2_mixture_d3", 3, 1_000_000, 32, 24, 0.0, "mixture",
+              "D=3, N=1,000,000 64-component Gaussian mixture (sigma=0.02), K=32, mean 24"),
+    3: Config("cfg3_lowrank_d12", 12, 500_000, 32, 24, 0.0, "lowrank4",
+              "D=12, N=500,000 rank-4 + 0.01 noise, min-max to [0,1], K=32, mean 24"),
+    4: Config("cfg4_lowrank_d16", 16, 1_500_000, 64, 48, 0.0, "lowrank6",
+              "D=16, N=1,500,000 rank-6 + 0.01 noise, min-max to [0,1], K=64, mean 48"),
+    5: Config("cfg5_sphere_d128", 128, 1_000_000, 128, 64, 0.0, "sphere",
+              "D=128, N=1,000,000 unit-sphere Gaussian directions, K=128, mean 64"),
+}
+
+# Pinned radii for the full-size clouds (calibrate_radius with defaults).
+_PINNED = {
+    1: uniform_radius(200_000, 3, 16),
+    2: 0.004968632893508178,
+    3: 0.03711896133486163,
+    4: 0.07947997893394668,
+    5: 1.1565264502236734,
+}
+
+
+def config(i: int) -> Config:
+    c = CONFIGS[i]
+    r = _PINNED.get(i, c.radius)
+    return Config(c.name, c.D, c.N, c.K, c.target, r, c.kind, c.describe)
+
+
+def cloud(i: int, N: int | None = None, seed: int = SEED) -> tuple[np.ndarray, float]:
+    """(points (N, D) float32, radius) for configuration i.  At the
+    configuration's own size and seed the pinned radius is returned; for a
+    smaller cloud the radius is calibrated on that cloud (1,024-query sample)
+    so the expected neighbour count stays the configuration's target."""
+    c = config(i)
+    n = c.N if N is None else N
+    pts = generate(c.kind, n, c.D, seed)
+    if n == c.N and seed == SEED:
+        return pts, c.radius
+    if i == 1:
+        return pts, uniform_radius(n, c.D, c.K)
+    return pts, calibrate_radius(pts, c.target, sample=min(1024, n), seed=seed)
+
+
+def soa(pts: np.ndarray) -> np.ndarray:
+    """Row-major (N, D) -> contiguous SoA (D, N) float32."""
+    return np.ascontiguousarray(pts.T, dtype=np.float32)

@@ -1,0 +1,178 @@
+"""CPU tests of the oracle (the parity checker) and of the data generators.
+
+The oracle restates the reference engine on the CPU; these tests pin it
+against an independent float64 brute force, against the reference's
+dispatcher as probed for the five benchmark configurations, and (when the
+fixtures exist) against outputs of the reference engine itself recorded on a
+B200 (tests/golden/)."""
+
+import glob
+import os
+
+import numpy as np
+import pytest
+
+from frnn_cuda import datagen
+from parity import compare_to_reference, sort_rows
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def f64_truth(pts_soa, K, r):
+    """Independent float64 brute force: rows of (idx, d2) ascending, d2 < r^2."""
+    P = pts_soa.T.astype(np.float64)
+    d2 = ((P[:, None, :] - P[None, :, :]) ** 2).sum(-1)
+    r2 = float(np.float32(r) * np.float32(r))
+    out = []
+    for q in range(P.shape[0]):
+        j = np.nonzero(d2[q] < r2)[0]
+        o = np.lexsort((j, d2[q, j]))
+        out.append((j[o][:K], d2[q, j[o]][:K]))
+    return out
+
+
+@pytest.mark.parametrize("D,N,K,kind", [(3, 700, 16, "uniform"), (2, 900, 8, "uniform"),
+                                        (5, 600, 32, "uniform"), (12, 500, 16, "lowrank4"),
+                                        (3, 800, 32, "mixture"), (1, 400, 4, "uniform")])
+def test_oracle_matches_float64_bruteforce(oracle_mod, D, N, K, kind):
+    pts = datagen.generate(kind, N, D, seed=7)
+    soa = datagen.soa(pts)
+    r = datagen.uniform_radius(N, D, 1.5 * K) if kind == "uniform" else 0.08 if D <= 3 else 0.25
+    idx, dist, ncand = oracle_mod.search(soa, K, r)
+    assert ncand > 0
+    truth = f64_truth(soa, K, r)
+    r2 = float(np.float32(r) * np.float32(r))
+    for q in range(N):
+        got = idx[:, q]
+        n = int((got >= 0).sum())
+        ti, td = truth[q]
+        # distances agree with float64 to fp32 rounding
+        np.testing.assert_allclose(dist[:n, q], td[:n], rtol=2e-6, atol=1e-12)
+        if set(got[:n].tolist()) != set(ti.tolist()):
+            # only ties at the K-th distance or the boundary band may differ
+            diff = set(got[:n].tolist()) ^ set(ti.tolist())
+            for j in diff:
+                dj = ((soa[:, q].astype(np.float64) - soa[:, j]) ** 2).sum()
+                assert abs(dj - r2) <= 1e-6 * r2 or abs(dj - td[-1]) <= 1e-6 * max(td[-1], 1e-30), (q, j)
+        # padding
+        assert np.all(idx[n:, q] == -1)
+        assert np.all(dist[n:, q] == np.float32(r2))
+        # ascending (d2, idx)
+        keys = list(zip(dist[:n, q].tolist(), got[:n].tolist()))
+        assert keys == sorted(keys)
+
+
+def test_oracle_subset_equals_full(oracle_mod):
+    pts = datagen.generate("mixture", 3000, 3, seed=3)
+    soa = datagen.soa(pts)
+    idx, dist, _ = oracle_mod.search(soa, 16, 0.03)
+    q = np.array([0, 5, 17, 2999, 1234], np.int32)
+    si, sd, _ = oracle_mod.search_subset(soa, q, 16, 0.03)
+    assert np.array_equal(si, idx[:, q]) and np.array_equal(sd, dist[:, q])
+
+
+def test_oracle_grid_equals_bruteforce_order(oracle_mod):
+    # A radius so large the oracle's grid degenerates to brute force must give
+    # the same answer as a radius that uses the grid, restricted to the same K.
+    pts = datagen.generate("uniform", 2000, 3, seed=11)
+    soa = datagen.soa(pts)
+    i1, d1, _ = oracle_mod.search(soa, 8, 0.05)
+    i2, d2, _ = oracle_mod.search(soa, 8, 0.05, order=oracle_mod.ORDER_AOS3)
+    assert np.array_equal(i1, i2) and np.array_equal(d1, d2)
+
+
+# The reference dispatcher (frnn_engine.cu:195-250) on the five benchmark
+# configurations; expected paths and grids as probed from the reference source.
+@pytest.mark.parametrize("cfg,path,g,res", [(1, "grid_aos3", 3, 38), (2, "bf_fallback", 0, None),
+                                            (3, "firstd", 4, 27), (4, "firstd", 4, 13),
+                                            (5, "bf_fallback", 0, None)])
+def test_reference_dispatch_restated(oracle_mod, cfg, path, g, res):
+    c = datagen.config(cfg)
+    assert c.radius > 0
+    p = oracle_mod.ref_plan(c.N, c.D, c.K, c.radius)
+    assert p["path"] == path
+    assert p["grid_dim"] == g
+    if res is not None:
+        assert p["res"] == res
+
+
+def test_reference_dispatch_small_inputs(oracle_mod):
+    # N^2*D*ceil(K/8) <= 2e6 -> brute force (frnn_engine.cu:215-219)
+    assert oracle_mod.ref_plan(800, 3, 8, 0.05)["path"] == "bf_small"
+    assert oracle_mod.ref_plan(900, 3, 8, 0.05)["path"] == "grid_aos3"
+    assert oracle_mod.ref_plan(5000, 2, 16, 0.02)["path"] == "grid_nd"
+
+
+def test_ref_mode_equals_exact_in_domain(oracle_mod):
+    pts = datagen.generate("uniform", 4000, 3, seed=5)
+    soa = datagen.soa(pts)
+    r = datagen.uniform_radius(4000, 3, 16)
+    ei, ed, _ = oracle_mod.search(soa, 16, r)
+    ri, rd, valid, path = oracle_mod.ref_search(soa, 16, r)
+    assert path == "grid_aos3" and valid.all()
+    assert np.array_equal(ei, ri) and np.array_equal(ed, rd)
+
+
+def test_ref_mode_drops_out_of_domain(oracle_mod):
+    pts = datagen.generate("uniform", 4000, 3, seed=5)
+    pts[:10] += 2.0  # outside [0,1): the reference grid drops these points
+    soa = datagen.soa(pts)
+    r = datagen.uniform_radius(4000, 3, 16)
+    ri, rd, valid, path = oracle_mod.ref_search(soa, 16, r)
+    assert path == "grid_aos3"
+    assert not valid[:10].any() and valid[10:].all()
+    assert not np.isin(np.arange(10), ri).any()
+
+
+def test_golden_fixtures_pin_oracle(oracle_mod):
+    """Outputs of the reference engine (compiled from its sources, run on a
+    B200 by tests/golden/make_golden.py) against the oracle's reference mode."""
+    files = sorted(glob.glob(os.path.join(GOLDEN, "*.npz")))
+    if not files:
+        pytest.skip("no golden fixtures recorded yet")
+    for f in files:
+        z = np.load(f)
+        soa, K, r = z["points_soa"], int(z["K"]), float(z["radius"])
+        oi, od, valid, path = oracle_mod.ref_search(soa, K, r)
+        assert path == str(z["ref_path"]), (f, path)
+        st = compare_to_reference(oi, od, z["ref_idx"], z["ref_dist"], soa, r, valid=valid,
+                                  d2_f64=lambda qi, pj: oracle_mod.pair_d2_f64(soa, qi, pj))
+        assert st["mismatch"] == 0 and st["dist_mismatch"] == 0, (os.path.basename(f), st)
+
+
+def test_sort_rows_helper():
+    idx = np.array([[3, -1], [1, 2], [2, 0]], np.int32)
+    dist = np.array([[0.5, 9.0], [0.1, 0.2], [0.1, 0.1]], np.float32)
+    i, d = sort_rows(idx, dist)
+    assert i[0].tolist() == [1, 2, 3] and i[1].tolist() == [0, 2, -1]
+
+
+# ---- generators ---------------------------------------------------------------
+
+
+def test_generators_deterministic_and_shaped():
+    for cfg in (1, 2, 3, 4, 5):
+        c = datagen.config(cfg)
+        a = datagen.generate(c.kind, 1000, c.D, seed=1)
+        b = datagen.generate(c.kind, 1000, c.D, seed=1)
+        assert a.shape == (1000, c.D) and a.dtype == np.float32
+        assert np.array_equal(a, b)
+        if c.kind in ("lowrank4", "lowrank6"):
+            assert a.min() == 0.0 and a.max() == 1.0
+        if c.kind == "sphere":
+            np.testing.assert_allclose(np.linalg.norm(a, axis=1), 1.0, rtol=1e-5)
+
+
+def test_pinned_radii_present():
+    for cfg in (1, 2, 3, 4, 5):
+        assert datagen.config(cfg).radius > 0
+
+
+def test_calibration_hits_target_on_small_cloud():
+    pts = datagen.generate("mixture", 20000, 3, seed=2)
+    r = datagen.calibrate_radius(pts, 24, sample=512)
+    P = pts.astype(np.float64)
+    rng = np.random.default_rng(9)
+    q = rng.choice(len(P), 256, replace=False)
+    cnt = [(((P - P[i]) ** 2).sum(1) <= r * r).sum() for i in q]
+    assert 18 < np.mean(cnt) < 30
