@@ -120,6 +120,15 @@ int frnn_search_gpu_async(frnn_engine* e, const float* d_points_soa, int N, int 
 int frnn_search_host_soa(frnn_engine* e, const float* h_points_soa, int N, int dim, int K,
                          float radius, int* h_idxs, float* h_dists);
 
+/* Tuning options (frnn_set_option). */
+enum frnn_option {
+    /* Result sets up to this many bytes (N*K*8) are written straight to
+     * original query order from the search kernel; larger ones are written in
+     * cell order and unpermuted one output row at a time.  Default 48 MiB. */
+    FRNN_OPT_DIRECT_OUTPUT_MAX_BYTES = 1
+};
+int frnn_set_option(frnn_engine* e, int option, int64_t value);
+
 /* Per-stage device timing.  When enabled, each search records CUDA events
  * around its stages on the engine stream; frnn_last_stage_times writes the
  * last search's milliseconds for stages 0..n-1 (0 bounding box, 1 cell

@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import argparse
 import concurrent.futures as cf
+import hashlib
 import os
 import shutil
 import subprocess
@@ -49,8 +50,16 @@ def _stale(target: str, deps: list[str]) -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False) -> str:
-    os.makedirs(OBJ, exist_ok=True)
+def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False,
+          defines: list[str] | None = None, out: str | None = None) -> str:
+    """Compile and link.  ``defines`` are extra -D macros (launch-policy
+    knobs); with defines or ``out`` the objects go to a separate folder and the
+    library to ``out``, leaving the default build untouched."""
+    defines = defines or []
+    lib = out or LIB
+    tag = hashlib.sha1(repr((sorted(defines), os.path.abspath(lib))).encode()).hexdigest()[:10]
+    obj_dir = OBJ if not (defines or out) else OBJ + "_" + tag
+    os.makedirs(obj_dir, exist_ok=True)
     srcs = sorted(f for f in os.listdir(CSRC) if f.endswith(".cu"))
     hdrs = _headers()
     cc = nvcc()
@@ -58,10 +67,10 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
     objs = []
     for f in srcs:
         src = os.path.join(CSRC, f)
-        obj = os.path.join(OBJ, f[:-3] + ".o")
+        obj = os.path.join(obj_dir, f[:-3] + ".o")
         objs.append(obj)
         if force or _stale(obj, [src] + hdrs):
-            cmd = [cc, "-c", src, "-o", obj] + NVCC_FLAGS
+            cmd = [cc, "-c", src, "-o", obj] + NVCC_FLAGS + ["-D" + d for d in defines]
             if ptxas_verbose:
                 cmd += ["-Xptxas", "-v"]
             jobs.append(cmd)
@@ -83,14 +92,14 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
         for cmd, p in failed:
             sys.stderr.write(" ".join(cmd) + "\n" + p.stdout + p.stderr + "\n")
         raise RuntimeError(f"nvcc failed for {len(failed)} file(s)")
-    if force or jobs or _stale(LIB, objs):
-        cmd = [cc, "-shared", "-o", LIB] + objs + ARCH + ["-lcudart"]
+    if force or jobs or _stale(lib, objs):
+        cmd = [cc, "-shared", "-o", lib] + objs + ARCH + ["-lcudart"]
         if verbose:
             print(" ".join(cmd), flush=True)
         p = subprocess.run(cmd, capture_output=True, text=True)
         if p.returncode != 0:
             raise RuntimeError("link failed:\n" + p.stdout + p.stderr)
-    return LIB
+    return lib
 
 
 if __name__ == "__main__":
@@ -98,5 +107,8 @@ if __name__ == "__main__":
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--ptxas", action="store_true", help="print register/spill usage")
+    ap.add_argument("-D", dest="defines", action="append", default=[],
+                    help="extra macro, e.g. -D FRNN_COOP_MIN_BLOCKS=6")
+    ap.add_argument("--out", default=None, help="library path (default: in-tree frnn_cuda/)")
     a = ap.parse_args()
-    print(build(a.force, a.verbose, a.ptxas))
+    print(build(a.force, a.verbose, a.ptxas, a.defines, a.out))

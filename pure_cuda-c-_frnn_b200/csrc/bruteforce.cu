@@ -19,18 +19,18 @@ constexpr int kBfThreads = 128;
 constexpr int kBfTileMax = 128;
 constexpr size_t kSmemLimit = 227 * 1024;
 
-template <bool D3>
+template <bool D3, int KMAX>
 __global__ void __launch_bounds__(kBfThreads)
     bruteforce_kernel(const float* __restrict__ pts, int n, int dim, int K, float r2, int q0, int q1,
                       int* __restrict__ oidx, float* __restrict__ odist, long long ostride,
                       int kBfTile) {
     extern __shared__ unsigned long long smem[];
-    unsigned long long* heap = smem;                                    // K x T keys
-    float* tile = reinterpret_cast<float*>(heap + (size_t)K * kBfThreads);  // dim x kBfTile
+    unsigned long long* heap = smem;                                    // (K+B) x T keys
+    float* tile = reinterpret_cast<float*>(heap + (size_t)TopK<KMAX>::slots(K) * kBfThreads);  // dim x kBfTile
     float* qs = tile + (size_t)dim * kBfTile;                          // dim x T
     const int q = q0 + blockIdx.x * kBfThreads + threadIdx.x;
     const bool active = q < q1;
-    TopK tk;
+    TopK<KMAX> tk;
     tk.init(heap + threadIdx.x, kBfThreads, K, r2);
     for (int d = 0; d < dim; ++d)
         qs[d * kBfThreads + threadIdx.x] = active ? __ldg(&pts[(long long)d * n + q]) : 0.0f;
@@ -61,8 +61,7 @@ __global__ void __launch_bounds__(kBfThreads)
                 }
                 if (d < dim) continue;
             }
-            const unsigned long long key = make_key(d2, j0 + j);
-            if (key < tk.thr) tk.push(key);
+            tk.offer(d2, j0 + j);
         }
     }
     if (active) {
@@ -71,32 +70,39 @@ __global__ void __launch_bounds__(kBfThreads)
     }
 }
 
+template <bool D3, int KMAX>
+cudaError_t launch_bf(const float* pts, int n, int dim, int K, float r2, int q0, int q1, int* oidx,
+                      float* odist, long long ostride, int tile, size_t smem, int blocks,
+                      cudaStream_t s) {
+    cudaError_t err = cudaFuncSetAttribute(bruteforce_kernel<D3, KMAX>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (err != cudaSuccess) return err;
+    bruteforce_kernel<D3, KMAX><<<blocks, kBfThreads, smem, s>>>(pts, n, dim, K, r2, q0, q1, oidx,
+                                                                 odist, ostride, tile);
+    return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_bruteforce(const float* pts, int n, int dim, int K, float r2, int q0, int q1,
                               int* oidx, float* odist, long long ostride, cudaStream_t s) {
     if (q1 <= q0) return cudaSuccess;
-    const size_t fixed = (size_t)K * 8 * kBfThreads + (size_t)dim * 4 * kBfThreads;
+    const size_t fixed = (size_t)TopK<128>::slots(K) * 8 * kBfThreads + (size_t)dim * 4 * kBfThreads;
     if (fixed + (size_t)dim * 4 * 8 > kSmemLimit) return cudaErrorInvalidConfiguration;
     int tile = (int)((kSmemLimit - fixed) / ((size_t)dim * 4));
     tile = tile > kBfTileMax ? kBfTileMax : (tile / 8) * 8;
     const size_t smem = fixed + (size_t)dim * 4 * tile;
     const int blocks = (q1 - q0 + kBfThreads - 1) / kBfThreads;
-    cudaError_t err;
     if (dim == 3) {
-        err = cudaFuncSetAttribute(bruteforce_kernel<true>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (err != cudaSuccess) return err;
-        bruteforce_kernel<true><<<blocks, kBfThreads, smem, s>>>(pts, n, dim, K, r2, q0, q1, oidx,
-                                                                 odist, ostride, tile);
-    } else {
-        err = cudaFuncSetAttribute(bruteforce_kernel<false>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (err != cudaSuccess) return err;
-        bruteforce_kernel<false><<<blocks, kBfThreads, smem, s>>>(pts, n, dim, K, r2, q0, q1,
-                                                                  oidx, odist, ostride, tile);
+        if (K <= 16) return launch_bf<true, 16>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s);
+        if (K <= 32) return launch_bf<true, 32>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s);
+        if (K <= 64) return launch_bf<true, 64>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s);
+        return launch_bf<true, 128>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s);
     }
-    return cudaGetLastError();
+    if (K <= 16) return launch_bf<false, 16>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s);
+    if (K <= 32) return launch_bf<false, 32>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s);
+    if (K <= 64) return launch_bf<false, 64>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s);
+    return launch_bf<false, 128>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s);
 }
 
 }  // namespace frnn

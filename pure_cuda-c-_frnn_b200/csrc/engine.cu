@@ -49,6 +49,7 @@ struct frnn_engine {
     cudaStream_t stream = 0;
     int forced_path = FRNN_PATH_AUTO;
     unsigned epoch = 0;
+    long long direct_output_max_bytes = 48LL << 20;
 
     DevBuf box_partial, box_ticket, box_out;
     DevBuf counts, starts, scan_status, scan_ticket, err_flag;
@@ -229,7 +230,11 @@ bool make_plan(const float* box, int N, int dim, float radius, GridPlan& P) {
     // (|error| of (x-origin)*inv_cell is a few ulps of the cell index).
     const double u = 1.0 / 16777216.0;
     double cell = (double)radius * (1.0 + 1e-5 + 8.0 * u * (ext_max / radius + 2.0));
-    const long long budget = std::max<long long>(1LL << 22, 8LL * N);
+    // Dense cell table budget: 32 cells per point (12 bytes of build traffic
+    // per cell); sparse clouds such as Gaussian mixtures leave most cells
+    // empty, and coarser cells would multiply the candidates of every query.
+    const long long budget = std::min<long long>(std::max<long long>(1LL << 22, 32LL * N),
+                                                 (1LL << 31) - 2);
     long long res[kMaxGridAxes];
     long long cells = 1;
     for (int iter = 0; iter < 64; ++iter) {
@@ -319,8 +324,8 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
     // Small result sets: write straight to the original query ids (the
     // scattered stores stay in L2).  Large ones: write in cell order, then
     // unpermute one output row at a time.
-    const size_t out_bytes = (size_t)N * K * 8;
-    if (out_bytes <= (size_t)48 << 20) {
+    const long long out_bytes = (long long)N * K * 8;
+    if (out_bytes <= e->direct_output_max_bytes) {
         stage_begin(e, ST_SEARCH);
         FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(), P, K,
                                          r2, 0, N, out_idx, out_dist, N, e->ids.as<int>(), s),
@@ -506,6 +511,18 @@ int frnn_set_path(frnn_engine* e, int path) {
         return fail(e, FRNN_ERR_INVALID_ARG, "unknown path");
     e->forced_path = path;
     return FRNN_OK;
+}
+
+int frnn_set_option(frnn_engine* e, int option, int64_t value) {
+    if (!e) return FRNN_ERR_INVALID_ARG;
+    switch (option) {
+        case FRNN_OPT_DIRECT_OUTPUT_MAX_BYTES:
+            if (value < 0) return fail(e, FRNN_ERR_INVALID_ARG, "value must be >= 0");
+            e->direct_output_max_bytes = value;
+            return FRNN_OK;
+        default:
+            return fail(e, FRNN_ERR_INVALID_ARG, "unknown option");
+    }
 }
 
 int frnn_last_plan(const frnn_engine* e, int* path, int* grid_dims, int64_t* cells) {

@@ -35,7 +35,9 @@ _lib = None
 
 
 def library_path() -> str:
-    return os.path.join(_HERE, "libfrnn_b200.so")
+    """The engine library: FRNN_B200_LIBRARY if set (an alternate build, e.g.
+    with other launch-policy macros), else the in-tree build."""
+    return os.environ.get("FRNN_B200_LIBRARY") or os.path.join(_HERE, "libfrnn_b200.so")
 
 
 class FRNNError(RuntimeError):
@@ -70,6 +72,7 @@ def load_library() -> ctypes.CDLL:
         "frnn_set_timing": (I, [P, I]),
         "frnn_last_stage_times": (I, [P, ctypes.POINTER(F), I]),
         "frnn_launch_count": (I, [P, ctypes.POINTER(L)]),
+        "frnn_set_option": (I, [P, I, L]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -214,6 +217,11 @@ class FRNNEngine:
         if isinstance(path, str):
             path = {v: k for k, v in PATH_NAMES.items()}[path]
         self._check(self._lib.frnn_set_path(self._eng, int(path)), "set_path")
+
+    OPT_DIRECT_OUTPUT_MAX_BYTES = 1
+
+    def set_option(self, option: int, value: int) -> None:
+        self._check(self._lib.frnn_set_option(self._eng, int(option), int(value)), "set_option")
 
     STAGES = ("bbox", "hash", "scan", "scatter", "search", "unpermute", "brute")
 
