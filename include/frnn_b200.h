@@ -140,6 +140,22 @@ int frnn_last_stage_times(frnn_engine* e, float* ms, int n);
 /* Number of kernels this engine has launched since it was created. */
 int frnn_launch_count(const frnn_engine* e, int64_t* n);
 
+/* Allocation-free search.  No counterpart in the reference: it is for callers
+ * that cannot allocate device memory while they search (a framework whose own
+ * pool owns all device memory, a real-time loop with a fixed budget, code that
+ * must avoid the implicit synchronisation of cudaMalloc/cudaFree).  No engine
+ * object: the caller passes SoA points d_points_soa [d*N + i] and two
+ * caller-owned device buffers of K*N elements that receive the same SoA
+ * results [k*N + q] as frnn_search_gpu.  Scratch comes from one fixed device
+ * array inside the library (8.75 MiB, held on every GPU that loads the library
+ * until exit); nothing is allocated.  Limits: N <= 65,536, 1 <= dim <= 16,
+ * K <= 128; larger inputs return FRNN_ERR_INVALID_ARG.  All calls on a device
+ * share that array, so calls that overlap on the GPU race: serialise them.
+ * The first call on a device looks up the array's address; make it before any
+ * stream capture.  Runs on `stream` (0 = legacy default) and waits for it. */
+int frnn_search_gpu_noalloc(const float* d_points_soa, int N, int dim, int K, float radius,
+                            int* d_idx_out, float* d_dist_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
