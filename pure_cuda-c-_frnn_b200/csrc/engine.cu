@@ -53,7 +53,8 @@ struct frnn_engine {
 
     DevBuf box_partial, box_ticket, box_out;
     DevBuf counts, starts, scan_status, scan_ticket, err_flag;
-    DevBuf cellrank, rows, ids;
+    DevBuf cellrank, rows, ids, inv;
+    DevBuf lists, list_counts, overflow, n_overflow;
     DevBuf tmp_idx, tmp_dist, out_idx, out_dist;
     DevBuf in_stage, in_soa, out_rm_idx, out_rm_dist;
     float* h_box = nullptr;   // pinned, 9 floats
@@ -315,12 +316,43 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
                               e->epoch, e->err_flag.as<int>(), s),
                "scan launch");
     stage_end(e, ST_SCAN);
+    const bool two_kernel = P.dim == 3 && P.g == 3 && K <= 32;
+    if (two_kernel) FRNN_GROW(e, e->inv, (size_t)N * 4);
     stage_begin(e, ST_SCATTER);
     FRNN_CHECK(e, launch_scatter(d_pts, P, e->cellrank.as<int2>(), e->starts.as<int>(),
-                                 e->rows.as<float>(), e->ids.as<int>(), s),
+                                 e->rows.as<float>(), e->ids.as<int>(), s,
+                                 two_kernel ? e->inv.as<int>() : nullptr),
                "scatter launch");
     stage_end(e, ST_SCATTER);
     e->launches += 2;
+    if (two_kernel) {
+        // D = 3: collect every in-radius key per query, then sort and emit in
+        // original query order (no unpermute); queries whose list overflows
+        // are searched again by the cooperative kernel.
+        const int cap = K <= 16 ? 64 : 128;
+        FRNN_GROW(e, e->lists, (size_t)N * cap * 8);
+        FRNN_GROW(e, e->list_counts, (size_t)N * 4);
+        FRNN_GROW(e, e->overflow, (size_t)N * 4);
+        FRNN_GROW(e, e->n_overflow, 16);
+        FRNN_CHECK(e, cudaMemsetAsync(e->n_overflow.p, 0, 4, s), "memset overflow count");
+        stage_begin(e, ST_SEARCH);
+        FRNN_CHECK(e, launch_collect_d3(e->rows.as<float>(), e->starts.as<int>(), P, r2, cap,
+                                        e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
+                                        e->overflow.as<int>(), e->n_overflow.as<int>(), s),
+                   "collect launch");
+        stage_end(e, ST_SEARCH);
+        stage_begin(e, ST_UNPERMUTE);
+        FRNN_CHECK(e, launch_emit_lists(e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
+                                        e->inv.as<int>(), N, K, cap, r2, out_idx, out_dist, s),
+                   "emit launch");
+        FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(),
+                                         P, K, r2, 0, N, out_idx, out_dist, N, e->ids.as<int>(), s,
+                                         e->overflow.as<int>(), e->n_overflow.as<int>()),
+                   "overflow search launch");
+        stage_end(e, ST_UNPERMUTE);
+        e->launches += 3;
+        return FRNN_OK;
+    }
     // Small result sets: write straight to the original query ids (the
     // scattered stores stay in L2).  Large ones: write in cell order, then
     // unpermute one output row at a time.
@@ -487,7 +519,8 @@ int frnn_destroy(frnn_engine* e) {
         if (e->stream) cudaStreamSynchronize(e->stream);
         DevBuf* bufs[] = {&e->box_partial, &e->box_ticket, &e->box_out, &e->counts, &e->starts,
                           &e->scan_status, &e->scan_ticket, &e->err_flag, &e->cellrank, &e->rows,
-                          &e->ids, &e->tmp_idx, &e->tmp_dist, &e->out_idx, &e->out_dist,
+                          &e->ids, &e->inv, &e->lists, &e->list_counts, &e->overflow,
+                          &e->n_overflow, &e->tmp_idx, &e->tmp_dist, &e->out_idx, &e->out_dist,
                           &e->in_stage, &e->in_soa, &e->out_rm_idx, &e->out_rm_dist};
         for (DevBuf* b : bufs) free_buf(*b);
         for (cudaEvent_t& ev : e->ev)

@@ -17,17 +17,36 @@ long long scan_tiles(long long cells);
 cudaError_t launch_scan(const int* counts, int* starts, long long cells,
                         unsigned long long* status, int* ticket, unsigned epoch, int* err,
                         cudaStream_t s);
+// inv (optional): inv[original index] = sorted position
 cudaError_t launch_scatter(const float* pts, const GridPlan& P, const int2* cellrank,
-                           const int* starts, float* rows, int* ids, cudaStream_t s);
+                           const int* starts, float* rows, int* ids, cudaStream_t s,
+                           int* inv = nullptr);
 
 // grid_search.cu
 // Searches sorted query positions [q0, q1).  Results for sorted position sq go
 // to row (sq - q0) of the outputs: out[k*ostride + (sq - q0)], or, when
 // scatter_ids is non-null, straight to out[k*ostride + scatter_ids[sq]].
+// qlist (optional): the searched sorted positions are qlist[q0..q1) instead
+// of q0..q1 (then scatter_ids must be given); qcount (optional, device): only
+// the first *qcount of them.
 cudaError_t launch_grid_search(const float* rows, const int* ids, const int* starts,
                                const GridPlan& P, int K, float r2, int q0, int q1, int* oidx,
                                float* odist, long long ostride, const int* scatter_ids,
-                               cudaStream_t s);
+                               cudaStream_t s, const int* qlist = nullptr,
+                               const int* qcount = nullptr);
+
+// grid_collect.cu -- D = 3 two-kernel search (K <= 32).
+// collect: every in-radius key of sorted query sq goes to lists[sq*cap + j];
+// counts[sq] = number found; queries with more than cap are appended to
+// overflow[0..*n_overflow).
+cudaError_t launch_collect_d3(const float* rows, const int* starts, const GridPlan& P, float r2,
+                              int cap, unsigned long long* lists, int* counts, int* overflow,
+                              int* n_overflow, cudaStream_t s);
+// emit: for every original query q (sorted position inv[q]) whose count is at
+// most cap, the K smallest keys ascending to out[k*n + q], padded (-1, r2).
+cudaError_t launch_emit_lists(const unsigned long long* lists, const int* counts, const int* inv,
+                              int n, int K, int cap, float r2, int* oidx, float* odist,
+                              cudaStream_t s);
 // out[k*N + ids[sq]] = in[k*N + sq]
 cudaError_t launch_unpermute(const int* in_idx, const float* in_dist, const int* ids, int n,
                              int K, int* out_idx, float* out_dist, cudaStream_t s);

@@ -239,7 +239,8 @@ __global__ void __launch_bounds__(256) scatter_d3_kernel(const float* __restrict
                                                          const int2* __restrict__ cellrank,
                                                          const int* __restrict__ starts,
                                                          float4* __restrict__ rows,
-                                                         int* __restrict__ ids) {
+                                                         int* __restrict__ ids,
+                                                         int* __restrict__ inv) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     int2 cr = cellrank[i];
@@ -248,6 +249,7 @@ __global__ void __launch_bounds__(256) scatter_d3_kernel(const float* __restrict
     float x = __ldg(&pts[i]), y = __ldg(&pts[(long long)n + i]), z = __ldg(&pts[2LL * n + i]);
     rows[pos] = make_float4(x, y, z, __int_as_float(i));
     ids[pos] = i;
+    if (inv) inv[i] = pos;
 }
 
 __global__ void __launch_bounds__(256) scatter_rows_kernel(const float* __restrict__ pts, int n,
@@ -255,7 +257,8 @@ __global__ void __launch_bounds__(256) scatter_rows_kernel(const float* __restri
                                                            const int2* __restrict__ cellrank,
                                                            const int* __restrict__ starts,
                                                            float* __restrict__ rows,
-                                                           int* __restrict__ ids) {
+                                                           int* __restrict__ ids,
+                                                           int* __restrict__ inv) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     int2 cr = cellrank[i];
@@ -271,6 +274,7 @@ __global__ void __launch_bounds__(256) scatter_rows_kernel(const float* __restri
         dst[d >> 2] = t;
     }
     ids[pos] = i;
+    if (inv) inv[i] = (int)pos;
 }
 
 }  // namespace
@@ -306,13 +310,13 @@ cudaError_t launch_scan(const int* counts, int* starts, long long cells,
 }
 
 cudaError_t launch_scatter(const float* pts, const GridPlan& P, const int2* cellrank,
-                           const int* starts, float* rows, int* ids, cudaStream_t s) {
+                           const int* starts, float* rows, int* ids, cudaStream_t s, int* inv) {
     if (P.dim == 3)
         scatter_d3_kernel<<<(P.n + 255) / 256, 256, 0, s>>>(pts, P.n, cellrank, starts,
-                                                            reinterpret_cast<float4*>(rows), ids);
+                                                            reinterpret_cast<float4*>(rows), ids, inv);
     else
         scatter_rows_kernel<<<(P.n + 255) / 256, 256, 0, s>>>(pts, P.n, P.dim, P.row, cellrank,
-                                                              starts, rows, ids);
+                                                              starts, rows, ids, inv);
     return cudaGetLastError();
 }
 

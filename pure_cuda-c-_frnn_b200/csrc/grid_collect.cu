@@ -1,0 +1,176 @@
+// grid_collect.cu -- the D = 3 search as two kernels: collect, then emit.
+//
+// Replaces, for D = 3, the reference's FindNbrsAoS3Kernel (find_nbrs.cu:400-491)
+// followed by ScatterToOrigKernel (find_nbrs.cu:505-523).  Same candidates (the
+// 27-cell shell), same arithmetic, same acceptance rule (d2 < r2 strict, K
+// smallest, ties to the smaller index); the work is split where the GPU wants
+// it split:
+//
+//   collect  one thread per query in cell order (the lanes of a warp walk
+//            neighbouring cells, so candidate rows come from L1): every
+//            candidate with d2 < r2 is appended, as a 64-bit (d2, index) key,
+//            to the query's own list in global memory.  No selection and no
+//            sorting here, so the loop stays small and the kernel runs at full
+//            occupancy.  The lists are in cell order (lists[sq*cap + j]): a
+//            list fills whole 32-byte sectors as it grows, and the lists of a
+//            warp's queries are neighbours in memory.
+//   emit     one thread per query in ORIGINAL order (inv[] maps it to its cell
+//            order position), so the K result rows are written coalesced and no
+//            unpermute pass is needed.  Each thread keeps its K smallest keys in
+//            registers: the first KN keys are sorted by a bitonic network, the
+//            rest are folded in 16 at a time (sort the batch, keep the KN
+//            smallest of both with a half-cleaner, re-sort with a bitonic
+//            merge).  No shuffles and no warp-wide serialisation.
+//
+// A query with more than `cap` in-radius candidates is listed as overflowing
+// and searched again by the warp-cooperative kernel (grid_coop.cuh), which
+// has no such limit.
+#include "frnn_device.cuh"
+#include "frnn_internal.h"
+
+namespace frnn {
+namespace {
+
+__global__ void __launch_bounds__(256)
+    collect_d3_kernel(const float4* __restrict__ rows, const int* __restrict__ starts, GridPlan P,
+                      float r2, int cap, unsigned long long* __restrict__ lists,
+                      int* __restrict__ counts, int* __restrict__ overflow,
+                      int* __restrict__ n_overflow) {
+    const int sq = blockIdx.x * blockDim.x + threadIdx.x;
+    if (sq >= P.n) return;
+    const float4 q = __ldg(&rows[sq]);
+    const float cs = P.cell, eps = P.eps;
+    const int gx = cell_coord(q.x, P.origin[0], P.inv_cell, P.res[0]);
+    const int gy = cell_coord(q.y, P.origin[1], P.inv_cell, P.res[1]);
+    const int gz = cell_coord(q.z, P.origin[2], P.inv_cell, P.res[2]);
+    unsigned long long* mine = lists + (long long)sq * cap;
+    int n = 0;
+    for (int cz = max(gz - 1, 0); cz <= min(gz + 1, P.res[2] - 1); ++cz) {
+        const float bz = axis_gap(q.z, cz, P.origin[2], cs, eps);
+        if (bz * kPruneScale > r2) continue;
+        for (int cy = max(gy - 1, 0); cy <= min(gy + 1, P.res[1] - 1); ++cy) {
+            const float byz = bz + axis_gap(q.y, cy, P.origin[1], cs, eps);
+            if (byz * kPruneScale > r2) continue;
+            int xlo = max(gx - 1, 0), xhi = min(gx + 1, P.res[0] - 1);
+            if (xlo < gx && (byz + axis_gap(q.x, xlo, P.origin[0], cs, eps)) * kPruneScale > r2) xlo = gx;
+            if (xhi > gx && (byz + axis_gap(q.x, xhi, P.origin[0], cs, eps)) * kPruneScale > r2) xhi = gx;
+            const long long rb = (long long)cz * P.stride[2] + (long long)cy * P.stride[1];
+            // clamped to [0, n): a corrupt start table never reads out of bounds
+            int j = min(max(__ldg(&starts[rb + xlo]), 0), P.n);
+            const int e = min(max(__ldg(&starts[rb + xhi + 1]), j), P.n);
+            for (; j + 1 < e; j += 2) {
+                const float4 p0 = __ldg(&rows[j]);
+                const float4 p1 = __ldg(&rows[j + 1]);
+                const float d0 = dist2_d3(q.x, q.y, q.z, p0.x, p0.y, p0.z);
+                const float d1 = dist2_d3(q.x, q.y, q.z, p1.x, p1.y, p1.z);
+                if (d0 < r2) {
+                    if (n < cap) mine[n] = make_key(d0, __float_as_int(p0.w));
+                    ++n;
+                }
+                if (d1 < r2) {
+                    if (n < cap) mine[n] = make_key(d1, __float_as_int(p1.w));
+                    ++n;
+                }
+            }
+            if (j < e) {
+                const float4 p = __ldg(&rows[j]);
+                const float d = dist2_d3(q.x, q.y, q.z, p.x, p.y, p.z);
+                if (d < r2) {
+                    if (n < cap) mine[n] = make_key(d, __float_as_int(p.w));
+                    ++n;
+                }
+            }
+        }
+    }
+    counts[sq] = n;
+    if (n > cap) overflow[atomicAdd(n_overflow, 1)] = sq;
+}
+
+// Ascending bitonic merge of a bitonic register array.
+template <int N>
+__device__ __forceinline__ void bitonic_merge(unsigned long long (&a)[N]) {
+#pragma unroll
+    for (int j = N >> 1; j > 0; j >>= 1) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            const int l = i ^ j;
+            if (l > i) {
+                const unsigned long long x = a[i], y = a[l];
+                a[i] = x < y ? x : y;
+                a[l] = x < y ? y : x;
+            }
+        }
+    }
+}
+
+// The KN smallest keys of list[0..cnt) ascending in registers: sort the first
+// KN, then fold the remainder in batches of 16.
+template <int KN>
+__device__ __forceinline__ void top_keys(const unsigned long long* list, int cnt,
+                                         unsigned long long (&a)[KN]) {
+#pragma unroll
+    for (int i = 0; i < KN; ++i) a[i] = i < cnt ? list[i] : ~0ull;
+    bitonic_sort<KN>(a);
+    for (int base = KN; base < cnt; base += 16) {
+        unsigned long long b[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) b[i] = base + i < cnt ? list[base + i] : ~0ull;
+        bitonic_sort<16>(b);
+        // a ascending, b ascending padded with ~0 to KN: min(a[i], b'[KN-1-i])
+        // is bitonic and holds the KN smallest of both
+#pragma unroll
+        for (int i = KN - 16; i < KN; ++i) {
+            const unsigned long long v = b[KN - 1 - i];
+            a[i] = v < a[i] ? v : a[i];
+        }
+        bitonic_merge<KN>(a);
+    }
+}
+
+template <int KN>
+__global__ void __launch_bounds__(128)
+    emit_lists_kernel(const unsigned long long* __restrict__ lists, const int* __restrict__ counts,
+                      const int* __restrict__ inv, int n, int K, int cap, float r2,
+                      int* __restrict__ oidx, float* __restrict__ odist) {
+    const int q = blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= n) return;
+    const int sq = __ldg(&inv[q]);
+    const int cnt = __ldg(&counts[sq]);
+    if (cnt > cap) return;  // searched by the overflow pass
+    unsigned long long a[KN];
+    top_keys<KN>(lists + (long long)sq * cap, cnt, a);
+#pragma unroll
+    for (int i = 0; i < KN; ++i) {
+        if (i < K) {
+            const bool real = i < cnt;
+            oidx[(long long)i * n + q] = real ? key_idx(a[i]) : -1;
+            odist[(long long)i * n + q] = real ? key_d2(a[i]) : r2;
+        }
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_collect_d3(const float* rows, const int* starts, const GridPlan& P, float r2,
+                              int cap, unsigned long long* lists, int* counts, int* overflow,
+                              int* n_overflow, cudaStream_t s) {
+    collect_d3_kernel<<<(P.n + 255) / 256, 256, 0, s>>>(reinterpret_cast<const float4*>(rows),
+                                                        starts, P, r2, cap, lists, counts, overflow,
+                                                        n_overflow);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_emit_lists(const unsigned long long* lists, const int* counts, const int* inv,
+                              int n, int K, int cap, float r2, int* oidx, float* odist,
+                              cudaStream_t s) {
+    if (K > 32) return cudaErrorInvalidValue;  // the register top-K holds at most 32 keys
+    if (K <= 16)
+        emit_lists_kernel<16><<<(n + 127) / 128, 128, 0, s>>>(lists, counts, inv, n, K, cap, r2,
+                                                              oidx, odist);
+    else
+        emit_lists_kernel<32><<<(n + 127) / 128, 128, 0, s>>>(lists, counts, inv, n, K, cap, r2,
+                                                              oidx, odist);
+    return cudaGetLastError();
+}
+
+}  // namespace frnn

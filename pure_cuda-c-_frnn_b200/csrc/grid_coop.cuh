@@ -227,8 +227,10 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
     grid_coop_kernel(const float4* __restrict__ rows, const int* __restrict__ ids,
                      const int* __restrict__ starts, GridPlan P, int K, float r2, int q0, int q1,
                      int* __restrict__ oidx, float* __restrict__ odist, long long ostride,
-                     const int* __restrict__ scatter_ids) {
+                     const int* __restrict__ scatter_ids, const int* __restrict__ qlist,
+                     const int* __restrict__ qcount) {
     extern __shared__ __align__(16) unsigned char smem[];
+    if (qcount) q1 = min(q1, q0 + __ldg(qcount));  // list length known only on the device
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int cap = list_cap(K);
     unsigned char* wbase = smem + (size_t)warp * warp_bytes<NV, D3>(K);
@@ -248,7 +250,8 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
     int mygc[G];
 #pragma unroll
     for (int v = 0; v < NV; ++v)
-        myq[v] = lane < nq ? __ldg(&rows[(long long)(base + lane) * NV + v]) : make_float4(0, 0, 0, 0);
+        myq[v] = lane < nq ? __ldg(&rows[(long long)(qlist ? __ldg(&qlist[base + lane]) : base + lane) * NV + v])
+                           : make_float4(0, 0, 0, 0);
     {
         long long c = 0;
 #pragma unroll
@@ -383,7 +386,7 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
         for (int g = 0; g < kGroup; ++g) {
             if (g < gq) {
                 const int n = gcnt[g];
-                const int sq = base + g0 + g;
+                const int sq = qlist ? __ldg(&qlist[base + g0 + g]) : base + g0 + g;
                 const long long orow =
                     scatter_ids ? (long long)__ldg(&scatter_ids[sq]) : (long long)(sq - q0);
                 const unsigned long long* list = lists + (size_t)g * cap;

@@ -244,3 +244,18 @@ def test_search_is_deterministic(frnn):
     a = run_engine(frnn, soa, 32, r)
     b = run_engine(frnn, soa, 32, r)
     assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+
+
+@pytest.mark.parametrize("K", [8, 16, 32])
+def test_dense_lists_overflow_to_cooperative_pass(frnn, oracle_mod, K):
+    # D=3 with K <= 32 collects every in-radius key per query (64 or 128 of
+    # them at most) and hands queries with more to the cooperative kernel:
+    # a dense core (hundreds in radius) next to a sparse halo exercises both.
+    rng = np.random.default_rng(K)
+    core = (0.5 + 0.002 * rng.standard_normal((3000, 3))).astype(np.float32)
+    halo = rng.random((20000, 3)).astype(np.float32)
+    pts = np.concatenate([halo[:10000], core, halo[10000:]])
+    soa = datagen.soa(pts)
+    idx, dist, plan = run_engine(frnn, soa, K, 0.01, path="grid")
+    oi, od, _ = oracle_mod.search(soa, K, 0.01)
+    assert_bit_exact(idx, dist, oi, od, f"overflow K={K}")
