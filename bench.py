@@ -252,6 +252,9 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
             "scatter": N * D * 4 + N * 8 + N * row + 4 * N,
             "bbox": N * min(D, 4) * 4,
             "brute": N * D * 4 + N * K * 8,
+            # lists hold every in-radius key (mean = the calibrated target count)
+            "collect": N * row + 4 * (cells + 1) + N * c.target * 8 + 4 * N,
+            "emit": N * c.target * 8 + 8 * N + N * K * 8,
         }[dom]
         t = stage_ms[dom] / 1e3
         achieved = alg / t / 1e9

@@ -59,8 +59,10 @@ enum frnn_path {
     FRNN_PATH_GRID = 1,        /* uniform grid on the leading min(D,4) axes,      *
                                 * full-D ranking (full-D grid when D <= 3)         */
     FRNN_PATH_BRUTE = 2,       /* tiled brute force, SIMT fp32                    */
-    FRNN_PATH_BRUTE_TC = 3     /* brute force with a tcgen05 distance filter and  *
-                                * exact fp32 re-rank (D a multiple of 16)          */
+    FRNN_PATH_BRUTE_TC = 3     /* brute force with a tcgen05 fp16 distance filter *
+                                * and exact fp32 re-rank; same results as         *
+                                * FRNN_PATH_BRUTE.  The dispatcher takes it for   *
+                                * D > 32 and N >= 1024                            */
 };
 
 /* Constructor.  Replaces FRNNEngine::FRNNEngine(int max_points)
@@ -133,7 +135,11 @@ int frnn_set_option(frnn_engine* e, int option, int64_t value);
  * around its stages on the engine stream; frnn_last_stage_times writes the
  * last search's milliseconds for stages 0..n-1 (0 bounding box, 1 cell
  * histogram, 2 prefix scan, 3 scatter, 4 neighbour search, 5 unpermute,
- * 6 brute force), -1 for stages that did not run. */
+ * 6 brute force, 7 candidate collection and 8 list emit -- stages 7 and 8
+ * replace 4 and 5 for D = 3 with K <= 32 -- and, on FRNN_PATH_BRUTE_TC,
+ * 9 prep, 10 tensor-core filter, 11 exact re-rank, with 6 timing the
+ * brute-force pass over queries whose candidate list overflowed), -1 for
+ * stages that did not run. */
 int frnn_set_timing(frnn_engine* e, int enable);
 int frnn_last_stage_times(frnn_engine* e, float* ms, int n);
 

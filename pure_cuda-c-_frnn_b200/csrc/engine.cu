@@ -32,13 +32,20 @@ struct DevBuf {
 };
 
 constexpr int kBoxMaxBlocks = 1024;
-#define FRNN_STAGES 7   // bbox, hash, scan, scatter, search, unpermute, brute force
+// bbox, hash, scan, scatter, search, unpermute, brute force, collect, emit,
+// tensor-core prep, tensor-core filter, exact re-rank
+#define FRNN_STAGES 12
 
 // Brute force is taken when the all-pairs work is small enough that the grid
 // build would dominate (the reference's own small-input rule is
 // N^2*D*ceil(K/8) <= 2e6, frnn_engine.cu:215-219; a B200 finishes far larger
 // all-pairs problems in the time of one grid build).
 constexpr double kBruteSmallWork = 4.0e8;   // N*N*D below this -> brute force
+// D > 32 goes to brute force; from this many points on, with the tcgen05
+// distance filter (measured on B200 at D = 128, K = 128: 0.22 ms against the
+// SIMT kernel's 29 ms at N = 4096; below ~1K points the filter's prep and two
+// host round trips are most of its time).
+constexpr int kTcMinPoints = 1024;
 
 }  // namespace
 
@@ -57,7 +64,9 @@ struct frnn_engine {
     DevBuf lists, list_counts, overflow, n_overflow;
     DevBuf tmp_idx, tmp_dist, out_idx, out_dist;
     DevBuf in_stage, in_soa, out_rm_idx, out_rm_dist;
+    DevBuf tc_box, tc_center, tc_tiles, tc_rows, tc_qa, tc_pb;
     float* h_box = nullptr;   // pinned, 9 floats
+    float* h_tc = nullptr;    // pinned, 512 floats: per-dimension box + flag, then the centre
     int* h_err = nullptr;     // pinned
 
     int last_N = -1, last_K = -1;
@@ -130,7 +139,10 @@ int grow(frnn_engine* e, DevBuf& b, size_t bytes, const char* what) {
         if (st__ != FRNN_OK) return st__;                          \
     } while (0)
 
-enum Stage { ST_BBOX = 0, ST_HASH, ST_SCAN, ST_SCATTER, ST_SEARCH, ST_UNPERMUTE, ST_BRUTE };
+enum Stage {
+    ST_BBOX = 0, ST_HASH, ST_SCAN, ST_SCATTER, ST_SEARCH, ST_UNPERMUTE, ST_BRUTE, ST_COLLECT, ST_EMIT,
+    ST_TC_PREP, ST_TC_FILTER, ST_TC_RERANK
+};
 
 void stage_begin(frnn_engine* e, int st) {
     if (e->timing) cudaEventRecord(e->ev[2 * st], e->stream);
@@ -335,13 +347,13 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
         FRNN_GROW(e, e->overflow, (size_t)N * 4);
         FRNN_GROW(e, e->n_overflow, 16);
         FRNN_CHECK(e, cudaMemsetAsync(e->n_overflow.p, 0, 4, s), "memset overflow count");
-        stage_begin(e, ST_SEARCH);
+        stage_begin(e, ST_COLLECT);
         FRNN_CHECK(e, launch_collect_d3(e->rows.as<float>(), e->starts.as<int>(), P, r2, cap,
                                         e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
                                         e->overflow.as<int>(), e->n_overflow.as<int>(), s),
                    "collect launch");
-        stage_end(e, ST_SEARCH);
-        stage_begin(e, ST_UNPERMUTE);
+        stage_end(e, ST_COLLECT);
+        stage_begin(e, ST_EMIT);
         FRNN_CHECK(e, launch_emit_lists(e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
                                         e->inv.as<int>(), N, K, cap, r2, out_idx, out_dist, s),
                    "emit launch");
@@ -349,7 +361,7 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
                                          P, K, r2, 0, N, out_idx, out_dist, N, e->ids.as<int>(), s,
                                          e->overflow.as<int>(), e->n_overflow.as<int>()),
                    "overflow search launch");
-        stage_end(e, ST_UNPERMUTE);
+        stage_end(e, ST_EMIT);
         e->launches += 3;
         return FRNN_OK;
     }
@@ -383,6 +395,100 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
     return FRNN_OK;
 }
 
+// Brute force with the tcgen05 distance filter (bf_tc.cu).  Sets *done = false
+// (and launches nothing that writes results) when the data do not suit the
+// filter -- non-finite coordinates, or a radius whose scaled square is not a
+// finite fp32 -- and the caller runs the SIMT brute force instead.
+int run_brute_tc(frnn_engine* e, const float* d_pts, int N, int dim, int K, float radius,
+                 int* out_idx, float* out_dist, bool* done) {
+    cudaStream_t s = e->stream;
+    *done = false;
+    const float r2 = radius * radius;
+    FRNN_GROW(e, e->tc_box, 512 * sizeof(float) + 16);
+    int* nonfinite = reinterpret_cast<int*>(e->tc_box.as<float>() + 512);
+    stage_begin(e, ST_TC_PREP);
+    FRNN_CHECK(e, cudaMemsetAsync(nonfinite, 0, sizeof(int), s), "memset non-finite flag");
+    FRNN_CHECK(e, launch_tc_box(d_pts, N, dim, e->tc_box.as<float>(), nonfinite, s), "box launch");
+    e->launches++;
+    FRNN_CHECK(e, cudaMemcpyAsync(e->h_tc, e->tc_box.p, 2 * dim * sizeof(float), cudaMemcpyDeviceToHost, s),
+               "box readback");
+    FRNN_CHECK(e, cudaMemcpyAsync(e->h_tc + 2 * kMaxK, nonfinite, sizeof(int), cudaMemcpyDeviceToHost, s),
+               "flag readback");
+    FRNN_CHECK(e, cudaStreamSynchronize(s), "box sync");
+    int flag = 0;
+    std::memcpy(&flag, e->h_tc + 2 * kMaxK, sizeof(int));
+    if (flag != 0) return FRNN_OK;
+
+    // centre = per-dimension midpoint; scale = 2^(14 - e) with max|x - c| < 2^e,
+    // so every scaled coordinate stays below 2^14 in magnitude (fp16 max 65504)
+    float* center = e->h_tc + 2 * kMaxK + 4;
+    double hmax = 0.0;
+    for (int d = 0; d < dim; ++d) {
+        const double lo = e->h_tc[2 * d], hi = e->h_tc[2 * d + 1];
+        center[d] = (float)(0.5 * (lo + hi));
+        hmax = std::max(hmax, std::max(hi - (double)center[d], (double)center[d] - lo));
+    }
+    int ex = 0;
+    if (hmax > 0.0) std::frexp(hmax * (1.0 + 1e-6), &ex);
+    const int sexp = std::max(-120, std::min(120, 14 - ex));
+    const double scale = hmax > 0.0 ? std::ldexp(1.0, sexp) : 1.0;
+    const double eta = std::ldexp(1.0, -25);
+    const double rcd = (double)r2 * scale * scale * (1.0 + std::ldexp(1.0, -15)) + 4.0 * dim * eta * eta;
+    float rc = (float)rcd;
+    if ((double)rc < rcd) rc = std::nextafter(rc, INFINITY);
+    if (!std::isfinite(rc)) return FRNN_OK;
+    const float one_minus_alpha = 1.0f - std::ldexp(1.0f, -8);
+    const float eta_c = (float)(4.0 * eta * std::sqrt((double)dim));
+
+    const int ntiles = (N + 127) / 128;
+    const int dp = tc_row_floats(dim);
+    const int cap = tc_list_cap(K);
+    FRNN_GROW(e, e->tc_center, (size_t)dim * 4);
+    FRNN_GROW(e, e->tc_tiles, (size_t)ntiles * tc_tile_bytes(dim));
+    FRNN_GROW(e, e->tc_rows, (size_t)N * dp * 4);
+    FRNN_GROW(e, e->tc_qa, (size_t)ntiles * 128 * 4);
+    FRNN_GROW(e, e->tc_pb, (size_t)ntiles * 128 * 4);
+    FRNN_GROW(e, e->lists, (size_t)N * cap * 4);
+    FRNN_GROW(e, e->list_counts, (size_t)N * 4);
+    FRNN_GROW(e, e->overflow, (size_t)N * 4);
+    FRNN_GROW(e, e->n_overflow, 16);
+    FRNN_CHECK(e, cudaMemcpyAsync(e->tc_center.p, center, (size_t)dim * 4, cudaMemcpyHostToDevice, s),
+               "centre upload");
+    FRNN_CHECK(e, launch_tc_prep(d_pts, N, dim, e->tc_center.as<float>(), (float)scale, one_minus_alpha,
+                                 eta_c, rc, e->tc_tiles.as<uint8_t>(), e->tc_rows.as<float>(),
+                                 e->tc_qa.as<float>(), e->tc_pb.as<float>(), s),
+               "prep launch");
+    stage_end(e, ST_TC_PREP);
+    FRNN_CHECK(e, cudaMemsetAsync(e->n_overflow.p, 0, 4, s), "memset overflow count");
+    stage_begin(e, ST_TC_FILTER);
+    FRNN_CHECK(e, launch_tc_filter(e->tc_tiles.as<uint8_t>(), e->tc_qa.as<float>(), e->tc_pb.as<float>(), N,
+                                   dim, cap, e->lists.as<int>(), e->list_counts.as<int>(),
+                                   e->overflow.as<int>(), e->n_overflow.as<int>(), e->err_flag.as<int>(), s),
+               "filter launch");
+    stage_end(e, ST_TC_FILTER);
+    stage_begin(e, ST_TC_RERANK);
+    FRNN_CHECK(e, launch_tc_rerank(e->tc_rows.as<float>(), dim, e->lists.as<int>(), e->list_counts.as<int>(),
+                                   cap, N, K, r2, out_idx, out_dist, s),
+               "rerank launch");
+    stage_end(e, ST_TC_RERANK);
+    e->launches += 3;
+    // queries with more candidates than their list holds: SIMT brute force
+    int* h_nov = reinterpret_cast<int*>(e->h_tc + 2 * kMaxK + 1);
+    FRNN_CHECK(e, cudaMemcpyAsync(h_nov, e->n_overflow.p, sizeof(int), cudaMemcpyDeviceToHost, s),
+               "overflow count readback");
+    FRNN_CHECK(e, cudaStreamSynchronize(s), "overflow count sync");
+    if (*h_nov > 0) {
+        stage_begin(e, ST_BRUTE);
+        FRNN_CHECK(e, launch_bruteforce(d_pts, N, dim, K, r2, 0, *h_nov, out_idx, out_dist, N, s,
+                                        e->overflow.as<int>()),
+                   "overflow brute force launch");
+        stage_end(e, ST_BRUTE);
+        e->launches++;
+    }
+    *done = true;
+    return FRNN_OK;
+}
+
 int search_core(frnn_engine* e, const float* d_pts, int N, int dim, int K, float radius,
                 bool blocking) {
     cudaStream_t s = e->stream;
@@ -396,10 +502,10 @@ int search_core(frnn_engine* e, const float* d_pts, int N, int dim, int K, float
     int path = e->forced_path;
     if (path == FRNN_PATH_AUTO) {
         const double work = (double)N * (double)N * dim;
-        if (dim > 32 || work <= kBruteSmallWork) path = FRNN_PATH_BRUTE;
+        if (dim > 32) path = N >= kTcMinPoints ? FRNN_PATH_BRUTE_TC : FRNN_PATH_BRUTE;
+        else if (work <= kBruteSmallWork) path = FRNN_PATH_BRUTE;
         else path = FRNN_PATH_GRID;
     }
-    if (path == FRNN_PATH_BRUTE_TC) path = FRNN_PATH_BRUTE;  // until the tensor-core path lands
     if (path == FRNN_PATH_GRID && dim > 32) path = FRNN_PATH_BRUTE;
 
     GridPlan P{};
@@ -422,12 +528,20 @@ int search_core(frnn_engine* e, const float* d_pts, int N, int dim, int K, float
         if (!grid_ok) path = FRNN_PATH_BRUTE;
     }
 
+    if (path == FRNN_PATH_BRUTE_TC) {
+        bool done = false;
+        int st = run_brute_tc(e, d_pts, N, dim, K, radius, out_idx, out_dist, &done);
+        if (st != FRNN_OK) return st;
+        if (!done) path = FRNN_PATH_BRUTE;
+        e->last_g = 0;
+        e->last_cells = 0;
+    }
     if (path == FRNN_PATH_GRID) {
         int st = run_grid(e, d_pts, N, dim, K, r2, P, out_idx, out_dist);
         if (st != FRNN_OK) return st;
         e->last_g = P.g;
         e->last_cells = P.cells;
-    } else {
+    } else if (path == FRNN_PATH_BRUTE) {
         stage_begin(e, ST_BRUTE);
         FRNN_CHECK(e, launch_bruteforce(d_pts, N, dim, K, r2, 0, N, out_idx, out_dist, N, s),
                    "bruteforce launch");
@@ -447,7 +561,7 @@ int search_core(frnn_engine* e, const float* d_pts, int N, int dim, int K, float
             cudaMemsetAsync(e->err_flag.p, 0, sizeof(int), s);
             cudaStreamSynchronize(s);
             e->last_N = -1;
-            return fail(e, FRNN_ERR_TIMEOUT, "prefix-scan look-back wait gave up");
+            return fail(e, FRNN_ERR_TIMEOUT, "a bounded device-side wait gave up");
         }
     }
     return FRNN_OK;
@@ -502,7 +616,8 @@ int frnn_create(int max_points, int device, frnn_engine** out) {
     }
     if (cudaMemset(e->box_ticket.p, 0, e->box_ticket.bytes) != cudaSuccess ||
         cudaMemset(e->err_flag.p, 0, e->err_flag.bytes) != cudaSuccess ||
-        cudaMallocHost(&e->h_box, 64) != cudaSuccess || cudaMallocHost(&e->h_err, 64) != cudaSuccess) {
+        cudaMallocHost(&e->h_box, 64) != cudaSuccess || cudaMallocHost(&e->h_err, 64) != cudaSuccess ||
+        cudaMallocHost(&e->h_tc, 512 * sizeof(float)) != cudaSuccess) {
         cudaGetLastError();
         frnn_destroy(e);
         return FRNN_ERR_OOM;
@@ -521,12 +636,15 @@ int frnn_destroy(frnn_engine* e) {
                           &e->scan_status, &e->scan_ticket, &e->err_flag, &e->cellrank, &e->rows,
                           &e->ids, &e->inv, &e->lists, &e->list_counts, &e->overflow,
                           &e->n_overflow, &e->tmp_idx, &e->tmp_dist, &e->out_idx, &e->out_dist,
-                          &e->in_stage, &e->in_soa, &e->out_rm_idx, &e->out_rm_dist};
+                          &e->in_stage, &e->in_soa, &e->out_rm_idx, &e->out_rm_dist,
+                          &e->tc_box, &e->tc_center, &e->tc_tiles, &e->tc_rows, &e->tc_qa,
+                          &e->tc_pb};
         for (DevBuf* b : bufs) free_buf(*b);
         for (cudaEvent_t& ev : e->ev)
             if (ev) cudaEventDestroy(ev);
         if (e->h_box) cudaFreeHost(e->h_box);
         if (e->h_err) cudaFreeHost(e->h_err);
+        if (e->h_tc) cudaFreeHost(e->h_tc);
     }
     delete e;
     return FRNN_OK;

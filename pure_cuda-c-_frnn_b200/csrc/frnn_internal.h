@@ -3,6 +3,8 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
 #include "frnn_device.cuh"
 
 namespace frnn {
@@ -53,8 +55,31 @@ cudaError_t launch_unpermute(const int* in_idx, const float* in_dist, const int*
 
 // bruteforce.cu
 // Queries [q0, q1) of the SoA cloud against all n points; results of query q
-// go to out[k*ostride + (q - q0)].
+// go to out[k*ostride + (q - q0)].  With qlist (device), the queries are
+// qlist[q0..q1) instead and query q's results go to out[k*ostride + q].
 cudaError_t launch_bruteforce(const float* pts, int n, int dim, int K, float r2, int q0, int q1,
-                              int* oidx, float* odist, long long ostride, cudaStream_t s);
+                              int* oidx, float* odist, long long ostride, cudaStream_t s,
+                              const int* qlist = nullptr);
+
+// bf_tc.cu -- brute force with a tcgen05 distance filter, 33 <= dim <= 128.
+int tc_kc(int dim);                 // 64-dimension slabs per row (1 or 2)
+size_t tc_tile_bytes(int dim);      // bytes of one 128-row fp16 tile
+int tc_row_floats(int dim);         // floats per fp32 row (dim rounded up to 4)
+int tc_list_cap(int K);             // candidate list capacity per query
+// box[2d], box[2d+1] = min, max of dimension d; *nonfinite |= any NaN/Inf
+cudaError_t launch_tc_box(const float* pts, int n, int dim, float* box, int* nonfinite, cudaStream_t s);
+// fp16 tiles (ceil(n/128) tiles), fp32 rows, threshold terms qa / pb (padded
+// to whole tiles with +inf)
+cudaError_t launch_tc_prep(const float* pts, int n, int dim, const float* center, float scale,
+                           float one_minus_alpha, float eta_c, float rc, uint8_t* tiles, float* rows32,
+                           float* qa, float* pb, cudaStream_t s);
+// counts[q] = candidates of query q (all q < n); the first cap of them in
+// lists[q*cap ..]; queries with more go to overflow[0..*n_overflow)
+cudaError_t launch_tc_filter(const uint8_t* tiles, const float* qa, const float* pb, int n, int dim,
+                             int cap, int* lists, int* counts, int* overflow, int* n_overflow, int* err,
+                             cudaStream_t s);
+// exact results for every query with counts[q] <= cap
+cudaError_t launch_tc_rerank(const float* rows32, int dim, const int* lists, const int* counts, int cap,
+                             int n, int K, float r2, int* oidx, float* odist, cudaStream_t s);
 
 }  // namespace frnn

@@ -223,7 +223,8 @@ class FRNNEngine:
     def set_option(self, option: int, value: int) -> None:
         self._check(self._lib.frnn_set_option(self._eng, int(option), int(value)), "set_option")
 
-    STAGES = ("bbox", "hash", "scan", "scatter", "search", "unpermute", "brute")
+    STAGES = ("bbox", "hash", "scan", "scatter", "search", "unpermute", "brute", "collect", "emit",
+              "tc_prep", "tc_filter", "tc_rerank")
 
     def set_timing(self, enable: bool) -> None:
         self._check(self._lib.frnn_set_timing(self._eng, int(bool(enable))), "set_timing")
