@@ -58,6 +58,10 @@ def parse():
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--mode", choices=["weak", "strong"], default="weak",
+                    help="weak: every rank searches its own cloud (no data-path collective); "
+                         "strong: one cloud, queries sharded over the ranks (broadcast, part "
+                         "search, gather to rank 0 inside every step)")
     return ap.parse_args()
 
 
@@ -66,8 +70,9 @@ def measured_peaks():
     if os.path.exists(path):
         with open(path) as f:
             j = json.load(f)
-        return float(j["hbm_gbs"]), float(j.get("bf16_tflops", 1590.0)), "measured"
-    return 6650.0, 1590.0, "fallback"
+        return (float(j["hbm_gbs"]), float(j.get("bf16_tflops", 1590.0)),
+                float(j.get("bf16_tflops_sustained", 1400.0)), "measured")
+    return 6650.0, 1590.0, 1400.0, "fallback"
 
 
 class ClockSampler:
@@ -168,12 +173,18 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
     import frnn_cuda
     c = datagen.config(a.config)
     N, D, K, r = c.N, c.D, c.K, c.radius
-    pts = datagen.generate(c.kind, N, D, seed=datagen.SEED + rank)
+    strong = a.mode == "strong" and world > 1
+    pts = datagen.generate(c.kind, N, D, seed=datagen.SEED + (0 if strong else rank))
     soa = datagen.soa(pts)
     x = torch.from_numpy(soa).to(dev)
     eng = frnn_cuda.FRNNEngine(max_points=N, device=dev)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
-    step = lambda: eng.search_gpu(x.data_ptr(), N, D, K, r)  # noqa: E731
+    if strong:
+        from frnn_cuda.sharded import engine_part_search, search_sharded
+        part = engine_part_search(eng)
+        step = lambda: search_sharded(x if rank == 0 else None, N, D, K, r, part)  # noqa: E731
+    else:
+        step = lambda: eng.search_gpu(x.data_ptr(), N, D, K, r)  # noqa: E731
 
     for _ in range(max(3, a.warmup)):
         step()
@@ -211,7 +222,7 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
     if world > 1:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms_max = float(ms_t.item())
-    value = world * N / (ms_max / 1e3)
+    value = (1 if strong else world) * N / (ms_max / 1e3)
 
     # end-to-end through the host-buffer entry point (pinned buffers)
     e2e = None
@@ -220,7 +231,17 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
         h_idx = torch.empty((K, N), dtype=torch.int32).pin_memory()
         h_dst = torch.empty((K, N), dtype=torch.float32).pin_memory()
         hi, hx, hd = h_in.numpy(), h_idx.numpy(), h_dst.numpy()
-        e2e_step = lambda: eng.search_soa_host(hi, K, r, hx, hd)  # noqa: E731
+        if strong:
+            def e2e_step():
+                # rank 0: pinned host cloud in, sharded search, results out
+                if rank == 0:
+                    x.copy_(h_in, non_blocking=True)
+                out = step()
+                if rank == 0:
+                    h_idx.copy_(out[0])
+                    h_dst.copy_(out[1])
+        else:
+            e2e_step = lambda: eng.search_soa_host(hi, K, r, hx, hd)  # noqa: E731
         for _ in range(2):
             e2e_step()
         if world > 1:
@@ -229,14 +250,14 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
         et = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
         if world > 1:
             dist.all_reduce(et, op=dist.ReduceOp.MAX)
-        e2e = {"value": world * N / (float(et.item()) / 1e3), "unit": "queries/s",
+        e2e = {"value": (1 if strong else world) * N / (float(et.item()) / 1e3), "unit": "queries/s",
                "h2d_bytes_per_step": int(N * D * 4), "d2h_bytes_per_step": int(N * K * 8),
                "ms_per_step": float(et.item())}
 
     if rank != 0:
         return None
 
-    hbm, bf16, peak_src = measured_peaks()
+    hbm, bf16, bf16_sus, peak_src = measured_peaks()
     # dominant kernel: the stage with the largest device time
     dom = max(stage_ms, key=stage_ms.get) if stage_ms else None
     roofline = None
@@ -255,26 +276,46 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
             # lists hold every in-radius key (mean = the calibrated target count)
             "collect": N * row + 4 * (cells + 1) + N * c.target * 8 + 4 * N,
             "emit": N * c.target * 8 + 8 * N + N * K * 8,
+            # tensor-core brute force: prep reads the SoA cloud, writes fp16
+            # tiles, fp32 rows and two terms per point; the re-rank reads each
+            # query's candidate rows (mean = the calibrated target count) and
+            # writes K results
+            "tc_prep": N * D * 4 + N * ((D + 63) // 64 * 64) * 2 + N * ((D + 3) // 4 * 4) * 4 + 8 * N,
+            "tc_rerank": N * c.target * (((D + 3) // 4 * 4) * 4 + 4) + N * K * 8,
+            # the filter is a dense contraction: 2*N*N*D flops (below)
+            "tc_filter": 2.0 * N * N * D,
         }[dom]
         t = stage_ms[dom] / 1e3
-        achieved = alg / t / 1e9
         traffic = None
         tpath = os.path.join(ROOT, "profiles", "traffic.json")
         if os.path.exists(tpath):
             with open(tpath) as f:
                 traffic = json.load(f).get(f"cfg{a.config}", {}).get(dom)
-        roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm,
-                    "unit": "GB/s", "frac": achieved / hbm, "traffic": traffic,
-                    "peak_source": peak_src, "alg_bytes": int(alg), "kernel_ms": stage_ms[dom]}
+        if dom == "tc_filter":
+            # a kernel of hundreds of ms inside the step: the sustained peak
+            achieved = alg / t / 1e12
+            roofline = {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": bf16_sus,
+                        "unit": "TFLOP/s", "frac": achieved / bf16_sus, "traffic": traffic,
+                        "peak_source": peak_src + " (bf16 sustained; the filter runs fp16 inputs "
+                                                  "with fp32 accumulation, same dense rate)",
+                        "alg_flops": alg, "kernel_ms": stage_ms[dom]}
+        else:
+            achieved = alg / t / 1e9
+            roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm,
+                        "unit": "GB/s", "frac": achieved / hbm, "traffic": traffic,
+                        "peak_source": peak_src, "alg_bytes": int(alg), "kernel_ms": stage_ms[dom]}
     b_alg = 4 * N * (3 * D + 4 + 2 * K) + 12 * plan["cells"]
     line = {
         "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_max,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong" if strong else "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic (seeded generator, rank r uses seed 1234+r)",
         "config": {"workload": c.name, "describe": c.describe, "N": N, "D": D, "K": K,
-                   "radius": r, "queries_per_gpu": N, "l2": "flushed before every timed step",
-                   "parallelism": f"independent clouds x{world}"},
+                   "radius": r, "queries_per_gpu": N // world if strong else N,
+                   "l2": "flushed before every timed step",
+                   "parallelism": (f"one cloud, queries sharded over {world} ranks (NCCL broadcast "
+                                   f"+ part search + gather to rank 0 in every step)") if strong
+                                  else f"independent clouds x{world}"},
         "latency_ms": ms_max,
         "pipeline": {"b_alg_bytes": int(b_alg), "b_alg_gbs": b_alg / (ms_max / 1e3) / 1e9,
                      "b_alg_frac": b_alg / (ms_max / 1e3) / 1e9 / hbm, "plan": plan,

@@ -116,6 +116,25 @@ int frnn_last_plan(const frnn_engine* e, int* path, int* grid_dims, int64_t* cel
 int frnn_search_gpu_async(frnn_engine* e, const float* d_points_soa, int N, int dim, int K,
                           float radius, int** d_idxs, float** d_dists);
 
+/* Part of a search, for sharding the queries of one cloud over several
+ * engines (one per GPU).  No counterpart in the reference, whose engine only
+ * searches whole clouds; SURVEY-style query sharding splits the reference's
+ * search_gpu (python_interface/frnn_engine.cu:195-250) this way.  Every part
+ * sees all N points; part `part` of `nparts` searches one contiguous slice of
+ * the engine's query order (cell order on the grid path, input order on brute
+ * force, whole 128-query tiles on the tensor-core path), and the slices of
+ * parts 0..nparts-1 cover every query exactly once when every part is given
+ * the same points, N, dim, K, radius and path.  On return *n_rows is the
+ * slice's size and the engine-owned device arrays hold
+ *   d_row_ids[j]                original index of the query of row j,
+ *   d_idxs[k*n_rows + j],       its k-th neighbour (ascending (d2, index),
+ *   d_dists[k*n_rows + j]       padding (-1, r^2)), exactly as the whole
+ *                               search would report it.
+ * Blocking, like frnn_search_gpu.  frnn_get_results does not read parts. */
+int frnn_search_gpu_part(frnn_engine* e, const float* d_points_soa, int N, int dim, int K, float radius,
+                         int part, int nparts, int* n_rows, int** d_row_ids, int** d_idxs,
+                         float** d_dists);
+
 /* Host path with caller-provided pinned or pageable buffers in the device
  * layouts: h_points_soa [d*N + i] in, SoA results [k*N + q] out.  The copies
  * run on the engine stream; used for end-to-end timing. */

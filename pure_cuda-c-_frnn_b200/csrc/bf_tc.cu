@@ -335,7 +335,8 @@ template <int KC>
 __global__ void __launch_bounds__(kThreads, 1)
     filter_kernel(const uint8_t* __restrict__ tiles, const float* __restrict__ qa, const float* __restrict__ pb,
                   int n, int ntiles, int cap, int* __restrict__ lists, int* __restrict__ counts,
-                  int* __restrict__ overflow, int* __restrict__ n_overflow, int* __restrict__ err) {
+                  int* __restrict__ overflow, int* __restrict__ n_overflow, int* __restrict__ err,
+                  int qb_begin, int qb_end) {
     using C = Cfg<KC>;
     constexpr int S = C::kStages;
     constexpr uint32_t TB = C::kTileBytes;
@@ -357,8 +358,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     int* qcnt = reinterpret_cast<int*>(tmem_slot + 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int qb0 = 2 * blockIdx.x;
-    const bool has1 = qb0 + 1 < ntiles;
+    // this CTA's two query blocks (the second absent at an odd end); the point
+    // tiles are all ntiles
+    const int qb0 = qb_begin + 2 * blockIdx.x;
+    const bool has1 = qb0 + 1 < qb_end;
     const int qb1 = has1 ? qb0 + 1 : qb0;
 
     if (threadIdx.x < 2 * kRows) qcnt[threadIdx.x] = 0;
@@ -527,15 +530,15 @@ constexpr int kRerankWarps = 8;
 template <int LCAP>
 __global__ void __launch_bounds__(kRerankWarps * 32)
     rerank_kernel(const float* __restrict__ rows32, int dim, int dp, const int* __restrict__ lists,
-                  const int* __restrict__ counts, int cap, int n, int K, float r2, int* __restrict__ oidx,
-                  float* __restrict__ odist) {
+                  const int* __restrict__ counts, int cap, int K, float r2, int* __restrict__ oidx,
+                  float* __restrict__ odist, int q0, int q1) {
     extern __shared__ unsigned long long rsmem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     unsigned long long* keys = rsmem + (size_t)warp * LCAP;
     float* qrow = reinterpret_cast<float*>(rsmem + (size_t)kRerankWarps * LCAP) + (size_t)warp * dp;
     const bool d3 = dp == 4 && dim == 3;
-    const int q = blockIdx.x * kRerankWarps + warp;
-    if (q >= n) return;
+    const int q = q0 + blockIdx.x * kRerankWarps + warp;
+    if (q >= q1) return;
     const int cnt = __ldg(&counts[q]);
     if (cnt > cap) return;  // searched by the fallback
     const float* qsrc = rows32 + (size_t)q * dp;
@@ -583,31 +586,33 @@ __global__ void __launch_bounds__(kRerankWarps * 32)
         }
     }
     __syncwarp();
-    coop::emit_list(keys, nl, K, r2, oidx + q, odist + q, n);
+    coop::emit_list(keys, nl, K, r2, oidx + (q - q0), odist + (q - q0), q1 - q0);
 }
 
 template <int LCAP>
-cudaError_t launch_rerank(const float* rows32, int dim, int dp, const int* lists, const int* counts, int cap, int n,
-                          int K, float r2, int* oidx, float* odist, cudaStream_t s) {
+cudaError_t launch_rerank(const float* rows32, int dim, int dp, const int* lists, const int* counts, int cap,
+                          int K, float r2, int* oidx, float* odist, int q0, int q1, cudaStream_t s) {
     const size_t smem = (size_t)kRerankWarps * (LCAP * 8 + dp * 4);
     cudaError_t e = cudaFuncSetAttribute(rerank_kernel<LCAP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
-    rerank_kernel<LCAP><<<(n + kRerankWarps - 1) / kRerankWarps, kRerankWarps * 32, smem, s>>>(
-        rows32, dim, dp, lists, counts, cap, n, K, r2, oidx, odist);
+    if (q1 <= q0) return cudaSuccess;
+    rerank_kernel<LCAP><<<(q1 - q0 + kRerankWarps - 1) / kRerankWarps, kRerankWarps * 32, smem, s>>>(
+        rows32, dim, dp, lists, counts, cap, K, r2, oidx, odist, q0, q1);
     return cudaGetLastError();
 }
 
 template <int KC>
 cudaError_t launch_filter_kc(const uint8_t* tiles, const float* qa, const float* pb, int n, int ntiles,
                              int cap, int* lists, int* counts, int* overflow, int* n_overflow, int* err,
-                             cudaStream_t s) {
+                             int qb_begin, int qb_end, cudaStream_t s) {
     const size_t smem = Cfg<KC>::kSmem;
     cudaError_t e =
         cudaFuncSetAttribute(filter_kernel<KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    filter_kernel<KC><<<(ntiles + 1) / 2, kThreads, smem, s>>>(tiles, qa, pb, n, ntiles, cap, lists, counts,
-                                                               overflow, n_overflow, err);
+    if (qb_end <= qb_begin) return cudaSuccess;
+    filter_kernel<KC><<<(qb_end - qb_begin + 1) / 2, kThreads, smem, s>>>(
+        tiles, qa, pb, n, ntiles, cap, lists, counts, overflow, n_overflow, err, qb_begin, qb_end);
     return cudaGetLastError();
 }
 
@@ -635,20 +640,25 @@ cudaError_t launch_tc_prep(const float* pts, int n, int dim, const float* center
 
 cudaError_t launch_tc_filter(const uint8_t* tiles, const float* qa, const float* pb, int n, int dim,
                              int cap, int* lists, int* counts, int* overflow, int* n_overflow, int* err,
-                             cudaStream_t s) {
+                             int qb_begin, int qb_end, cudaStream_t s) {
     const int ntiles = (n + tc::kRows - 1) / tc::kRows;
+    if (qb_begin < 0 || qb_end > ntiles) return cudaErrorInvalidValue;
     if (tc_kc(dim) == 1)
-        return tc::launch_filter_kc<1>(tiles, qa, pb, n, ntiles, cap, lists, counts, overflow, n_overflow, err, s);
-    return tc::launch_filter_kc<2>(tiles, qa, pb, n, ntiles, cap, lists, counts, overflow, n_overflow, err, s);
+        return tc::launch_filter_kc<1>(tiles, qa, pb, n, ntiles, cap, lists, counts, overflow, n_overflow, err,
+                                       qb_begin, qb_end, s);
+    return tc::launch_filter_kc<2>(tiles, qa, pb, n, ntiles, cap, lists, counts, overflow, n_overflow, err,
+                                   qb_begin, qb_end, s);
 }
 
 cudaError_t launch_tc_rerank(const float* rows32, int dim, const int* lists, const int* counts, int cap,
-                             int n, int K, float r2, int* oidx, float* odist, cudaStream_t s) {
+                             int n, int K, float r2, int* oidx, float* odist, int q0, int q1,
+                             cudaStream_t s) {
+    if (q0 < 0 || q1 > n) return cudaErrorInvalidValue;
     const int dp = tc_row_floats(dim);
     const int lcap = coop::list_cap(K);
-    if (lcap == 64) return tc::launch_rerank<64>(rows32, dim, dp, lists, counts, cap, n, K, r2, oidx, odist, s);
-    if (lcap == 128) return tc::launch_rerank<128>(rows32, dim, dp, lists, counts, cap, n, K, r2, oidx, odist, s);
-    return tc::launch_rerank<256>(rows32, dim, dp, lists, counts, cap, n, K, r2, oidx, odist, s);
+    if (lcap == 64) return tc::launch_rerank<64>(rows32, dim, dp, lists, counts, cap, K, r2, oidx, odist, q0, q1, s);
+    if (lcap == 128) return tc::launch_rerank<128>(rows32, dim, dp, lists, counts, cap, K, r2, oidx, odist, q0, q1, s);
+    return tc::launch_rerank<256>(rows32, dim, dp, lists, counts, cap, K, r2, oidx, odist, q0, q1, s);
 }
 
 }  // namespace frnn

@@ -23,13 +23,13 @@ template <bool D3, int KMAX>
 __global__ void __launch_bounds__(kBfThreads)
     bruteforce_kernel(const float* __restrict__ pts, int n, int dim, int K, float r2, int q0, int q1,
                       int* __restrict__ oidx, float* __restrict__ odist, long long ostride,
-                      int kBfTile, const int* __restrict__ qlist) {
+                      int kBfTile, const int* __restrict__ qlist, int row_base) {
     extern __shared__ unsigned long long smem[];
     unsigned long long* heap = smem;                                    // (K+B) x T keys
     float* tile = reinterpret_cast<float*>(heap + (size_t)TopK<KMAX>::slots(K) * kBfThreads);  // dim x kBfTile
     float* qs = tile + (size_t)dim * kBfTile;                          // dim x T
-    // slot q0 + i is query i of [q0, q1), or query qlist[q0 + i] with its
-    // results at its own row
+    // slot q0 + i is query q0 + i, or query qlist[q0 + i] with its results at
+    // row q - row_base
     const int slot = q0 + blockIdx.x * kBfThreads + threadIdx.x;
     const bool active = slot < q1;
     const int q = active && qlist ? __ldg(&qlist[slot]) : slot;
@@ -68,7 +68,7 @@ __global__ void __launch_bounds__(kBfThreads)
         }
     }
     if (active) {
-        const long long orow = qlist ? q : q - q0;
+        const long long orow = qlist ? q - row_base : q - q0;
         tk.emit(oidx + orow, odist + orow, ostride, r2);
     }
 }
@@ -76,12 +76,12 @@ __global__ void __launch_bounds__(kBfThreads)
 template <bool D3, int KMAX>
 cudaError_t launch_bf(const float* pts, int n, int dim, int K, float r2, int q0, int q1, int* oidx,
                       float* odist, long long ostride, int tile, size_t smem, int blocks,
-                      cudaStream_t s, const int* qlist) {
+                      cudaStream_t s, const int* qlist, int row_base) {
     cudaError_t err = cudaFuncSetAttribute(bruteforce_kernel<D3, KMAX>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
     bruteforce_kernel<D3, KMAX><<<blocks, kBfThreads, smem, s>>>(pts, n, dim, K, r2, q0, q1, oidx,
-                                                                 odist, ostride, tile, qlist);
+                                                                 odist, ostride, tile, qlist, row_base);
     return cudaGetLastError();
 }
 
@@ -89,7 +89,7 @@ cudaError_t launch_bf(const float* pts, int n, int dim, int K, float r2, int q0,
 
 cudaError_t launch_bruteforce(const float* pts, int n, int dim, int K, float r2, int q0, int q1,
                               int* oidx, float* odist, long long ostride, cudaStream_t s,
-                              const int* qlist) {
+                              const int* qlist, int row_base) {
     if (q1 <= q0) return cudaSuccess;
     const size_t fixed = (size_t)TopK<128>::slots(K) * 8 * kBfThreads + (size_t)dim * 4 * kBfThreads;
     if (fixed + (size_t)dim * 4 * 8 > kSmemLimit) return cudaErrorInvalidConfiguration;
@@ -98,15 +98,15 @@ cudaError_t launch_bruteforce(const float* pts, int n, int dim, int K, float r2,
     const size_t smem = fixed + (size_t)dim * 4 * tile;
     const int blocks = (q1 - q0 + kBfThreads - 1) / kBfThreads;
     if (dim == 3) {
-        if (K <= 16) return launch_bf<true, 16>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist);
-        if (K <= 32) return launch_bf<true, 32>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist);
-        if (K <= 64) return launch_bf<true, 64>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist);
-        return launch_bf<true, 128>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist);
+        if (K <= 16) return launch_bf<true, 16>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base);
+        if (K <= 32) return launch_bf<true, 32>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base);
+        if (K <= 64) return launch_bf<true, 64>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base);
+        return launch_bf<true, 128>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base);
     }
-    if (K <= 16) return launch_bf<false, 16>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist);
-    if (K <= 32) return launch_bf<false, 32>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist);
-    if (K <= 64) return launch_bf<false, 64>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist);
-    return launch_bf<false, 128>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist);
+    if (K <= 16) return launch_bf<false, 16>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base);
+    if (K <= 32) return launch_bf<false, 32>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base);
+    if (K <= 64) return launch_bf<false, 64>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base);
+    return launch_bf<false, 128>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base);
 }
 
 }  // namespace frnn

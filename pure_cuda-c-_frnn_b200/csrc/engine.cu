@@ -65,6 +65,8 @@ struct frnn_engine {
     DevBuf tmp_idx, tmp_dist, out_idx, out_dist;
     DevBuf in_stage, in_soa, out_rm_idx, out_rm_dist;
     DevBuf tc_box, tc_center, tc_tiles, tc_rows, tc_qa, tc_pb;
+    DevBuf part_ids;          // original query index of each row of a part search
+    int last_part_rows = -1;  // rows of the last part search (-1: last search was whole)
     float* h_box = nullptr;   // pinned, 9 floats
     float* h_tc = nullptr;    // pinned, 512 floats: per-dimension box + flag, then the centre
     int* h_err = nullptr;     // pinned
@@ -209,6 +211,39 @@ __global__ void transpose32_kernel(const unsigned* __restrict__ in, unsigned* __
     }
 }
 
+// out[i] = starts[c] for the largest cell c with starts[c] <= t[i]: a target
+// position rounded down to the first point of its cell (the order of points
+// inside a cell depends on atomic ranks and changes between builds; the cell
+// starts do not).
+__global__ void cell_floor_kernel(const int* __restrict__ starts, long long cells, int t0, int t1,
+                                  int* __restrict__ out) {
+    const int i = threadIdx.x;
+    if (i > 1) return;
+    const int t = i == 0 ? t0 : t1;
+    long long lo = 0, hi = cells;  // starts[0] = 0 <= t; find the last c with starts[c] <= t
+    while (hi - lo > 1) {
+        const long long mid = (lo + hi) / 2;
+        if (starts[mid] <= t) lo = mid;
+        else hi = mid;
+    }
+    out[i] = starts[lo];
+}
+
+cudaError_t launch_cell_floor(const int* starts, long long cells, int t0, int t1, int* out, cudaStream_t s) {
+    cell_floor_kernel<<<1, 32, 0, s>>>(starts, cells, t0, t1, out);
+    return cudaGetLastError();
+}
+
+__global__ void iota_kernel(int* __restrict__ out, int base, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = base + i;
+}
+
+cudaError_t launch_iota(int* out, int base, int n, cudaStream_t s) {
+    iota_kernel<<<(n + 255) / 256, 256, 0, s>>>(out, base, n);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_transpose(const void* in, void* out, int rows, int cols, cudaStream_t s) {
     const long long tiles = (long long)((cols + 31) / 32) * ((rows + 31) / 32);
     dim3 grid((unsigned)tiles), block(32, 8);
@@ -298,8 +333,11 @@ bool make_plan(const float* box, int N, int dim, float radius, GridPlan& P) {
 
 // ---- the search core ------------------------------------------------------------
 
+// Whole search (part == false): results for every query in original order,
+// out[k*N + q].  Part search: the queries at sorted positions [s0, s1) only,
+// row j = sorted position s0 + j of out[k*(s1-s0) + j].
 int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2,
-             const GridPlan& P, int* out_idx, float* out_dist) {
+             const GridPlan& P, int* out_idx, float* out_dist, bool part, int& s0, int& s1) {
     cudaStream_t s = e->stream;
     FRNN_GROW(e, e->counts, (size_t)P.cells * 4);
     FRNN_GROW(e, e->starts, ((size_t)P.cells + 1) * 4);
@@ -328,6 +366,18 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
                               e->epoch, e->err_flag.as<int>(), s),
                "scan launch");
     stage_end(e, ST_SCAN);
+    if (part) {
+        // part boundaries move to cell boundaries, so that parts searched by
+        // separate builds cover every query exactly once
+        int* h = reinterpret_cast<int*>(e->h_tc);
+        FRNN_CHECK(e, launch_cell_floor(e->starts.as<int>(), P.cells, s0, s1, e->scan_ticket.as<int>() + 1, s),
+                   "cell floor launch");
+        FRNN_CHECK(e, cudaMemcpyAsync(h, e->scan_ticket.as<int>() + 1, 2 * sizeof(int), cudaMemcpyDeviceToHost, s),
+                   "part bounds readback");
+        FRNN_CHECK(e, cudaStreamSynchronize(s), "part bounds sync");
+        s0 = s0 >= N ? N : h[0];
+        s1 = s1 >= N ? N : h[1];
+    }
     const bool two_kernel = P.dim == 3 && P.g == 3 && K <= 32;
     if (two_kernel) FRNN_GROW(e, e->inv, (size_t)N * 4);
     stage_begin(e, ST_SCATTER);
@@ -347,19 +397,23 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
         FRNN_GROW(e, e->overflow, (size_t)N * 4);
         FRNN_GROW(e, e->n_overflow, 16);
         FRNN_CHECK(e, cudaMemsetAsync(e->n_overflow.p, 0, 4, s), "memset overflow count");
+        const int q0 = part ? s0 : 0, q1 = part ? s1 : N, rows = q1 - q0;
         stage_begin(e, ST_COLLECT);
         FRNN_CHECK(e, launch_collect_d3(e->rows.as<float>(), e->starts.as<int>(), P, r2, cap,
                                         e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
-                                        e->overflow.as<int>(), e->n_overflow.as<int>(), s),
+                                        e->overflow.as<int>(), e->n_overflow.as<int>(), q0, q1, s),
                    "collect launch");
         stage_end(e, ST_COLLECT);
         stage_begin(e, ST_EMIT);
+        // whole: rows in original order through inv; part: rows in sorted order
         FRNN_CHECK(e, launch_emit_lists(e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
-                                        e->inv.as<int>(), N, K, cap, r2, out_idx, out_dist, s),
+                                        part ? nullptr : e->inv.as<int>(), q0, rows, K, cap, r2,
+                                        out_idx, out_dist, s),
                    "emit launch");
         FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(),
-                                         P, K, r2, 0, N, out_idx, out_dist, N, e->ids.as<int>(), s,
-                                         e->overflow.as<int>(), e->n_overflow.as<int>()),
+                                         P, K, r2, 0, N, out_idx, out_dist, rows,
+                                         part ? nullptr : e->ids.as<int>(), s, e->overflow.as<int>(),
+                                         e->n_overflow.as<int>(), q0),
                    "overflow search launch");
         stage_end(e, ST_EMIT);
         e->launches += 3;
@@ -369,7 +423,14 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
     // scattered stores stay in L2).  Large ones: write in cell order, then
     // unpermute one output row at a time.
     const long long out_bytes = (long long)N * K * 8;
-    if (out_bytes <= e->direct_output_max_bytes) {
+    if (part) {
+        stage_begin(e, ST_SEARCH);
+        FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(), P, K,
+                                         r2, s0, s1, out_idx, out_dist, s1 - s0, nullptr, s),
+                   "grid search launch");
+        stage_end(e, ST_SEARCH);
+        e->launches++;
+    } else if (out_bytes <= e->direct_output_max_bytes) {
         stage_begin(e, ST_SEARCH);
         FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(), P, K,
                                          r2, 0, N, out_idx, out_dist, N, e->ids.as<int>(), s),
@@ -399,8 +460,10 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
 // (and launches nothing that writes results) when the data do not suit the
 // filter -- non-finite coordinates, or a radius whose scaled square is not a
 // finite fp32 -- and the caller runs the SIMT brute force instead.
+// Queries [qb_begin*128, min(N, qb_end*128)) (all of them for a whole search),
+// results to rows q - qb_begin*128 of out[k*rows + row].
 int run_brute_tc(frnn_engine* e, const float* d_pts, int N, int dim, int K, float radius,
-                 int* out_idx, float* out_dist, bool* done) {
+                 int* out_idx, float* out_dist, int qb_begin, int qb_end, bool* done) {
     cudaStream_t s = e->stream;
     *done = false;
     const float r2 = radius * radius;
@@ -459,16 +522,18 @@ int run_brute_tc(frnn_engine* e, const float* d_pts, int N, int dim, int K, floa
                                  e->tc_qa.as<float>(), e->tc_pb.as<float>(), s),
                "prep launch");
     stage_end(e, ST_TC_PREP);
+    const int q0 = qb_begin * 128, q1 = std::min(N, qb_end * 128), rows = q1 - q0;
     FRNN_CHECK(e, cudaMemsetAsync(e->n_overflow.p, 0, 4, s), "memset overflow count");
     stage_begin(e, ST_TC_FILTER);
     FRNN_CHECK(e, launch_tc_filter(e->tc_tiles.as<uint8_t>(), e->tc_qa.as<float>(), e->tc_pb.as<float>(), N,
                                    dim, cap, e->lists.as<int>(), e->list_counts.as<int>(),
-                                   e->overflow.as<int>(), e->n_overflow.as<int>(), e->err_flag.as<int>(), s),
+                                   e->overflow.as<int>(), e->n_overflow.as<int>(), e->err_flag.as<int>(),
+                                   qb_begin, qb_end, s),
                "filter launch");
     stage_end(e, ST_TC_FILTER);
     stage_begin(e, ST_TC_RERANK);
     FRNN_CHECK(e, launch_tc_rerank(e->tc_rows.as<float>(), dim, e->lists.as<int>(), e->list_counts.as<int>(),
-                                   cap, N, K, r2, out_idx, out_dist, s),
+                                   cap, N, K, r2, out_idx, out_dist, q0, q1, s),
                "rerank launch");
     stage_end(e, ST_TC_RERANK);
     e->launches += 3;
@@ -479,8 +544,8 @@ int run_brute_tc(frnn_engine* e, const float* d_pts, int N, int dim, int K, floa
     FRNN_CHECK(e, cudaStreamSynchronize(s), "overflow count sync");
     if (*h_nov > 0) {
         stage_begin(e, ST_BRUTE);
-        FRNN_CHECK(e, launch_bruteforce(d_pts, N, dim, K, r2, 0, *h_nov, out_idx, out_dist, N, s,
-                                        e->overflow.as<int>()),
+        FRNN_CHECK(e, launch_bruteforce(d_pts, N, dim, K, r2, 0, *h_nov, out_idx, out_dist, rows, s,
+                                        e->overflow.as<int>(), q0),
                    "overflow brute force launch");
         stage_end(e, ST_BRUTE);
         e->launches++;
@@ -489,14 +554,23 @@ int run_brute_tc(frnn_engine* e, const float* d_pts, int N, int dim, int K, floa
     return FRNN_OK;
 }
 
+// Whole search (nparts == 0): every query, results out[k*N + q].  Part search
+// (0 <= part < nparts): the part-th of nparts contiguous slices of the path's
+// query order -- cell order on the grid path, input order on brute force,
+// whole 128-query tiles on the tensor-core path -- with row j of
+// out[k*rows + j] belonging to query part_ids[j].  The slices of all parts
+// cover every query exactly once.
 int search_core(frnn_engine* e, const float* d_pts, int N, int dim, int K, float radius,
-                bool blocking) {
+                bool blocking, int part = 0, int nparts = 0) {
     cudaStream_t s = e->stream;
     const float r2 = radius * radius;
+    const bool is_part = nparts > 0;
     FRNN_GROW(e, e->out_idx, (size_t)N * K * 4);
     FRNN_GROW(e, e->out_dist, (size_t)N * K * 4);
     int* out_idx = e->out_idx.as<int>();
     float* out_dist = e->out_dist.as<float>();
+    e->last_N = -1;
+    e->last_part_rows = -1;
 
     for (int i = 0; i < FRNN_STAGES; ++i) e->stage_used[i] = false;
     int path = e->forced_path;
@@ -507,6 +581,21 @@ int search_core(frnn_engine* e, const float* d_pts, int N, int dim, int K, float
         else path = FRNN_PATH_GRID;
     }
     if (path == FRNN_PATH_GRID && dim > 32) path = FRNN_PATH_BRUTE;
+
+    // this call's slice: [s0, s1) of the query order (tiles [qb0, qb1) on the
+    // tensor-core path)
+    const int ntq = (N + 127) / 128;
+    int qb0 = 0, qb1 = ntq, s0 = 0, s1 = N;
+    if (is_part && path == FRNN_PATH_BRUTE_TC) {
+        qb0 = (int)((long long)ntq * part / nparts);
+        qb1 = (int)((long long)ntq * (part + 1) / nparts);
+        s0 = std::min(N, qb0 * 128);
+        s1 = std::min(N, qb1 * 128);
+    } else if (is_part) {
+        s0 = (int)((long long)N * part / nparts);
+        s1 = (int)((long long)N * (part + 1) / nparts);
+    }
+    int rows = s1 - s0;
 
     GridPlan P{};
     bool grid_ok = false;
@@ -530,29 +619,39 @@ int search_core(frnn_engine* e, const float* d_pts, int N, int dim, int K, float
 
     if (path == FRNN_PATH_BRUTE_TC) {
         bool done = false;
-        int st = run_brute_tc(e, d_pts, N, dim, K, radius, out_idx, out_dist, &done);
+        int st = run_brute_tc(e, d_pts, N, dim, K, radius, out_idx, out_dist, qb0, qb1, &done);
         if (st != FRNN_OK) return st;
         if (!done) path = FRNN_PATH_BRUTE;
         e->last_g = 0;
         e->last_cells = 0;
     }
     if (path == FRNN_PATH_GRID) {
-        int st = run_grid(e, d_pts, N, dim, K, r2, P, out_idx, out_dist);
+        int st = run_grid(e, d_pts, N, dim, K, r2, P, out_idx, out_dist, is_part, s0, s1);
         if (st != FRNN_OK) return st;
+        rows = s1 - s0;
         e->last_g = P.g;
         e->last_cells = P.cells;
     } else if (path == FRNN_PATH_BRUTE) {
         stage_begin(e, ST_BRUTE);
-        FRNN_CHECK(e, launch_bruteforce(d_pts, N, dim, K, r2, 0, N, out_idx, out_dist, N, s),
+        FRNN_CHECK(e, launch_bruteforce(d_pts, N, dim, K, r2, s0, s1, out_idx, out_dist, rows, s),
                    "bruteforce launch");
         stage_end(e, ST_BRUTE);
         e->launches++;
         e->last_g = 0;
         e->last_cells = 0;
     }
+    if (is_part) {
+        FRNN_GROW(e, e->part_ids, (size_t)std::max(rows, 1) * 4);
+        if (rows > 0) {
+            if (path == FRNN_PATH_GRID)
+                FRNN_CHECK(e, cudaMemcpyAsync(e->part_ids.p, e->ids.as<int>() + s0, (size_t)rows * 4,
+                                              cudaMemcpyDeviceToDevice, s),
+                           "part ids copy");
+            else
+                FRNN_CHECK(e, launch_iota(e->part_ids.as<int>(), s0, rows, s), "part ids launch");
+        }
+    }
     e->last_path = path;
-    e->last_N = N;
-    e->last_K = K;
     if (blocking) {
         FRNN_CHECK(e, cudaMemcpyAsync(e->h_err, e->err_flag.p, sizeof(int), cudaMemcpyDeviceToHost, s),
                    "error flag readback");
@@ -560,10 +659,15 @@ int search_core(frnn_engine* e, const float* d_pts, int N, int dim, int K, float
         if (*e->h_err != 0) {
             cudaMemsetAsync(e->err_flag.p, 0, sizeof(int), s);
             cudaStreamSynchronize(s);
-            e->last_N = -1;
             return fail(e, FRNN_ERR_TIMEOUT, "a bounded device-side wait gave up");
         }
     }
+    if (is_part) {
+        e->last_part_rows = rows;
+    } else {
+        e->last_N = N;
+    }
+    e->last_K = K;
     return FRNN_OK;
 }
 
@@ -638,7 +742,7 @@ int frnn_destroy(frnn_engine* e) {
                           &e->n_overflow, &e->tmp_idx, &e->tmp_dist, &e->out_idx, &e->out_dist,
                           &e->in_stage, &e->in_soa, &e->out_rm_idx, &e->out_rm_dist,
                           &e->tc_box, &e->tc_center, &e->tc_tiles, &e->tc_rows, &e->tc_qa,
-                          &e->tc_pb};
+                          &e->tc_pb, &e->part_ids};
         for (DevBuf* b : bufs) free_buf(*b);
         for (cudaEvent_t& ev : e->ev)
             if (ev) cudaEventDestroy(ev);
@@ -707,6 +811,27 @@ int frnn_search_gpu(frnn_engine* e, const float* d_points_soa, int N, int dim, i
 int frnn_search_gpu_async(frnn_engine* e, const float* d_points_soa, int N, int dim, int K,
                           float radius, int** d_idxs, float** d_dists) {
     return search_gpu_impl(e, d_points_soa, N, dim, K, radius, d_idxs, d_dists, false);
+}
+
+int frnn_search_gpu_part(frnn_engine* e, const float* d_points_soa, int N, int dim, int K, float radius,
+                         int part, int nparts, int* n_rows, int** d_row_ids, int** d_idxs,
+                         float** d_dists) {
+    int st = check_search_args(e, d_points_soa, N, dim, K, radius);
+    if (st != FRNN_OK) return st;
+    if (nparts < 1 || part < 0 || part >= nparts)
+        return fail(e, FRNN_ERR_INVALID_ARG, "part must be in [0, nparts)");
+    if (!n_rows || !d_row_ids || !d_idxs || !d_dists)
+        return fail(e, FRNN_ERR_INVALID_ARG, "output pointers are null");
+    DeviceGuard g(e->device);
+    st = check_device_ptr(e, d_points_soa);
+    if (st != FRNN_OK) return st;
+    st = search_core(e, d_points_soa, N, dim, K, radius, true, part, nparts);
+    if (st != FRNN_OK) return st;
+    *n_rows = e->last_part_rows;
+    *d_row_ids = e->part_ids.as<int>();
+    *d_idxs = e->out_idx.as<int>();
+    *d_dists = e->out_dist.as<float>();
+    return FRNN_OK;
 }
 
 int frnn_search(frnn_engine* e, const float* h_points_aos, int64_t count, int K, float radius,

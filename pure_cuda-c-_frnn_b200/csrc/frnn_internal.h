@@ -29,25 +29,27 @@ cudaError_t launch_scatter(const float* pts, const GridPlan& P, const int2* cell
 // to row (sq - q0) of the outputs: out[k*ostride + (sq - q0)], or, when
 // scatter_ids is non-null, straight to out[k*ostride + scatter_ids[sq]].
 // qlist (optional): the searched sorted positions are qlist[q0..q1) instead
-// of q0..q1 (then scatter_ids must be given); qcount (optional, device): only
-// the first *qcount of them.
+// of q0..q1; qcount (optional, device): only the first *qcount of them.
+// row_base (>= 0): without scatter_ids, sorted position sq goes to row
+// sq - row_base instead of sq - q0 (for query lists).
 cudaError_t launch_grid_search(const float* rows, const int* ids, const int* starts,
                                const GridPlan& P, int K, float r2, int q0, int q1, int* oidx,
                                float* odist, long long ostride, const int* scatter_ids,
                                cudaStream_t s, const int* qlist = nullptr,
-                               const int* qcount = nullptr);
+                               const int* qcount = nullptr, long long row_base = -1);
 
 // grid_collect.cu -- D = 3 two-kernel search (K <= 32).
-// collect: every in-radius key of sorted query sq goes to lists[sq*cap + j];
-// counts[sq] = number found; queries with more than cap are appended to
-// overflow[0..*n_overflow).
+// collect: for sorted queries sq in [q0, q1), every in-radius key goes to
+// lists[sq*cap + j]; counts[sq] = number found; queries with more than cap are
+// appended to overflow[0..*n_overflow).
 cudaError_t launch_collect_d3(const float* rows, const int* starts, const GridPlan& P, float r2,
                               int cap, unsigned long long* lists, int* counts, int* overflow,
-                              int* n_overflow, cudaStream_t s);
-// emit: for every original query q (sorted position inv[q]) whose count is at
-// most cap, the K smallest keys ascending to out[k*n + q], padded (-1, r2).
-cudaError_t launch_emit_lists(const unsigned long long* lists, const int* counts, const int* inv,
-                              int n, int K, int cap, float r2, int* oidx, float* odist,
+                              int* n_overflow, int q0, int q1, cudaStream_t s);
+// emit: for output rows q < n -- sorted position map[q] (map = inv: rows in
+// original order), or q0 + q without map -- whose count is at most cap, the K
+// smallest keys ascending to out[k*n + q], padded (-1, r2).
+cudaError_t launch_emit_lists(const unsigned long long* lists, const int* counts, const int* map,
+                              int q0, int n, int K, int cap, float r2, int* oidx, float* odist,
                               cudaStream_t s);
 // out[k*N + ids[sq]] = in[k*N + sq]
 cudaError_t launch_unpermute(const int* in_idx, const float* in_dist, const int* ids, int n,
@@ -56,10 +58,10 @@ cudaError_t launch_unpermute(const int* in_idx, const float* in_dist, const int*
 // bruteforce.cu
 // Queries [q0, q1) of the SoA cloud against all n points; results of query q
 // go to out[k*ostride + (q - q0)].  With qlist (device), the queries are
-// qlist[q0..q1) instead and query q's results go to out[k*ostride + q].
+// qlist[q0..q1) instead and query q's results go to out[k*ostride + q - row_base].
 cudaError_t launch_bruteforce(const float* pts, int n, int dim, int K, float r2, int q0, int q1,
                               int* oidx, float* odist, long long ostride, cudaStream_t s,
-                              const int* qlist = nullptr);
+                              const int* qlist = nullptr, int row_base = 0);
 
 // bf_tc.cu -- brute force with a tcgen05 distance filter, 33 <= dim <= 128.
 int tc_kc(int dim);                 // 64-dimension slabs per row (1 or 2)
@@ -69,7 +71,7 @@ int tc_list_cap(int K);             // candidate list capacity per query
 // box[2d], box[2d+1] = min, max of dimension d; *nonfinite |= any NaN/Inf
 cudaError_t launch_tc_box(const float* pts, int n, int dim, float* box, int* nonfinite, cudaStream_t s);
 // fp16 tiles (ceil(n/128) tiles), fp32 rows, threshold terms qa / pb (padded
-// to whole tiles with +inf)
+// to whole tiles with +inf); the query blocks searched are [qb_begin, qb_end)
 cudaError_t launch_tc_prep(const float* pts, int n, int dim, const float* center, float scale,
                            float one_minus_alpha, float eta_c, float rc, uint8_t* tiles, float* rows32,
                            float* qa, float* pb, cudaStream_t s);
@@ -77,9 +79,11 @@ cudaError_t launch_tc_prep(const float* pts, int n, int dim, const float* center
 // lists[q*cap ..]; queries with more go to overflow[0..*n_overflow)
 cudaError_t launch_tc_filter(const uint8_t* tiles, const float* qa, const float* pb, int n, int dim,
                              int cap, int* lists, int* counts, int* overflow, int* n_overflow, int* err,
-                             cudaStream_t s);
-// exact results for every query with counts[q] <= cap
+                             int qb_begin, int qb_end, cudaStream_t s);
+// exact results for the queries q in [q0, q1) with counts[q] <= cap, to row
+// q - q0 of out[k*(q1-q0) + row]
 cudaError_t launch_tc_rerank(const float* rows32, int dim, const int* lists, const int* counts, int cap,
-                             int n, int K, float r2, int* oidx, float* odist, cudaStream_t s);
+                             int n, int K, float r2, int* oidx, float* odist, int q0, int q1,
+                             cudaStream_t s);
 
 }  // namespace frnn

@@ -35,9 +35,9 @@ __global__ void __launch_bounds__(256)
     collect_d3_kernel(const float4* __restrict__ rows, const int* __restrict__ starts, GridPlan P,
                       float r2, int cap, unsigned long long* __restrict__ lists,
                       int* __restrict__ counts, int* __restrict__ overflow,
-                      int* __restrict__ n_overflow) {
-    const int sq = blockIdx.x * blockDim.x + threadIdx.x;
-    if (sq >= P.n) return;
+                      int* __restrict__ n_overflow, int q0, int q1) {
+    const int sq = q0 + blockIdx.x * blockDim.x + threadIdx.x;
+    if (sq >= q1) return;
     const float4 q = __ldg(&rows[sq]);
     const float cs = P.cell, eps = P.eps;
     const int gx = cell_coord(q.x, P.origin[0], P.inv_cell, P.res[0]);
@@ -130,11 +130,13 @@ __device__ __forceinline__ void top_keys(const unsigned long long* list, int cnt
 template <int KN>
 __global__ void __launch_bounds__(128)
     emit_lists_kernel(const unsigned long long* __restrict__ lists, const int* __restrict__ counts,
-                      const int* __restrict__ inv, int n, int K, int cap, float r2,
+                      const int* __restrict__ map, int q0, int n, int K, int cap, float r2,
                       int* __restrict__ oidx, float* __restrict__ odist) {
+    // output row q: sorted position map[q] (original order), or q0 + q (a
+    // slice of the sorted order)
     const int q = blockIdx.x * blockDim.x + threadIdx.x;
     if (q >= n) return;
-    const int sq = __ldg(&inv[q]);
+    const int sq = map ? __ldg(&map[q]) : q0 + q;
     const int cnt = __ldg(&counts[sq]);
     if (cnt > cap) return;  // searched by the overflow pass
     unsigned long long a[KN];
@@ -153,22 +155,24 @@ __global__ void __launch_bounds__(128)
 
 cudaError_t launch_collect_d3(const float* rows, const int* starts, const GridPlan& P, float r2,
                               int cap, unsigned long long* lists, int* counts, int* overflow,
-                              int* n_overflow, cudaStream_t s) {
-    collect_d3_kernel<<<(P.n + 255) / 256, 256, 0, s>>>(reinterpret_cast<const float4*>(rows),
-                                                        starts, P, r2, cap, lists, counts, overflow,
-                                                        n_overflow);
+                              int* n_overflow, int q0, int q1, cudaStream_t s) {
+    if (q1 <= q0) return cudaSuccess;
+    collect_d3_kernel<<<(q1 - q0 + 255) / 256, 256, 0, s>>>(reinterpret_cast<const float4*>(rows),
+                                                            starts, P, r2, cap, lists, counts,
+                                                            overflow, n_overflow, q0, q1);
     return cudaGetLastError();
 }
 
-cudaError_t launch_emit_lists(const unsigned long long* lists, const int* counts, const int* inv,
-                              int n, int K, int cap, float r2, int* oidx, float* odist,
+cudaError_t launch_emit_lists(const unsigned long long* lists, const int* counts, const int* map,
+                              int q0, int n, int K, int cap, float r2, int* oidx, float* odist,
                               cudaStream_t s) {
     if (K > 32) return cudaErrorInvalidValue;  // the register top-K holds at most 32 keys
+    if (n <= 0) return cudaSuccess;
     if (K <= 16)
-        emit_lists_kernel<16><<<(n + 127) / 128, 128, 0, s>>>(lists, counts, inv, n, K, cap, r2,
+        emit_lists_kernel<16><<<(n + 127) / 128, 128, 0, s>>>(lists, counts, map, q0, n, K, cap, r2,
                                                               oidx, odist);
     else
-        emit_lists_kernel<32><<<(n + 127) / 128, 128, 0, s>>>(lists, counts, inv, n, K, cap, r2,
+        emit_lists_kernel<32><<<(n + 127) / 128, 128, 0, s>>>(lists, counts, map, q0, n, K, cap, r2,
                                                               oidx, odist);
     return cudaGetLastError();
 }

@@ -228,7 +228,7 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
                      const int* __restrict__ starts, GridPlan P, int K, float r2, int q0, int q1,
                      int* __restrict__ oidx, float* __restrict__ odist, long long ostride,
                      const int* __restrict__ scatter_ids, const int* __restrict__ qlist,
-                     const int* __restrict__ qcount) {
+                     const int* __restrict__ qcount, long long row_base) {
     extern __shared__ __align__(16) unsigned char smem[];
     if (qcount) q1 = min(q1, q0 + __ldg(qcount));  // list length known only on the device
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -388,7 +388,7 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
                 const int n = gcnt[g];
                 const int sq = qlist ? __ldg(&qlist[base + g0 + g]) : base + g0 + g;
                 const long long orow =
-                    scatter_ids ? (long long)__ldg(&scatter_ids[sq]) : (long long)(sq - q0);
+                    scatter_ids ? (long long)__ldg(&scatter_ids[sq]) : (long long)sq - row_base;
                 const unsigned long long* list = lists + (size_t)g * cap;
                 if (n <= 32 && K <= 32) {
                     emit_rank32(list, n, K, lane, r2, oidx + orow, odist + orow, ostride);

@@ -55,19 +55,33 @@ cudaError_t set_smem(Kern k, size_t smem) {
     return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
 }
 
+struct CoopArgs {
+    const float* rows;
+    const int* ids;
+    const int* starts;
+    GridPlan P;
+    int K;
+    float r2;
+    int q0, q1;
+    int* oidx;
+    float* odist;
+    long long ostride;
+    const int* scatter_ids;
+    const int* qlist;
+    const int* qcount;
+    long long row_base;
+};
+
 template <int NV, int G, bool D3>
-cudaError_t launch_coop(const float* rows, const int* ids, const int* starts, const GridPlan& P,
-                        int K, float r2, int q0, int q1, int* oidx, float* odist,
-                        long long ostride, const int* scatter_ids, cudaStream_t s,
-                        const int* qlist, const int* qcount) {
-    const size_t smem = (size_t)coop::kWarps * coop::warp_bytes<NV, D3>(K);
+cudaError_t launch_coop(const CoopArgs& a, cudaStream_t s) {
+    const size_t smem = (size_t)coop::kWarps * coop::warp_bytes<NV, D3>(a.K);
     cudaError_t err = set_smem(coop::grid_coop_kernel<NV, G, D3>, smem);
     if (err != cudaSuccess) return err;
     const int per_block = coop::kWarps * 32;
-    const int blocks = (q1 - q0 + per_block - 1) / per_block;
+    const int blocks = (a.q1 - a.q0 + per_block - 1) / per_block;
     coop::grid_coop_kernel<NV, G, D3><<<blocks, coop::kWarps * 32, smem, s>>>(
-        reinterpret_cast<const float4*>(rows), ids, starts, P, K, r2, q0, q1, oidx, odist, ostride,
-        scatter_ids, qlist, qcount);
+        reinterpret_cast<const float4*>(a.rows), a.ids, a.starts, a.P, a.K, a.r2, a.q0, a.q1, a.oidx,
+        a.odist, a.ostride, a.scatter_ids, a.qlist, a.qcount, a.row_base);
     return cudaGetLastError();
 }
 
@@ -76,21 +90,23 @@ cudaError_t launch_coop(const float* rows, const int* ids, const int* starts, co
 cudaError_t launch_grid_search(const float* rows, const int* ids, const int* starts,
                                const GridPlan& P, int K, float r2, int q0, int q1, int* oidx,
                                float* odist, long long ostride, const int* scatter_ids,
-                               cudaStream_t s, const int* qlist, const int* qcount) {
+                               cudaStream_t s, const int* qlist, const int* qcount,
+                               long long row_base) {
     if (q1 <= q0) return cudaSuccess;
-    if (P.dim == 3 && P.g == 3)
-        return launch_coop<1, 3, true>(rows, ids, starts, P, K, r2, q0, q1, oidx, odist, ostride, scatter_ids, s, qlist, qcount);
+    const CoopArgs a{rows, ids, starts, P, K, r2, q0, q1, oidx, odist, ostride, scatter_ids,
+                     qlist, qcount, row_base < 0 ? (long long)q0 : row_base};
+    if (P.dim == 3 && P.g == 3) return launch_coop<1, 3, true>(a, s);
     // (row float4s, grid axes) pairs the planner produces: G = min(D, 4)
     const int nv = P.row / 4;
-    if (nv == 1 && P.g == 1) return launch_coop<1, 1, false>(rows, ids, starts, P, K, r2, q0, q1, oidx, odist, ostride, scatter_ids, s, qlist, qcount);
-    if (nv == 1 && P.g == 2) return launch_coop<1, 2, false>(rows, ids, starts, P, K, r2, q0, q1, oidx, odist, ostride, scatter_ids, s, qlist, qcount);
-    if (nv == 1 && P.g == 4) return launch_coop<1, 4, false>(rows, ids, starts, P, K, r2, q0, q1, oidx, odist, ostride, scatter_ids, s, qlist, qcount);
+    if (nv == 1 && P.g == 1) return launch_coop<1, 1, false>(a, s);
+    if (nv == 1 && P.g == 2) return launch_coop<1, 2, false>(a, s);
+    if (nv == 1 && P.g == 4) return launch_coop<1, 4, false>(a, s);
     if (P.g != 4) return cudaErrorInvalidValue;
     switch (nv) {
-        case 2: return launch_coop<2, 4, false>(rows, ids, starts, P, K, r2, q0, q1, oidx, odist, ostride, scatter_ids, s, qlist, qcount);
-        case 3: return launch_coop<3, 4, false>(rows, ids, starts, P, K, r2, q0, q1, oidx, odist, ostride, scatter_ids, s, qlist, qcount);
-        case 4: return launch_coop<4, 4, false>(rows, ids, starts, P, K, r2, q0, q1, oidx, odist, ostride, scatter_ids, s, qlist, qcount);
-        case 8: return launch_coop<8, 4, false>(rows, ids, starts, P, K, r2, q0, q1, oidx, odist, ostride, scatter_ids, s, qlist, qcount);
+        case 2: return launch_coop<2, 4, false>(a, s);
+        case 3: return launch_coop<3, 4, false>(a, s);
+        case 4: return launch_coop<4, 4, false>(a, s);
+        case 8: return launch_coop<8, 4, false>(a, s);
         default: return cudaErrorInvalidValue;
     }
 }

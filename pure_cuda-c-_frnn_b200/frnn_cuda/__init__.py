@@ -61,6 +61,8 @@ def load_library() -> ctypes.CDLL:
         "frnn_destroy": (I, [P]),
         "frnn_search_gpu": (I, [P, P, I, I, I, F, ctypes.POINTER(P), ctypes.POINTER(P)]),
         "frnn_search_gpu_async": (I, [P, P, I, I, I, F, ctypes.POINTER(P), ctypes.POINTER(P)]),
+        "frnn_search_gpu_part": (I, [P, P, I, I, I, F, I, I, ctypes.POINTER(I), ctypes.POINTER(P),
+                                     ctypes.POINTER(P), ctypes.POINTER(P)]),
         "frnn_search": (I, [P, P, L, I, F, P, P]),
         "frnn_search_host_soa": (I, [P, P, I, I, I, F, P, P]),
         "frnn_get_results": (I, [P, I, I, P, P]),
@@ -209,6 +211,21 @@ class FRNNEngine:
                                              ctypes.byref(pd))
         self._check(st, "search_gpu_async")
         return int(pi.value), int(pd.value)
+
+    def search_gpu_part(self, dev_ptr: int, N: int, dim: int, K: int, radius: float, part: int,
+                        nparts: int):
+        """One of ``nparts`` slices of the search (frnn_search_gpu_part): returns
+        ``(n_rows, row_ids_ptr, idx_ptr, dist_ptr)``; row j of the SoA results
+        (``[k*n_rows + j]``) is query ``row_ids[j]``.  Device pointers are
+        engine-owned and valid until the next call."""
+        n = ctypes.c_int()
+        pr, pi, pd = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+        self._check(self._lib.frnn_search_gpu_part(self._eng, ctypes.c_void_p(int(dev_ptr)), int(N),
+                                                   int(dim), int(K), float(radius), int(part),
+                                                   int(nparts), ctypes.byref(n), ctypes.byref(pr),
+                                                   ctypes.byref(pi), ctypes.byref(pd)),
+                    "search_gpu_part")
+        return n.value, pr.value or 0, pi.value or 0, pd.value or 0
 
     def set_stream(self, stream: int) -> None:
         self._check(self._lib.frnn_set_stream(self._eng, ctypes.c_void_p(int(stream))), "set_stream")
