@@ -10,9 +10,14 @@ calibrated for 24 mean in-radius neighbours, self-query.  One step = one full
 search (grid build + neighbour search + results in the reference layout) of
 one cloud.
 
-Multi-GPU (one process per GPU under torchrun): every rank searches its own
-independent cloud (seed 1234+rank, same radius); no data-path collective, so
-scaling is weak.  ``value`` = all ranks' queries / max-over-ranks step time.
+Multi-GPU (one process per GPU under torchrun), ``--mode weak`` (default):
+every rank searches its own cloud -- replica ``rank`` of the configuration's
+distribution (same mixture centres or basis, its own sample of N points, same
+radius) -- with no data-path collective, so scaling is weak.  ``value`` = all
+ranks' queries / max-over-ranks step time.  ``--mode strong``: one cloud,
+queries sharded over the ranks (frnn_cuda.sharded: NCCL broadcast of the
+cloud, one part search per rank, gather to rank 0, all inside every step);
+``value`` = N / max-over-ranks step time.
 
 Timing: W untimed warm-up steps, then exactly K timed steps, bracketed by a
 barrier and torch.cuda.synchronize; each step is timed with CUDA events on the
@@ -174,7 +179,8 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
     c = datagen.config(a.config)
     N, D, K, r = c.N, c.D, c.K, c.radius
     strong = a.mode == "strong" and world > 1
-    pts = datagen.generate(c.kind, N, D, seed=datagen.SEED + (0 if strong else rank))
+    # weak: rank r searches replica r (its own sample of the same distribution)
+    pts = datagen.generate(c.kind, N, D, seed=datagen.SEED, replica=0 if strong else rank)
     soa = datagen.soa(pts)
     x = torch.from_numpy(soa).to(dev)
     eng = frnn_cuda.FRNNEngine(max_points=N, device=dev)
@@ -309,7 +315,7 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
         "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_max,
         "higher_is_better": True, "scaling": "strong" if strong else "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic (seeded generator, rank r uses seed 1234+r)",
+        "dtype": "f32", "data": "synthetic (seeded generator, seed 1234; rank r draws replica r of the same distribution)",
         "config": {"workload": c.name, "describe": c.describe, "N": N, "D": D, "K": K,
                    "radius": r, "queries_per_gpu": N // world if strong else N,
                    "l2": "flushed before every timed step",

@@ -39,45 +39,52 @@ class Config:
     describe: str
 
 
-def _uniform(rng, N, D):
-    return rng.random((N, D), dtype=np.float64).astype(np.float32)
+def _uniform(rng, srng, N, D):
+    return srng.random((N, D), dtype=np.float64).astype(np.float32)
 
 
-def _mixture(rng, N, D, comps=64, sigma=0.02):
+def _mixture(rng, srng, N, D, comps=64, sigma=0.02):
     centres = rng.random((comps, D))
-    labels = rng.integers(0, comps, N)
-    pts = centres[labels] + sigma * rng.standard_normal((N, D))
+    labels = srng.integers(0, comps, N)
+    pts = centres[labels] + sigma * srng.standard_normal((N, D))
     return pts.astype(np.float32)
 
 
-def _lowrank_minmax(rng, N, D, rank, noise=0.01):
+def _lowrank_minmax(rng, srng, N, D, rank, noise=0.01):
     a, _ = np.linalg.qr(rng.standard_normal((D, rank)))    # D x rank, orthonormal columns
-    z = rng.standard_normal((N, rank))
-    pts = z @ a.T + noise * rng.standard_normal((N, D))
+    z = srng.standard_normal((N, rank))
+    pts = z @ a.T + noise * srng.standard_normal((N, D))
     mn = pts.min(axis=0, keepdims=True)
     mx = pts.max(axis=0, keepdims=True)
     return ((pts - mn) / np.maximum(mx - mn, 1e-12)).astype(np.float32)
 
 
-def _sphere(rng, N, D):
-    x = rng.standard_normal((N, D))
+def _sphere(rng, srng, N, D):
+    x = srng.standard_normal((N, D))
     x /= np.linalg.norm(x, axis=1, keepdims=True)
     return x.astype(np.float32)
 
 
-def generate(kind: str, N: int, D: int, seed: int = SEED) -> np.ndarray:
-    """Row-major (N, D) float32 cloud of the given kind."""
+def generate(kind: str, N: int, D: int, seed: int = SEED, replica: int = 0) -> np.ndarray:
+    """Row-major (N, D) float32 cloud of the given kind.
+
+    ``replica`` > 0 draws another sample of N points from the same
+    distribution (the same mixture centres or low-rank basis, from ``seed``)
+    with its own random stream; replica 0 is the configuration's cloud itself.
+    The weak-scaling bench gives rank r replica r, so every rank's search has
+    the same expected cost."""
     rng = np.random.default_rng(seed)
+    srng = rng if replica == 0 else np.random.default_rng([seed, replica])
     if kind == "uniform":
-        return _uniform(rng, N, D)
+        return _uniform(rng, srng, N, D)
     if kind == "mixture":
-        return _mixture(rng, N, D)
+        return _mixture(rng, srng, N, D)
     if kind == "lowrank4":
-        return _lowrank_minmax(rng, N, D, 4)
+        return _lowrank_minmax(rng, srng, N, D, 4)
     if kind == "lowrank6":
-        return _lowrank_minmax(rng, N, D, 6)
+        return _lowrank_minmax(rng, srng, N, D, 6)
     if kind == "sphere":
-        return _sphere(rng, N, D)
+        return _sphere(rng, srng, N, D)
     raise ValueError(f"unknown cloud kind {kind!r}")
 
 
