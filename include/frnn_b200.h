@@ -146,9 +146,24 @@ enum frnn_option {
     /* Result sets up to this many bytes (N*K*8) are written straight to
      * original query order from the search kernel; larger ones are written in
      * cell order and unpermuted one output row at a time.  Default 48 MiB. */
-    FRNN_OPT_DIRECT_OUTPUT_MAX_BYTES = 1
+    FRNN_OPT_DIRECT_OUTPUT_MAX_BYTES = 1,
+    /* Grid axes for D > 4 (FRNN_GRID_AXES_*).  The reference grids the first
+     * coordinates (python_interface/frnn_engine.cu:64-102); the engine may
+     * instead grid the data's principal axes (up to 6), which finds the same
+     * neighbours with fewer candidates on correlated data.  Default AUTO: a
+     * sampled estimate of candidates per query decides. */
+    FRNN_OPT_GRID_AXES = 2
+};
+enum frnn_grid_axes {
+    FRNN_GRID_AXES_AUTO = 0,       /* cheaper of the two by the estimate    */
+    FRNN_GRID_AXES_LEADING = 1,    /* leading min(D, 4) coordinates only     */
+    FRNN_GRID_AXES_PRINCIPAL = 2   /* principal axes whenever D > 4          */
 };
 int frnn_set_option(frnn_engine* e, int option, int64_t value);
+
+/* Axes of the last search's grid: FRNN_GRID_AXES_LEADING (also for searches
+ * that used no grid) or FRNN_GRID_AXES_PRINCIPAL.  No reference counterpart. */
+int frnn_last_grid_axes(const frnn_engine* e, int* axes);
 
 /* Per-stage device timing.  When enabled, each search records CUDA events
  * around its stages on the engine stream; frnn_last_stage_times writes the

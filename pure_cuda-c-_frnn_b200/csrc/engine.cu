@@ -66,6 +66,12 @@ struct frnn_engine {
     DevBuf in_stage, in_soa, out_rm_idx, out_rm_dist;
     DevBuf tc_box, tc_center, tc_tiles, tc_rows, tc_qa, tc_pb;
     DevBuf part_ids;          // original query index of each row of a part search
+    // principal-axis grid: moments, axes, projected coordinates, estimate
+    DevBuf pca_partial, pca_moments, pca_mu, pca_pm, proj_box_partial, proj_ticket, proj_out;
+    DevBuf proj_u, proj_s, pca_smp, pca_h, pca_counts;
+    void* h_pca = nullptr;    // pinned, 32 KiB
+    int grid_axes_mode = 0;   // FRNN_OPT_GRID_AXES
+    int last_principal = 0;   // the last grid was on principal axes
     int last_part_rows = -1;  // rows of the last part search (-1: last search was whole)
     float* h_box = nullptr;   // pinned, 9 floats
     float* h_tc = nullptr;    // pinned, 512 floats: per-dimension box + flag, then the centre
@@ -265,8 +271,10 @@ int row_floats(int dim) {
 
 // Build the grid plan from the box.  Returns false when a grid is useless
 // (every query would scan nearly everything) or cannot be formed.
-bool make_plan(const float* box, int N, int dim, float radius, GridPlan& P) {
-    const int g = grid_axes_for(dim);
+// Plan a grid on g axes whose bounding box is box[2d], box[2d+1]; `extra` is
+// an absolute allowance added to the cell edge (the rounding bound of
+// projected coordinates; 0 for the data's own coordinates).
+bool make_plan_axes(const float* box, int g, int N, int dim, float radius, double extra, GridPlan& P) {
     double ext_max = 0.0, mag = 0.0;
     for (int d = 0; d < g; ++d) {
         double lo = box[2 * d], hi = box[2 * d + 1];
@@ -277,7 +285,7 @@ bool make_plan(const float* box, int N, int dim, float radius, GridPlan& P) {
     // the query's 3^g shell despite float rounding of the cell assignment
     // (|error| of (x-origin)*inv_cell is a few ulps of the cell index).
     const double u = 1.0 / 16777216.0;
-    double cell = (double)radius * (1.0 + 1e-5 + 8.0 * u * (ext_max / radius + 2.0));
+    double cell = (double)radius * (1.0 + 1e-5 + 8.0 * u * (ext_max / radius + 2.0)) + extra;
     // Dense cell table budget: 32 cells per point (12 bytes of build traffic
     // per cell); sparse clouds such as Gaussian mixtures leave most cells
     // empty, and coarser cells would multiply the candidates of every query.
@@ -331,13 +339,187 @@ bool make_plan(const float* box, int N, int dim, float radius, GridPlan& P) {
     return true;
 }
 
+bool make_plan(const float* box, int N, int dim, float radius, GridPlan& P) {
+    return make_plan_axes(box, grid_axes_for(dim), N, dim, radius, 0.0, P);
+}
+
+// Eigen-decomposition of a symmetric n x n matrix (row-major, destroyed) by
+// cyclic Jacobi rotations in double: w[i] eigenvalues, column i of V (row-major
+// n x n) the eigenvector of w[i].
+void jacobi_eigen(int n, double* A, double* V, double* w) {
+    for (int i = 0; i < n * n; ++i) V[i] = 0.0;
+    for (int i = 0; i < n; ++i) V[i * n + i] = 1.0;
+    for (int sweep = 0; sweep < 100; ++sweep) {
+        double off = 0.0, diag = 0.0;
+        for (int p = 0; p < n; ++p) {
+            diag += A[p * n + p] * A[p * n + p];
+            for (int q = p + 1; q < n; ++q) off += A[p * n + q] * A[p * n + q];
+        }
+        if (off <= 1e-30 * diag || off == 0.0) break;
+        for (int p = 0; p < n; ++p) {
+            for (int q = p + 1; q < n; ++q) {
+                const double apq = A[p * n + q];
+                if (apq == 0.0) continue;
+                const double theta = (A[q * n + q] - A[p * n + p]) / (2.0 * apq);
+                const double t = (theta >= 0 ? 1.0 : -1.0) / (std::fabs(theta) + std::sqrt(theta * theta + 1.0));
+                const double c = 1.0 / std::sqrt(t * t + 1.0), sn = t * c;
+                for (int k = 0; k < n; ++k) {
+                    const double akp = A[k * n + p], akq = A[k * n + q];
+                    A[k * n + p] = c * akp - sn * akq;
+                    A[k * n + q] = sn * akp + c * akq;
+                }
+                for (int k = 0; k < n; ++k) {
+                    const double apk = A[p * n + k], aqk = A[q * n + k];
+                    A[p * n + k] = c * apk - sn * aqk;
+                    A[q * n + k] = sn * apk + c * aqk;
+                }
+                for (int k = 0; k < n; ++k) {
+                    const double vkp = V[k * n + p], vkq = V[k * n + q];
+                    V[k * n + p] = c * vkp - sn * vkq;
+                    V[k * n + q] = sn * vkp + c * vkq;
+                }
+            }
+        }
+    }
+    for (int i = 0; i < n; ++i) w[i] = A[i * n + i];
+}
+
+// ---- principal axes ---------------------------------------------------------------
+
+// For 5 <= D <= 32 on the grid path: the sample moments give the principal
+// axes; every point is projected on the top min(D, 6) of them; a sampled
+// shell count estimates the candidates per query of the leading-coordinate
+// grid (`first`, if valid) and of principal-axis grids on g = 2..6 axes; the
+// cheapest is kept.  On return *principal says whether P now holds a
+// principal-axis plan (the projected coordinates are then in e->proj_u).
+int plan_principal(frnn_engine* e, const float* d_pts, int N, int dim, float radius, bool first_ok,
+                   GridPlan& P, bool* principal) {
+    cudaStream_t s = e->stream;
+    *principal = false;
+    const int slots = pca_slots(dim);
+    const int samples = std::min(N, 65536);
+    const int mblocks = std::max(1, std::min(64, samples / 256));
+    FRNN_GROW(e, e->pca_partial, (size_t)mblocks * slots * 8);
+    FRNN_GROW(e, e->pca_moments, (size_t)(slots + dim) * 8);
+    FRNN_CHECK(e, launch_pca_moments(d_pts, N, dim, samples, mblocks, e->pca_partial.as<double>(),
+                                     e->pca_moments.as<double>(), s),
+               "moments launch");
+    double* hm = static_cast<double*>(e->h_pca);
+    FRNN_CHECK(e, cudaMemcpyAsync(hm, e->pca_moments.p, (size_t)(slots + dim) * 8, cudaMemcpyDeviceToHost, s),
+               "moments readback");
+    FRNN_CHECK(e, cudaStreamSynchronize(s), "moments sync");
+    e->launches += 2;
+
+    // covariance of the sample (about x0, then about the mean)
+    double mean[kMaxPcaDim], C[kMaxPcaDim * kMaxPcaDim], V[kMaxPcaDim * kMaxPcaDim], w[kMaxPcaDim];
+    for (int d = 0; d < dim; ++d) mean[d] = hm[d] / samples;
+    int k = dim;
+    for (int a = 0; a < dim; ++a)
+        for (int b = a; b < dim; ++b, ++k) {
+            const double c = hm[k] / samples - mean[a] * mean[b];
+            C[a * dim + b] = c;
+            C[b * dim + a] = c;
+        }
+    jacobi_eigen(dim, C, V, w);
+    int order[kMaxPcaDim];
+    for (int i = 0; i < dim; ++i) order[i] = i;
+    std::stable_sort(order, order + dim, [&](int x, int y) { return w[x] > w[y]; });
+    const int axes = std::min(dim, kMaxGridAxes);
+    // host staging after the moments: mu (dim floats), pm (axes x dim floats)
+    float* hmu = reinterpret_cast<float*>(static_cast<char*>(e->h_pca) + 8192);
+    float* hpm = hmu + kMaxPcaDim;
+    for (int d = 0; d < dim; ++d) hmu[d] = (float)(hm[slots + d] + mean[d]);  // x0 + sample mean
+    for (int a = 0; a < axes; ++a) {
+        const int c = order[a];
+        int big = 0;
+        for (int d = 1; d < dim; ++d)
+            if (std::fabs(V[d * dim + c]) > std::fabs(V[big * dim + c])) big = d;
+        const double sg = V[big * dim + c] < 0 ? -1.0 : 1.0;
+        for (int d = 0; d < dim; ++d) hpm[a * dim + d] = (float)(sg * V[d * dim + c]);
+    }
+    FRNN_GROW(e, e->pca_mu, (size_t)kMaxPcaDim * 4);
+    FRNN_GROW(e, e->pca_pm, (size_t)kMaxGridAxes * kMaxPcaDim * 4);
+    FRNN_CHECK(e, cudaMemcpyAsync(e->pca_mu.p, hmu, (size_t)dim * 4, cudaMemcpyHostToDevice, s), "mu upload");
+    FRNN_CHECK(e, cudaMemcpyAsync(e->pca_pm.p, hpm, (size_t)axes * dim * 4, cudaMemcpyHostToDevice, s),
+               "axes upload");
+
+    // projection and its bounding box
+    const int pblocks = std::min(bbox_blocks(N, e->sms), kBoxMaxBlocks);
+    const int pslots = pca_project_slots();
+    FRNN_GROW(e, e->proj_u, (size_t)N * kProjStride * 4);
+    FRNN_GROW(e, e->proj_box_partial, (size_t)pblocks * pslots * 4);
+    if (!e->proj_ticket.p) {
+        FRNN_GROW(e, e->proj_ticket, 16);
+        FRNN_CHECK(e, cudaMemsetAsync(e->proj_ticket.p, 0, 16, s), "memset ticket");
+    }
+    FRNN_GROW(e, e->proj_out, 64 * 4);
+    FRNN_CHECK(e, launch_pca_project(d_pts, N, dim, axes, e->pca_mu.as<float>(), e->pca_pm.as<float>(),
+                                     e->proj_u.as<float>(), e->proj_box_partial.as<float>(),
+                                     e->proj_ticket.as<unsigned>(), e->proj_out.as<float>(), pblocks, s),
+               "project launch");
+    float* hbox = hpm + kMaxGridAxes * kMaxPcaDim;
+    FRNN_CHECK(e, cudaMemcpyAsync(hbox, e->proj_out.p, (size_t)pslots * 4, cudaMemcpyDeviceToHost, s),
+               "projected box readback");
+    FRNN_CHECK(e, cudaStreamSynchronize(s), "projected box sync");
+    e->launches++;
+    if (hbox[pslots - 1] != 0.0f) return fail(e, FRNN_ERR_INVALID_ARG, "points contain NaN or Inf coordinates");
+
+    // Rounding bound of a projected coordinate: (D + 2) 2^-24 |x - mu|; a pair
+    // within r differs by at most r (1 + 2^-20) + 2 delta on every axis.
+    const double nmax = std::sqrt(std::max(0.0, (double)hbox[pslots - 2])) * 1.001;
+    const double extra = 2.0 * (dim + 2) * std::ldexp(nmax, -24) + (double)radius * std::ldexp(1.0, -20);
+    GridPlan cand[kMaxGridAxes + 1];
+    bool ok[kMaxGridAxes + 1] = {};
+    for (int g = 2; g <= axes; ++g) ok[g] = make_plan_axes(hbox, g, N, dim, radius, extra, cand[g]);
+
+    // sampled shell counts
+    const int m = std::min(N, 16384), nq = std::min(m, 256);
+    float* hh = hbox + 16;
+    for (int t = 0; t < 16; ++t) hh[t] = -1.0f;
+    if (first_ok) hh[P.g - 1] = 1.5f * P.cell;
+    for (int g = 2; g <= axes; ++g)
+        if (ok[g]) hh[8 + g - 1] = 1.5f * cand[g].cell;
+    FRNN_GROW(e, e->pca_h, 16 * 4);
+    FRNN_GROW(e, e->pca_smp, (size_t)m * 16 * 4);
+    FRNN_GROW(e, e->pca_counts, (size_t)nq * 16 * 4);
+    FRNN_CHECK(e, cudaMemcpyAsync(e->pca_h.p, hh, 16 * 4, cudaMemcpyHostToDevice, s), "estimate upload");
+    FRNN_CHECK(e, launch_pca_estimate(d_pts, N, dim, e->proj_u.as<float>(), m, nq, e->pca_smp.as<float>(),
+                                      e->pca_h.as<float>(), e->pca_counts.as<int>(), s),
+               "estimate launch");
+    int* hc = reinterpret_cast<int*>(static_cast<char*>(e->h_pca) + 16384);
+    FRNN_CHECK(e, cudaMemcpyAsync(hc, e->pca_counts.p, (size_t)nq * 16 * 4, cudaMemcpyDeviceToHost, s),
+               "estimate readback");
+    FRNN_CHECK(e, cudaStreamSynchronize(s), "estimate sync");
+    e->launches += 2;
+    // cost per query: candidates plus a fixed charge per shell row (3^(g-1))
+    auto cost = [&](int col, int g) {
+        double c = 0.0;
+        for (int q = 0; q < nq; ++q) c += hc[q * 16 + col];
+        return c / nq * ((double)N / m) + 8.0 * std::pow(3.0, g - 1);
+    };
+    int best_g = 0;
+    double best = INFINITY;
+    for (int g = 2; g <= axes; ++g)
+        if (ok[g] && cost(8 + g - 1, g) < best) best = cost(8 + g - 1, g), best_g = g;
+    if (best_g == 0) return FRNN_OK;
+    // principal axes replace the leading coordinates (the reference's grid)
+    // only when clearly cheaper, unless they are forced
+    if (e->grid_axes_mode != FRNN_GRID_AXES_PRINCIPAL && first_ok && !(1.25 * best < cost(P.g - 1, P.g)))
+        return FRNN_OK;
+    P = cand[best_g];
+    *principal = true;
+    return FRNN_OK;
+}
+
 // ---- the search core ------------------------------------------------------------
 
 // Whole search (part == false): results for every query in original order,
 // out[k*N + q].  Part search: the queries at sorted positions [s0, s1) only,
 // row j = sorted position s0 + j of out[k*(s1-s0) + j].
+// proj: the points' projected coordinates when P is a principal-axis grid.
 int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2,
-             const GridPlan& P, int* out_idx, float* out_dist, bool part, int& s0, int& s1) {
+             const GridPlan& P, int* out_idx, float* out_dist, bool part, int& s0, int& s1,
+             const float* proj) {
     cudaStream_t s = e->stream;
     FRNN_GROW(e, e->counts, (size_t)P.cells * 4);
     FRNN_GROW(e, e->starts, ((size_t)P.cells + 1) * 4);
@@ -350,7 +532,7 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
     FRNN_CHECK(e, cudaMemsetAsync(e->counts.p, 0, (size_t)P.cells * 4, s), "memset counts");
     FRNN_CHECK(e, cudaMemsetAsync(e->scan_ticket.p, 0, 4, s), "memset scan ticket");
     stage_begin(e, ST_HASH);
-    FRNN_CHECK(e, launch_hash_count(d_pts, P, e->counts.as<int>(), e->cellrank.as<int2>(), s),
+    FRNN_CHECK(e, launch_hash_count(d_pts, P, e->counts.as<int>(), e->cellrank.as<int2>(), s, proj),
                "hash_count launch");
     stage_end(e, ST_HASH);
     e->launches++;
@@ -380,10 +562,16 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
     }
     const bool two_kernel = P.dim == 3 && P.g == 3 && K <= 32;
     if (two_kernel) FRNN_GROW(e, e->inv, (size_t)N * 4);
+    const float* proj_s = nullptr;
+    if (proj) {
+        FRNN_GROW(e, e->proj_s, (size_t)N * kProjStride * 4);
+        proj_s = e->proj_s.as<float>();
+    }
     stage_begin(e, ST_SCATTER);
     FRNN_CHECK(e, launch_scatter(d_pts, P, e->cellrank.as<int2>(), e->starts.as<int>(),
                                  e->rows.as<float>(), e->ids.as<int>(), s,
-                                 two_kernel ? e->inv.as<int>() : nullptr),
+                                 two_kernel ? e->inv.as<int>() : nullptr, proj,
+                                 proj ? e->proj_s.as<float>() : nullptr),
                "scatter launch");
     stage_end(e, ST_SCATTER);
     e->launches += 2;
@@ -426,14 +614,16 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
     if (part) {
         stage_begin(e, ST_SEARCH);
         FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(), P, K,
-                                         r2, s0, s1, out_idx, out_dist, s1 - s0, nullptr, s),
+                                         r2, s0, s1, out_idx, out_dist, s1 - s0, nullptr, s, nullptr,
+                                         nullptr, -1, proj_s),
                    "grid search launch");
         stage_end(e, ST_SEARCH);
         e->launches++;
     } else if (out_bytes <= e->direct_output_max_bytes) {
         stage_begin(e, ST_SEARCH);
         FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(), P, K,
-                                         r2, 0, N, out_idx, out_dist, N, e->ids.as<int>(), s),
+                                         r2, 0, N, out_idx, out_dist, N, e->ids.as<int>(), s, nullptr,
+                                         nullptr, -1, proj_s),
                    "grid search launch");
         stage_end(e, ST_SEARCH);
         e->launches++;
@@ -443,7 +633,7 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
         stage_begin(e, ST_SEARCH);
         FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(), P, K,
                                          r2, 0, N, e->tmp_idx.as<int>(), e->tmp_dist.as<float>(), N,
-                                         nullptr, s),
+                                         nullptr, s, nullptr, nullptr, -1, proj_s),
                    "grid search launch");
         stage_end(e, ST_SEARCH);
         stage_begin(e, ST_UNPERMUTE);
@@ -598,7 +788,7 @@ int search_core(frnn_engine* e, const float* d_pts, int N, int dim, int K, float
     int rows = s1 - s0;
 
     GridPlan P{};
-    bool grid_ok = false;
+    bool grid_ok = false, principal = false;
     if (path == FRNN_PATH_GRID) {
         const int g = grid_axes_for(dim);
         const int blocks = std::min(bbox_blocks(N, e->sms), kBoxMaxBlocks);
@@ -614,6 +804,11 @@ int search_core(frnn_engine* e, const float* d_pts, int N, int dim, int K, float
         if (e->h_box[8] != 0.0f)
             return fail(e, FRNN_ERR_INVALID_ARG, "points contain NaN or Inf coordinates");
         grid_ok = make_plan(e->h_box, N, dim, radius, P);
+        if (dim > 4 && dim <= kMaxPcaDim && e->grid_axes_mode != FRNN_GRID_AXES_LEADING) {
+            int st = plan_principal(e, d_pts, N, dim, radius, grid_ok, P, &principal);
+            if (st != FRNN_OK) return st;
+            grid_ok |= principal;
+        }
         if (!grid_ok) path = FRNN_PATH_BRUTE;
     }
 
@@ -626,7 +821,8 @@ int search_core(frnn_engine* e, const float* d_pts, int N, int dim, int K, float
         e->last_cells = 0;
     }
     if (path == FRNN_PATH_GRID) {
-        int st = run_grid(e, d_pts, N, dim, K, r2, P, out_idx, out_dist, is_part, s0, s1);
+        int st = run_grid(e, d_pts, N, dim, K, r2, P, out_idx, out_dist, is_part, s0, s1,
+                          principal ? e->proj_u.as<float>() : nullptr);
         if (st != FRNN_OK) return st;
         rows = s1 - s0;
         e->last_g = P.g;
@@ -652,6 +848,7 @@ int search_core(frnn_engine* e, const float* d_pts, int N, int dim, int K, float
         }
     }
     e->last_path = path;
+    e->last_principal = path == FRNN_PATH_GRID && principal;
     if (blocking) {
         FRNN_CHECK(e, cudaMemcpyAsync(e->h_err, e->err_flag.p, sizeof(int), cudaMemcpyDeviceToHost, s),
                    "error flag readback");
@@ -721,7 +918,8 @@ int frnn_create(int max_points, int device, frnn_engine** out) {
     if (cudaMemset(e->box_ticket.p, 0, e->box_ticket.bytes) != cudaSuccess ||
         cudaMemset(e->err_flag.p, 0, e->err_flag.bytes) != cudaSuccess ||
         cudaMallocHost(&e->h_box, 64) != cudaSuccess || cudaMallocHost(&e->h_err, 64) != cudaSuccess ||
-        cudaMallocHost(&e->h_tc, 512 * sizeof(float)) != cudaSuccess) {
+        cudaMallocHost(&e->h_tc, 512 * sizeof(float)) != cudaSuccess ||
+        cudaMallocHost(&e->h_pca, 32768) != cudaSuccess) {
         cudaGetLastError();
         frnn_destroy(e);
         return FRNN_ERR_OOM;
@@ -742,13 +940,16 @@ int frnn_destroy(frnn_engine* e) {
                           &e->n_overflow, &e->tmp_idx, &e->tmp_dist, &e->out_idx, &e->out_dist,
                           &e->in_stage, &e->in_soa, &e->out_rm_idx, &e->out_rm_dist,
                           &e->tc_box, &e->tc_center, &e->tc_tiles, &e->tc_rows, &e->tc_qa,
-                          &e->tc_pb, &e->part_ids};
+                          &e->tc_pb, &e->part_ids, &e->pca_partial, &e->pca_moments, &e->pca_mu,
+                          &e->pca_pm, &e->proj_box_partial, &e->proj_ticket, &e->proj_out,
+                          &e->proj_u, &e->proj_s, &e->pca_smp, &e->pca_h, &e->pca_counts};
         for (DevBuf* b : bufs) free_buf(*b);
         for (cudaEvent_t& ev : e->ev)
             if (ev) cudaEventDestroy(ev);
         if (e->h_box) cudaFreeHost(e->h_box);
         if (e->h_err) cudaFreeHost(e->h_err);
         if (e->h_tc) cudaFreeHost(e->h_tc);
+        if (e->h_pca) cudaFreeHost(e->h_pca);
     }
     delete e;
     return FRNN_OK;
@@ -768,12 +969,23 @@ int frnn_set_path(frnn_engine* e, int path) {
     return FRNN_OK;
 }
 
+int frnn_last_grid_axes(const frnn_engine* e, int* axes) {
+    if (!e || !axes) return FRNN_ERR_INVALID_ARG;
+    *axes = e->last_principal ? FRNN_GRID_AXES_PRINCIPAL : FRNN_GRID_AXES_LEADING;
+    return FRNN_OK;
+}
+
 int frnn_set_option(frnn_engine* e, int option, int64_t value) {
     if (!e) return FRNN_ERR_INVALID_ARG;
     switch (option) {
         case FRNN_OPT_DIRECT_OUTPUT_MAX_BYTES:
             if (value < 0) return fail(e, FRNN_ERR_INVALID_ARG, "value must be >= 0");
             e->direct_output_max_bytes = value;
+            return FRNN_OK;
+        case FRNN_OPT_GRID_AXES:
+            if (value < FRNN_GRID_AXES_AUTO || value > FRNN_GRID_AXES_PRINCIPAL)
+                return fail(e, FRNN_ERR_INVALID_ARG, "grid axes must be AUTO, LEADING or PRINCIPAL");
+            e->grid_axes_mode = (int)value;
             return FRNN_OK;
         default:
             return fail(e, FRNN_ERR_INVALID_ARG, "unknown option");

@@ -8,14 +8,20 @@ namespace frnn {
 
 constexpr int kMaxK = 128;           // grid.h:59 MAX_K_CAPACITY
 constexpr int kMaxD = 128;           // grid.h:60 MAX_DIM_SUPPORTED
-constexpr int kMaxGridAxes = 4;
+// Grid axes: the leading coordinates (at most 4, as the reference's first-d
+// grid) or the data's principal axes (at most 6).
+constexpr int kMaxGridAxes = 6;
+// Floats per point of projected (principal-axis) coordinates: 6 used, padded.
+constexpr int kProjStride = 8;
+// Largest D for which principal axes are computed (the grid path's limit).
+constexpr int kMaxPcaDim = 32;
 
 // Grid description computed on the host from the data's bounding box.
 // Replaces the reference's GridParams (grid.h:38-52): per-axis resolution and
 // origin instead of a fixed [0,1] domain, and axis 0 varying fastest in the
 // dense cell index so the three x-neighbours of a cell are one contiguous span.
 struct GridPlan {
-    int g;                       // grid axes = leading coordinates used for cells
+    int g;                       // grid axes (leading coordinates, or principal axes)
     int n;                       // number of points
     int dim;                     // full dimension D
     int row;                     // floats per sorted row (D rounded up to 4)

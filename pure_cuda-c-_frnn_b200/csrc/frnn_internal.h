@@ -13,16 +13,20 @@ namespace frnn {
 int bbox_blocks(int n, int sms);
 cudaError_t launch_bbox(const float* pts, int n, int g, float* partial, unsigned int* ticket,
                         float* out, int blocks, cudaStream_t s);
+// proj (optional): the grid axes are proj[i*kProjStride + d] instead of the
+// leading coordinates of pts
 cudaError_t launch_hash_count(const float* pts, const GridPlan& P, int* counts, int2* cellrank,
-                              cudaStream_t s);
+                              cudaStream_t s, const float* proj = nullptr);
 long long scan_tiles(long long cells);
 cudaError_t launch_scan(const int* counts, int* starts, long long cells,
                         unsigned long long* status, int* ticket, unsigned epoch, int* err,
                         cudaStream_t s);
-// inv (optional): inv[original index] = sorted position
+// inv (optional): inv[original index] = sorted position; proj (optional, D > 3):
+// projected coordinates copied to proj_sorted in cell order
 cudaError_t launch_scatter(const float* pts, const GridPlan& P, const int2* cellrank,
                            const int* starts, float* rows, int* ids, cudaStream_t s,
-                           int* inv = nullptr);
+                           int* inv = nullptr, const float* proj = nullptr,
+                           float* proj_sorted = nullptr);
 
 // grid_search.cu
 // Searches sorted query positions [q0, q1).  Results for sorted position sq go
@@ -31,12 +35,14 @@ cudaError_t launch_scatter(const float* pts, const GridPlan& P, const int2* cell
 // qlist (optional): the searched sorted positions are qlist[q0..q1) instead
 // of q0..q1; qcount (optional, device): only the first *qcount of them.
 // row_base (>= 0): without scatter_ids, sorted position sq goes to row
-// sq - row_base instead of sq - q0 (for query lists).
+// sq - row_base instead of sq - q0 (for query lists).  proj (optional): the
+// grid axes are the sorted projected coordinates proj[sq*kProjStride + d].
 cudaError_t launch_grid_search(const float* rows, const int* ids, const int* starts,
                                const GridPlan& P, int K, float r2, int q0, int q1, int* oidx,
                                float* odist, long long ostride, const int* scatter_ids,
                                cudaStream_t s, const int* qlist = nullptr,
-                               const int* qcount = nullptr, long long row_base = -1);
+                               const int* qcount = nullptr, long long row_base = -1,
+                               const float* proj = nullptr);
 
 // grid_collect.cu -- D = 3 two-kernel search (K <= 32).
 // collect: for sorted queries sq in [q0, q1), every in-radius key goes to
@@ -62,6 +68,27 @@ cudaError_t launch_unpermute(const int* in_idx, const float* in_dist, const int*
 cudaError_t launch_bruteforce(const float* pts, int n, int dim, int K, float r2, int q0, int q1,
                               int* oidx, float* odist, long long ostride, cudaStream_t s,
                               const int* qlist = nullptr, int row_base = 0);
+
+// grid_pca.cu -- principal axes for the grid (5 <= dim <= 32).
+int pca_slots(int dim);            // dim sums + dim*(dim+1)/2 products
+// sums over `samples` strided points of x - x0 and the upper triangle of
+// (x - x0)(x - x0)^T (x0 = point 0) into out[pca_slots(dim)] (double), then
+// x0 itself in out[pca_slots(dim) + d], via blocks x slots partials;
+// deterministic
+cudaError_t launch_pca_moments(const float* pts, int n, int dim, int samples, int blocks, double* partial,
+                               double* out, cudaStream_t s);
+int pca_project_slots();           // 2 * kMaxGridAxes + 2
+// proj[i*kProjStride + k] = sum_d pm[k*dim + d] (x_d - mu_d), k < axes;
+// out[2k], out[2k+1] = min, max of axis k; out[2*kMaxGridAxes] = max |x - mu|^2;
+// out[2*kMaxGridAxes + 1] = 1 if any coordinate is NaN or Inf
+cudaError_t launch_pca_project(const float* pts, int n, int dim, int axes, const float* mu, const float* pm,
+                               float* proj, float* partial, unsigned int* ticket, float* out, int blocks,
+                               cudaStream_t s);
+// counts[q*16 + b*8 + g-1] for nq sample queries over m sample points: points
+// within h[b*8 + g-1] of the query on each of the first g axes of basis b
+// (0 leading coordinates, 1 principal axes); smp is m x 16 floats of scratch
+cudaError_t launch_pca_estimate(const float* pts, int n, int dim, const float* proj, int m, int nq, float* smp,
+                                const float* h, int* counts, cudaStream_t s);
 
 // bf_tc.cu -- brute force with a tcgen05 distance filter, 33 <= dim <= 128.
 int tc_kc(int dim);                 // 64-dimension slabs per row (1 or 2)

@@ -23,7 +23,8 @@ namespace frnn {
 namespace {
 
 constexpr int kBoxThreads = 256;
-constexpr int kBoxSlots = 2 * kMaxGridAxes + 1;  // (min,max) per axis + non-finite flag
+constexpr int kBoxAxes = 4;                     // leading coordinates boxed (g <= 4)
+constexpr int kBoxSlots = 2 * kBoxAxes + 1;     // (min,max) per axis + non-finite flag
 
 // Per-axis min/max of the grid axes.  Each block writes a partial; the last
 // block to finish (atomic ticket) folds the partials into out[0..8]:
@@ -32,13 +33,13 @@ __global__ void __launch_bounds__(kBoxThreads) bbox_kernel(const float* __restri
                                                            float* __restrict__ partial,
                                                            unsigned int* __restrict__ ticket,
                                                            float* __restrict__ out) {
-    float mn[kMaxGridAxes], mx[kMaxGridAxes];
+    float mn[kBoxAxes], mx[kBoxAxes];
     bool bad = false;
 #pragma unroll
-    for (int d = 0; d < kMaxGridAxes; ++d) { mn[d] = INFINITY; mx[d] = -INFINITY; }
+    for (int d = 0; d < kBoxAxes; ++d) { mn[d] = INFINITY; mx[d] = -INFINITY; }
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
 #pragma unroll
-        for (int d = 0; d < kMaxGridAxes; ++d) {
+        for (int d = 0; d < kBoxAxes; ++d) {
             if (d < g) {
                 float v = __ldg(&pts[(long long)d * n + i]);
                 bad |= !isfinite(v);
@@ -51,7 +52,7 @@ __global__ void __launch_bounds__(kBoxThreads) bbox_kernel(const float* __restri
     __shared__ bool last;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
-    for (int d = 0; d < kMaxGridAxes; ++d) {
+    for (int d = 0; d < kBoxAxes; ++d) {
         float a = mn[d], b = mx[d];
         for (int o = 16; o > 0; o >>= 1) {
             a = fminf(a, __shfl_xor_sync(0xffffffffu, a, o));
@@ -91,16 +92,19 @@ __global__ void __launch_bounds__(kBoxThreads) bbox_kernel(const float* __restri
 
 // ---- histogram: cell of each point and its slot within the cell ------------
 
+// The grid axes are the leading coordinates of the SoA input, or, with proj,
+// the projected coordinates proj[i*kProjStride + d] (principal axes).
 __global__ void __launch_bounds__(256) hash_count_kernel(const float* __restrict__ pts, GridPlan P,
                                                          int* __restrict__ counts,
-                                                         int2* __restrict__ cellrank) {
+                                                         int2* __restrict__ cellrank,
+                                                         const float* __restrict__ proj) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= P.n) return;
     long long c = 0;
 #pragma unroll
     for (int d = 0; d < kMaxGridAxes; ++d) {
         if (d < P.g) {
-            float v = __ldg(&pts[(long long)d * P.n + i]);
+            float v = proj ? __ldg(&proj[(long long)i * kProjStride + d]) : __ldg(&pts[(long long)d * P.n + i]);
             c += (long long)cell_coord(v, P.origin[d], P.inv_cell, P.res[d]) * P.stride[d];
         }
     }
@@ -258,12 +262,19 @@ __global__ void __launch_bounds__(256) scatter_rows_kernel(const float* __restri
                                                            const int* __restrict__ starts,
                                                            float* __restrict__ rows,
                                                            int* __restrict__ ids,
-                                                           int* __restrict__ inv) {
+                                                           int* __restrict__ inv,
+                                                           const float4* __restrict__ proj,
+                                                           float4* __restrict__ proj_sorted) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     int2 cr = cellrank[i];
     long long pos = __ldg(&starts[cr.x]) + cr.y;
     if (pos < 0 || pos >= n) return;  // only reachable if the scan gave up (error flag set)
+    if (proj) {
+#pragma unroll
+        for (int v = 0; v < kProjStride / 4; ++v)
+            proj_sorted[pos * (kProjStride / 4) + v] = __ldg(&proj[(long long)i * (kProjStride / 4) + v]);
+    }
     float4* dst = reinterpret_cast<float4*>(rows + pos * row);
     for (int d = 0; d < row; d += 4) {
         float4 t;
@@ -293,8 +304,8 @@ int bbox_blocks(int n, int sms) {
 }
 
 cudaError_t launch_hash_count(const float* pts, const GridPlan& P, int* counts, int2* cellrank,
-                              cudaStream_t s) {
-    hash_count_kernel<<<(P.n + 255) / 256, 256, 0, s>>>(pts, P, counts, cellrank);
+                              cudaStream_t s, const float* proj) {
+    hash_count_kernel<<<(P.n + 255) / 256, 256, 0, s>>>(pts, P, counts, cellrank, proj);
     return cudaGetLastError();
 }
 
@@ -310,13 +321,16 @@ cudaError_t launch_scan(const int* counts, int* starts, long long cells,
 }
 
 cudaError_t launch_scatter(const float* pts, const GridPlan& P, const int2* cellrank,
-                           const int* starts, float* rows, int* ids, cudaStream_t s, int* inv) {
+                           const int* starts, float* rows, int* ids, cudaStream_t s, int* inv,
+                           const float* proj, float* proj_sorted) {
+    if (proj && P.dim == 3) return cudaErrorInvalidValue;  // principal axes are for D > 4
     if (P.dim == 3)
         scatter_d3_kernel<<<(P.n + 255) / 256, 256, 0, s>>>(pts, P.n, cellrank, starts,
                                                             reinterpret_cast<float4*>(rows), ids, inv);
     else
-        scatter_rows_kernel<<<(P.n + 255) / 256, 256, 0, s>>>(pts, P.n, P.dim, P.row, cellrank,
-                                                              starts, rows, ids, inv);
+        scatter_rows_kernel<<<(P.n + 255) / 256, 256, 0, s>>>(
+            pts, P.n, P.dim, P.row, cellrank, starts, rows, ids, inv,
+            reinterpret_cast<const float4*>(proj), reinterpret_cast<float4*>(proj_sorted));
     return cudaGetLastError();
 }
 

@@ -228,7 +228,8 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
                      const int* __restrict__ starts, GridPlan P, int K, float r2, int q0, int q1,
                      int* __restrict__ oidx, float* __restrict__ odist, long long ostride,
                      const int* __restrict__ scatter_ids, const int* __restrict__ qlist,
-                     const int* __restrict__ qcount, long long row_base) {
+                     const int* __restrict__ qcount, long long row_base,
+                     const float4* __restrict__ proj) {
     extern __shared__ __align__(16) unsigned char smem[];
     if (qcount) q1 = min(q1, q0 + __ldg(qcount));  // list length known only on the device
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -248,15 +249,17 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
     float4 myq[NV];
     long long mycell = -1;
     int mygc[G];
+    const long long mysq = lane < nq ? (qlist ? __ldg(&qlist[base + lane]) : base + lane) : 0;
 #pragma unroll
     for (int v = 0; v < NV; ++v)
-        myq[v] = lane < nq ? __ldg(&rows[(long long)(qlist ? __ldg(&qlist[base + lane]) : base + lane) * NV + v])
-                           : make_float4(0, 0, 0, 0);
+        myq[v] = lane < nq ? __ldg(&rows[mysq * NV + v]) : make_float4(0, 0, 0, 0);
     {
+        // grid coordinates: the leading coordinates of the row, or the
+        // query's projected (principal-axis) coordinates
         long long c = 0;
 #pragma unroll
         for (int a = 0; a < G; ++a) {
-            const float4& f = myq[a >> 2];
+            const float4 f = proj ? __ldg(&proj[mysq * (kProjStride / 4) + (a >> 2)]) : myq[a >> 2];
             const float x = (a & 3) == 0 ? f.x : (a & 3) == 1 ? f.y : (a & 3) == 2 ? f.z : f.w;
             mygc[a] = cell_coord(x, P.origin[a], P.inv_cell, P.res[a]);
             c += (long long)mygc[a] * P.stride[a];
@@ -264,7 +267,7 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
         if (lane < nq) mycell = c;
     }
 
-    constexpr int kRows = Shell<G>::rows;  // rows of the shell (axis 0 merged)
+    constexpr int kRows = Shell<G>::rows;  // rows of the shell (axis 0 merged), 32 per pass
     int g0 = 0;
     while (g0 < nq) {
         // ---- the group: lanes g0.. with the same cell, at most kGroup -------
@@ -297,10 +300,11 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
 #pragma unroll
         for (int a = 0; a < G; ++a) gc[a] = __shfl_sync(0xffffffffu, mygc[a], g0);
 
+        for (int sb = 0; sb < kRows; sb += 32) {
         // ---- candidate spans: one shell row per lane -----------------------
         int sstart = 0, slen = 0;
-        if (lane < kRows) {
-            int t = lane;
+        if (sb + lane < kRows) {
+            int t = sb + lane;
             long long rb = 0;
             bool ok = true;
 #pragma unroll
@@ -379,6 +383,7 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
                 }
             }
         }
+        }  // shell rows, 32 per pass
         __syncwarp();
 
         // ---- emit the group ------------------------------------------------

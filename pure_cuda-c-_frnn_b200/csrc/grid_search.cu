@@ -70,6 +70,7 @@ struct CoopArgs {
     const int* qlist;
     const int* qcount;
     long long row_base;
+    const float* proj;
 };
 
 template <int NV, int G, bool D3>
@@ -81,7 +82,8 @@ cudaError_t launch_coop(const CoopArgs& a, cudaStream_t s) {
     const int blocks = (a.q1 - a.q0 + per_block - 1) / per_block;
     coop::grid_coop_kernel<NV, G, D3><<<blocks, coop::kWarps * 32, smem, s>>>(
         reinterpret_cast<const float4*>(a.rows), a.ids, a.starts, a.P, a.K, a.r2, a.q0, a.q1, a.oidx,
-        a.odist, a.ostride, a.scatter_ids, a.qlist, a.qcount, a.row_base);
+        a.odist, a.ostride, a.scatter_ids, a.qlist, a.qcount, a.row_base,
+        reinterpret_cast<const float4*>(a.proj));
     return cudaGetLastError();
 }
 
@@ -91,24 +93,38 @@ cudaError_t launch_grid_search(const float* rows, const int* ids, const int* sta
                                const GridPlan& P, int K, float r2, int q0, int q1, int* oidx,
                                float* odist, long long ostride, const int* scatter_ids,
                                cudaStream_t s, const int* qlist, const int* qcount,
-                               long long row_base) {
+                               long long row_base, const float* proj) {
     if (q1 <= q0) return cudaSuccess;
     const CoopArgs a{rows, ids, starts, P, K, r2, q0, q1, oidx, odist, ostride, scatter_ids,
-                     qlist, qcount, row_base < 0 ? (long long)q0 : row_base};
-    if (P.dim == 3 && P.g == 3) return launch_coop<1, 3, true>(a, s);
-    // (row float4s, grid axes) pairs the planner produces: G = min(D, 4)
+                     qlist, qcount, row_base < 0 ? (long long)q0 : row_base, proj};
+    if (P.dim == 3 && P.g == 3 && !proj) return launch_coop<1, 3, true>(a, s);
+    // (row float4s, grid axes) pairs the planner produces: leading coordinates
+    // G = min(D, 4); principal axes (D > 4) G in 2..6
     const int nv = P.row / 4;
-    if (nv == 1 && P.g == 1) return launch_coop<1, 1, false>(a, s);
-    if (nv == 1 && P.g == 2) return launch_coop<1, 2, false>(a, s);
-    if (nv == 1 && P.g == 4) return launch_coop<1, 4, false>(a, s);
-    if (P.g != 4) return cudaErrorInvalidValue;
+    if (nv == 1 && !proj) {
+        if (P.g == 1) return launch_coop<1, 1, false>(a, s);
+        if (P.g == 2) return launch_coop<1, 2, false>(a, s);
+        if (P.g == 4) return launch_coop<1, 4, false>(a, s);
+        return cudaErrorInvalidValue;
+    }
+#define FRNN_COOP_G(NV)                                                   \
+    switch (P.g) {                                                        \
+        case 2: return launch_coop<NV, 2, false>(a, s);                   \
+        case 3: return launch_coop<NV, 3, false>(a, s);                   \
+        case 4: return launch_coop<NV, 4, false>(a, s);                   \
+        case 5: return launch_coop<NV, 5, false>(a, s);                   \
+        case 6: return launch_coop<NV, 6, false>(a, s);                   \
+        default: return cudaErrorInvalidValue;                            \
+    }
+    if (!proj && P.g != 4) return cudaErrorInvalidValue;
     switch (nv) {
-        case 2: return launch_coop<2, 4, false>(a, s);
-        case 3: return launch_coop<3, 4, false>(a, s);
-        case 4: return launch_coop<4, 4, false>(a, s);
-        case 8: return launch_coop<8, 4, false>(a, s);
+        case 2: FRNN_COOP_G(2)
+        case 3: FRNN_COOP_G(3)
+        case 4: FRNN_COOP_G(4)
+        case 8: FRNN_COOP_G(8)
         default: return cudaErrorInvalidValue;
     }
+#undef FRNN_COOP_G
 }
 
 cudaError_t launch_unpermute(const int* in_idx, const float* in_dist, const int* ids, int n,

@@ -75,6 +75,7 @@ def load_library() -> ctypes.CDLL:
         "frnn_last_stage_times": (I, [P, ctypes.POINTER(F), I]),
         "frnn_launch_count": (I, [P, ctypes.POINTER(L)]),
         "frnn_set_option": (I, [P, I, L]),
+        "frnn_last_grid_axes": (I, [P, ctypes.POINTER(I)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -236,6 +237,8 @@ class FRNNEngine:
         self._check(self._lib.frnn_set_path(self._eng, int(path)), "set_path")
 
     OPT_DIRECT_OUTPUT_MAX_BYTES = 1
+    OPT_GRID_AXES = 2
+    GRID_AXES_AUTO, GRID_AXES_LEADING, GRID_AXES_PRINCIPAL = 0, 1, 2
 
     def set_option(self, option: int, value: int) -> None:
         self._check(self._lib.frnn_set_option(self._eng, int(option), int(value)), "set_option")
@@ -262,4 +265,7 @@ class FRNNEngine:
         p, g, c = ctypes.c_int(), ctypes.c_int(), ctypes.c_int64()
         self._check(self._lib.frnn_last_plan(self._eng, ctypes.byref(p), ctypes.byref(g),
                                              ctypes.byref(c)), "last_plan")
-        return {"path": PATH_NAMES.get(p.value, str(p.value)), "grid_dims": g.value, "cells": c.value}
+        ax = ctypes.c_int()
+        self._check(self._lib.frnn_last_grid_axes(self._eng, ctypes.byref(ax)), "last_plan")
+        return {"path": PATH_NAMES.get(p.value, str(p.value)), "grid_dims": g.value, "cells": c.value,
+                "axes": "principal" if ax.value == self.GRID_AXES_PRINCIPAL else "leading"}
