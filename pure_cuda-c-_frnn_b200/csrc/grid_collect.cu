@@ -17,10 +17,9 @@
 //   emit     one thread per query in ORIGINAL order (inv[] maps it to its cell
 //            order position), so the K result rows are written coalesced and no
 //            unpermute pass is needed.  Each thread keeps its K smallest keys in
-//            registers: the first KN keys are sorted by a bitonic network, the
-//            rest are folded in 16 at a time (sort the batch, keep the KN
-//            smallest of both with a half-cleaner, re-sort with a bitonic
-//            merge).  No shuffles and no warp-wide serialisation.
+//            registers, folding its list in 16 at a time (sort the batch, keep
+//            the KN smallest of both with a half-cleaner, re-sort with a
+//            bitonic merge).  No shuffles and no warp-wide serialisation.
 //
 // A query with more than `cap` in-radius candidates is listed as overflowing
 // and searched again by the warp-cooperative kernel (grid_coop.cuh), which
@@ -103,15 +102,17 @@ __device__ __forceinline__ void bitonic_merge(unsigned long long (&a)[N]) {
     }
 }
 
-// The KN smallest keys of list[0..cnt) ascending in registers: sort the first
-// KN, then fold the remainder in batches of 16.
+// The KN smallest keys of list[0..cnt) ascending in registers, folded in
+// batches of 16 into an all-~0 start.  One sort-16 / merge-KN body for every
+// batch keeps the kernel's code small enough for the instruction cache (a
+// separate KN-wide first sort doubled it, and nearly every warp has a lane
+// with more than KN keys, so every warp ran both bodies).
 template <int KN>
 __device__ __forceinline__ void top_keys(const unsigned long long* list, int cnt,
                                          unsigned long long (&a)[KN]) {
 #pragma unroll
-    for (int i = 0; i < KN; ++i) a[i] = i < cnt ? list[i] : ~0ull;
-    bitonic_sort<KN>(a);
-    for (int base = KN; base < cnt; base += 16) {
+    for (int i = 0; i < KN; ++i) a[i] = ~0ull;
+    for (int base = 0; base < cnt; base += 16) {
         unsigned long long b[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) b[i] = base + i < cnt ? list[base + i] : ~0ull;
@@ -127,14 +128,39 @@ __device__ __forceinline__ void top_keys(const unsigned long long* list, int cnt
     }
 }
 
+constexpr int kEmitClasses = 10;  // 16-key batch counts 0..8 (lists up to 128), and overflow
+
 template <int KN>
 __global__ void __launch_bounds__(128)
     emit_lists_kernel(const unsigned long long* __restrict__ lists, const int* __restrict__ counts,
                       const int* __restrict__ map, int q0, int n, int K, int cap, float r2,
                       int* __restrict__ oidx, float* __restrict__ odist) {
     // output row q: sorted position map[q] (original order), or q0 + q (a
-    // slice of the sorted order)
-    const int q = blockIdx.x * blockDim.x + threadIdx.x;
+    // slice of the sorted order).  The block's 128 rows are dealt to its
+    // threads by the number of 16-key batches their lists need, so a warp's
+    // lanes do similar work (a warp runs as many batches as its longest
+    // list); the stores stay within the block's 128 consecutive rows.
+    __shared__ int hist[kEmitClasses + 1];
+    __shared__ short order[128];
+    const int t = threadIdx.x;
+    const int q_own = blockIdx.x * 128 + t;
+    int cls = 0, cnt_own = 0, sq_own = 0;
+    if (q_own < n) {
+        sq_own = map ? __ldg(&map[q_own]) : q0 + q_own;
+        cnt_own = __ldg(&counts[sq_own]);
+        cls = cnt_own > cap ? 0 : min((cnt_own + 15) >> 4, kEmitClasses - 1);
+    }
+    if (t <= kEmitClasses) hist[t] = 0;
+    __syncthreads();
+    const int rank = atomicAdd(&hist[cls + 1], 1);
+    __syncthreads();
+    if (t == 0)
+        for (int c = 1; c <= kEmitClasses; ++c) hist[c] += hist[c - 1];
+    __syncthreads();
+    order[hist[cls] + rank] = (short)t;
+    __syncthreads();
+    const int src = order[t];
+    const int q = blockIdx.x * 128 + src;
     if (q >= n) return;
     const int sq = map ? __ldg(&map[q]) : q0 + q;
     const int cnt = __ldg(&counts[sq]);
