@@ -116,6 +116,17 @@ int frnn_last_plan(const frnn_engine* e, int* path, int* grid_dims, int64_t* cel
 int frnn_search_gpu_async(frnn_engine* e, const float* d_points_soa, int N, int dim, int K,
                           float radius, int** d_idxs, float** d_dists);
 
+/* Search a separate query set: every one of the M queries (SoA
+ * d_queries_soa[d*M + q]) against the N points (SoA, N <= max_points), the
+ * same acceptance, ordering, padding and arithmetic as frnn_search_gpu, with
+ * no self-match (a query is not one of the points).  Results SoA
+ * [k*M + q] in engine-owned buffers; frnn_get_results(e, M, K) copies them.
+ * No counterpart in the reference engine, which self-queries only
+ * (python_interface/frnn_engine.cu:195-250); its kernels assume the query set
+ * is the point set (find_nbrs.cu:197,325,338).  Blocking. */
+int frnn_search_gpu_queries(frnn_engine* e, const float* d_points_soa, int N, const float* d_queries_soa, int M,
+                            int dim, int K, float radius, int** d_idxs, float** d_dists);
+
 /* Part of a search, for sharding the queries of one cloud over several
  * engines (one per GPU).  No counterpart in the reference, whose engine only
  * searches whole clouds; SURVEY-style query sharding splits the reference's

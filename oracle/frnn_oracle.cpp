@@ -234,9 +234,16 @@ void grid_visit(const CpuGrid& G, const float* q, F&& f) {
 
 // Core exact search over a query subset.  `include` (may be null) restricts the
 // candidate set; `order` selects the distance arithmetic.
+// Queries are read from qsoa (SoA, stride qstride): the points themselves
+// (qsoa = soa, qstride = N) for a self-query, or a separate query set.
 int search_core(const float* soa, int N, int D, int K, float r, int order,
                 const int* qids, int nq, const unsigned char* include, int threads,
-                int* idx_out, float* dist_out, int out_stride, long long* n_cand) {
+                int* idx_out, float* dist_out, int out_stride, long long* n_cand,
+                const float* qsoa = nullptr, long long qstride = 0) {
+    if (!qsoa) {
+        qsoa = soa;
+        qstride = N;
+    }
     const float r2 = r * r;  // float r2 = radius * radius (find_nbrs.cu:550, :571)
     CpuGrid G;
     bool have_grid = build_grid(soa, N, D, r, include, G);
@@ -250,7 +257,7 @@ int search_core(const float* soa, int N, int D, int K, float r, int order,
 #pragma omp for schedule(dynamic, 64)
         for (int t = 0; t < nq; ++t) {
             int qi = qids ? qids[t] : t;
-            for (int d = 0; d < D; ++d) q[d] = soa[(long long)d * N + qi];
+            for (int d = 0; d < D; ++d) q[d] = qsoa[(long long)d * qstride + qi];
             cand.clear();
             auto consider = [&](int j) {
                 ++total;
@@ -333,6 +340,16 @@ int oracle_search_subset(const float* soa, int N, int D, int K, float r, int ord
         if (qids[t] < 0 || qids[t] >= N) return 1;
     return search_core(soa, N, D, K, r, order, qids, nq, nullptr, threads, idx_out, dist_out,
                        nq, n_cand);
+}
+
+// Exact search for a separate query set (SoA qsoa[d*M + t], t < M) against the
+// N points (no counterpart in the reference engine, which only self-queries).
+// Output SoA [k*M + t].
+int oracle_search_queries(const float* soa, int N, const float* qsoa, int M, int D, int K, float r,
+                          int order, int threads, int* idx_out, float* dist_out, long long* n_cand) {
+    if (!args_ok(soa, N, D, K, r) || !qsoa || M <= 0 || !idx_out || !dist_out) return 1;
+    return search_core(soa, N, D, K, r, order, nullptr, M, nullptr, threads, idx_out, dist_out, M,
+                       n_cand, qsoa, M);
 }
 
 // Reference mode: the path the reference dispatcher picks, with that path's

@@ -45,11 +45,12 @@ def lib() -> ctypes.CDLL:
                                       ctypes.POINTER(I), ctypes.POINTER(LL)]
         L.oracle_search.argtypes = [P, I, I, I, F, I, I, P, P, ctypes.POINTER(LL)]
         L.oracle_search_subset.argtypes = [P, I, I, I, F, I, P, I, I, P, P, ctypes.POINTER(LL)]
+        L.oracle_search_queries.argtypes = [P, I, P, I, I, I, F, I, I, P, P, ctypes.POINTER(LL)]
         L.oracle_ref_search.argtypes = [P, I, I, I, F, I, P, P, P, ctypes.POINTER(I)]
         L.oracle_pair_d2_f64.argtypes = [P, I, I, P, P, LL, P]
         L.oracle_pair_d2_f32.argtypes = [P, I, I, I, P, P, LL, P]
-        for f in ("oracle_ref_plan", "oracle_search", "oracle_search_subset", "oracle_ref_search",
-                  "oracle_pair_d2_f64", "oracle_pair_d2_f32", "oracle_max_threads"):
+        for f in ("oracle_ref_plan", "oracle_search", "oracle_search_subset", "oracle_search_queries",
+                  "oracle_ref_search", "oracle_pair_d2_f64", "oracle_pair_d2_f32", "oracle_max_threads"):
             getattr(L, f).restype = I
         _oracle = L
     return _oracle
@@ -94,6 +95,24 @@ def search_subset(pts_soa: np.ndarray, qids: np.ndarray, K: int, r: float,
     nc = ctypes.c_longlong()
     st = lib().oracle_search_subset(p.ctypes.data, N, D, K, float(r), order, q.ctypes.data, len(q),
                                     threads, idx.ctypes.data, dist.ctypes.data, ctypes.byref(nc))
+    assert st == 0, st
+    return idx, dist, nc.value
+
+
+def search_queries(pts_soa: np.ndarray, q_soa: np.ndarray, K: int, r: float,
+                   order: int = ORDER_ENGINE, threads: int = 0):
+    """Exact search of a separate query set (SoA (D, M)) against the points
+    (SoA (D, N)); SoA (K, M) out."""
+    p = _soa(pts_soa)
+    q = _soa(q_soa)
+    D, N = p.shape
+    assert q.shape[0] == D
+    M = q.shape[1]
+    idx = np.empty((K, M), np.int32)
+    dist = np.empty((K, M), np.float32)
+    nc = ctypes.c_longlong()
+    st = lib().oracle_search_queries(p.ctypes.data, N, q.ctypes.data, M, D, K, float(r), order, threads,
+                                     idx.ctypes.data, dist.ctypes.data, ctypes.byref(nc))
     assert st == 0, st
     return idx, dist, nc.value
 

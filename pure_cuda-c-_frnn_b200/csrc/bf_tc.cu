@@ -336,7 +336,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     filter_kernel(const uint8_t* __restrict__ tiles, const float* __restrict__ qa, const float* __restrict__ pb,
                   int n, int ntiles, int cap, int* __restrict__ lists, int* __restrict__ counts,
                   int* __restrict__ overflow, int* __restrict__ n_overflow, int* __restrict__ err,
-                  int qb_begin, int qb_end) {
+                  int qb_begin, int qb_end, const uint8_t* __restrict__ qtiles) {
+    // qtiles: the query blocks' tiles (the points' own tiles for a self-query)
     using C = Cfg<KC>;
     constexpr int S = C::kStages;
     constexpr uint32_t TB = C::kTileBytes;
@@ -399,8 +400,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == kProducerWarp) {
         if (lane == 0) {
             mbar_expect_tx(afull, (has1 ? 2u : 1u) * TB);
-            bulk_g2s(sA, tiles + (size_t)qb0 * TB, TB, afull);
-            if (has1) bulk_g2s(sA + TB, tiles + (size_t)qb1 * TB, TB, afull);
+            bulk_g2s(sA, qtiles + (size_t)qb0 * TB, TB, afull);
+            if (has1) bulk_g2s(sA + TB, qtiles + (size_t)qb1 * TB, TB, afull);
             int issued = 0;
             for (int t = 0; t < ntiles; ++t) {
                 const int s = t % S;
@@ -531,7 +532,7 @@ template <int LCAP>
 __global__ void __launch_bounds__(kRerankWarps * 32)
     rerank_kernel(const float* __restrict__ rows32, int dim, int dp, const int* __restrict__ lists,
                   const int* __restrict__ counts, int cap, int K, float r2, int* __restrict__ oidx,
-                  float* __restrict__ odist, int q0, int q1) {
+                  float* __restrict__ odist, int q0, int q1, const float* __restrict__ qrows32) {
     extern __shared__ unsigned long long rsmem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     unsigned long long* keys = rsmem + (size_t)warp * LCAP;
@@ -541,7 +542,7 @@ __global__ void __launch_bounds__(kRerankWarps * 32)
     if (q >= q1) return;
     const int cnt = __ldg(&counts[q]);
     if (cnt > cap) return;  // searched by the fallback
-    const float* qsrc = rows32 + (size_t)q * dp;
+    const float* qsrc = qrows32 + (size_t)q * dp;  // the query's own fp32 row
     for (int d = lane; d < dp; d += 32) qrow[d] = __ldg(&qsrc[d]);
     __syncwarp();
     const int* mine = lists + (size_t)q * cap;
@@ -591,28 +592,29 @@ __global__ void __launch_bounds__(kRerankWarps * 32)
 
 template <int LCAP>
 cudaError_t launch_rerank(const float* rows32, int dim, int dp, const int* lists, const int* counts, int cap,
-                          int K, float r2, int* oidx, float* odist, int q0, int q1, cudaStream_t s) {
+                          int K, float r2, int* oidx, float* odist, int q0, int q1, cudaStream_t s,
+                          const float* qrows32) {
     const size_t smem = (size_t)kRerankWarps * (LCAP * 8 + dp * 4);
     cudaError_t e = cudaFuncSetAttribute(rerank_kernel<LCAP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
     if (q1 <= q0) return cudaSuccess;
     rerank_kernel<LCAP><<<(q1 - q0 + kRerankWarps - 1) / kRerankWarps, kRerankWarps * 32, smem, s>>>(
-        rows32, dim, dp, lists, counts, cap, K, r2, oidx, odist, q0, q1);
+        rows32, dim, dp, lists, counts, cap, K, r2, oidx, odist, q0, q1, qrows32);
     return cudaGetLastError();
 }
 
 template <int KC>
 cudaError_t launch_filter_kc(const uint8_t* tiles, const float* qa, const float* pb, int n, int ntiles,
                              int cap, int* lists, int* counts, int* overflow, int* n_overflow, int* err,
-                             int qb_begin, int qb_end, cudaStream_t s) {
+                             int qb_begin, int qb_end, cudaStream_t s, const uint8_t* qtiles) {
     const size_t smem = Cfg<KC>::kSmem;
     cudaError_t e =
         cudaFuncSetAttribute(filter_kernel<KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     if (qb_end <= qb_begin) return cudaSuccess;
     filter_kernel<KC><<<(qb_end - qb_begin + 1) / 2, kThreads, smem, s>>>(
-        tiles, qa, pb, n, ntiles, cap, lists, counts, overflow, n_overflow, err, qb_begin, qb_end);
+        tiles, qa, pb, n, ntiles, cap, lists, counts, overflow, n_overflow, err, qb_begin, qb_end, qtiles);
     return cudaGetLastError();
 }
 
@@ -640,25 +642,31 @@ cudaError_t launch_tc_prep(const float* pts, int n, int dim, const float* center
 
 cudaError_t launch_tc_filter(const uint8_t* tiles, const float* qa, const float* pb, int n, int dim,
                              int cap, int* lists, int* counts, int* overflow, int* n_overflow, int* err,
-                             int qb_begin, int qb_end, cudaStream_t s) {
+                             int qb_begin, int qb_end, cudaStream_t s, const uint8_t* qtiles, int m) {
     const int ntiles = (n + tc::kRows - 1) / tc::kRows;
-    if (qb_begin < 0 || qb_end > ntiles) return cudaErrorInvalidValue;
+    const int qtiles_n = qtiles ? (m + tc::kRows - 1) / tc::kRows : ntiles;
+    if (qb_begin < 0 || qb_end > qtiles_n) return cudaErrorInvalidValue;
+    if (!qtiles) {
+        qtiles = tiles;
+        m = n;
+    }
     if (tc_kc(dim) == 1)
-        return tc::launch_filter_kc<1>(tiles, qa, pb, n, ntiles, cap, lists, counts, overflow, n_overflow, err,
-                                       qb_begin, qb_end, s);
-    return tc::launch_filter_kc<2>(tiles, qa, pb, n, ntiles, cap, lists, counts, overflow, n_overflow, err,
-                                   qb_begin, qb_end, s);
+        return tc::launch_filter_kc<1>(tiles, qa, pb, m, ntiles, cap, lists, counts, overflow, n_overflow, err,
+                                       qb_begin, qb_end, s, qtiles);
+    return tc::launch_filter_kc<2>(tiles, qa, pb, m, ntiles, cap, lists, counts, overflow, n_overflow, err,
+                                   qb_begin, qb_end, s, qtiles);
 }
 
 cudaError_t launch_tc_rerank(const float* rows32, int dim, const int* lists, const int* counts, int cap,
                              int n, int K, float r2, int* oidx, float* odist, int q0, int q1,
-                             cudaStream_t s) {
+                             cudaStream_t s, const float* qrows32) {
     if (q0 < 0 || q1 > n) return cudaErrorInvalidValue;
+    if (!qrows32) qrows32 = rows32;
     const int dp = tc_row_floats(dim);
     const int lcap = coop::list_cap(K);
-    if (lcap == 64) return tc::launch_rerank<64>(rows32, dim, dp, lists, counts, cap, K, r2, oidx, odist, q0, q1, s);
-    if (lcap == 128) return tc::launch_rerank<128>(rows32, dim, dp, lists, counts, cap, K, r2, oidx, odist, q0, q1, s);
-    return tc::launch_rerank<256>(rows32, dim, dp, lists, counts, cap, K, r2, oidx, odist, q0, q1, s);
+    if (lcap == 64) return tc::launch_rerank<64>(rows32, dim, dp, lists, counts, cap, K, r2, oidx, odist, q0, q1, s, qrows32);
+    if (lcap == 128) return tc::launch_rerank<128>(rows32, dim, dp, lists, counts, cap, K, r2, oidx, odist, q0, q1, s, qrows32);
+    return tc::launch_rerank<256>(rows32, dim, dp, lists, counts, cap, K, r2, oidx, odist, q0, q1, s, qrows32);
 }
 
 }  // namespace frnn

@@ -23,7 +23,8 @@ template <bool D3, int KMAX>
 __global__ void __launch_bounds__(kBfThreads)
     bruteforce_kernel(const float* __restrict__ pts, int n, int dim, int K, float r2, int q0, int q1,
                       int* __restrict__ oidx, float* __restrict__ odist, long long ostride,
-                      int kBfTile, const int* __restrict__ qlist, int row_base) {
+                      int kBfTile, const int* __restrict__ qlist, int row_base,
+                      const float* __restrict__ qpts, int qn) {
     extern __shared__ unsigned long long smem[];
     unsigned long long* heap = smem;                                    // (K+B) x T keys
     float* tile = reinterpret_cast<float*>(heap + (size_t)TopK<KMAX>::slots(K) * kBfThreads);  // dim x kBfTile
@@ -36,7 +37,7 @@ __global__ void __launch_bounds__(kBfThreads)
     TopK<KMAX> tk;
     tk.init(heap + threadIdx.x, kBfThreads, K, r2);
     for (int d = 0; d < dim; ++d)
-        qs[d * kBfThreads + threadIdx.x] = active ? __ldg(&pts[(long long)d * n + q]) : 0.0f;
+        qs[d * kBfThreads + threadIdx.x] = active ? __ldg(&qpts[(long long)d * qn + q]) : 0.0f;
     float qx = 0.f, qy = 0.f, qz = 0.f;
     if (D3) { qx = qs[threadIdx.x]; qy = qs[kBfThreads + threadIdx.x]; qz = qs[2 * kBfThreads + threadIdx.x]; }
 
@@ -76,12 +77,12 @@ __global__ void __launch_bounds__(kBfThreads)
 template <bool D3, int KMAX>
 cudaError_t launch_bf(const float* pts, int n, int dim, int K, float r2, int q0, int q1, int* oidx,
                       float* odist, long long ostride, int tile, size_t smem, int blocks,
-                      cudaStream_t s, const int* qlist, int row_base) {
+                      cudaStream_t s, const int* qlist, int row_base, const float* qpts, int qn) {
     cudaError_t err = cudaFuncSetAttribute(bruteforce_kernel<D3, KMAX>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
     bruteforce_kernel<D3, KMAX><<<blocks, kBfThreads, smem, s>>>(pts, n, dim, K, r2, q0, q1, oidx,
-                                                                 odist, ostride, tile, qlist, row_base);
+                                                                 odist, ostride, tile, qlist, row_base, qpts ? qpts : pts, qpts ? qn : n);
     return cudaGetLastError();
 }
 
@@ -89,7 +90,7 @@ cudaError_t launch_bf(const float* pts, int n, int dim, int K, float r2, int q0,
 
 cudaError_t launch_bruteforce(const float* pts, int n, int dim, int K, float r2, int q0, int q1,
                               int* oidx, float* odist, long long ostride, cudaStream_t s,
-                              const int* qlist, int row_base) {
+                              const int* qlist, int row_base, const float* qpts, int qn) {
     if (q1 <= q0) return cudaSuccess;
     const size_t fixed = (size_t)TopK<128>::slots(K) * 8 * kBfThreads + (size_t)dim * 4 * kBfThreads;
     if (fixed + (size_t)dim * 4 * 8 > kSmemLimit) return cudaErrorInvalidConfiguration;
@@ -98,15 +99,15 @@ cudaError_t launch_bruteforce(const float* pts, int n, int dim, int K, float r2,
     const size_t smem = fixed + (size_t)dim * 4 * tile;
     const int blocks = (q1 - q0 + kBfThreads - 1) / kBfThreads;
     if (dim == 3) {
-        if (K <= 16) return launch_bf<true, 16>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base);
-        if (K <= 32) return launch_bf<true, 32>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base);
-        if (K <= 64) return launch_bf<true, 64>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base);
-        return launch_bf<true, 128>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base);
+        if (K <= 16) return launch_bf<true, 16>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base, qpts, qn);
+        if (K <= 32) return launch_bf<true, 32>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base, qpts, qn);
+        if (K <= 64) return launch_bf<true, 64>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base, qpts, qn);
+        return launch_bf<true, 128>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base, qpts, qn);
     }
-    if (K <= 16) return launch_bf<false, 16>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base);
-    if (K <= 32) return launch_bf<false, 32>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base);
-    if (K <= 64) return launch_bf<false, 64>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base);
-    return launch_bf<false, 128>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base);
+    if (K <= 16) return launch_bf<false, 16>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base, qpts, qn);
+    if (K <= 32) return launch_bf<false, 32>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base, qpts, qn);
+    if (K <= 64) return launch_bf<false, 64>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base, qpts, qn);
+    return launch_bf<false, 128>(pts, n, dim, K, r2, q0, q1, oidx, odist, ostride, tile, smem, blocks, s, qlist, row_base, qpts, qn);
 }
 
 }  // namespace frnn

@@ -69,6 +69,11 @@ struct frnn_engine {
     // principal-axis grid: moments, axes, projected coordinates, estimate
     DevBuf pca_partial, pca_moments, pca_mu, pca_pm, proj_box_partial, proj_ticket, proj_out;
     DevBuf proj_u, proj_s, pca_smp, pca_h, pca_counts;
+    // a separate query set: its grid (same plan as the points), projected
+    // coordinates and tensor-core tiles
+    DevBuf q_counts, q_starts, q_cellrank, q_rows, q_ids, q_inv, q_proj_u, q_proj_s, q_proj_partial,
+        q_proj_out, q_box_out;
+    DevBuf q_tiles, q_rows32, q_qa, q_pb;
     void* h_pca = nullptr;    // pinned, 32 KiB
     int grid_axes_mode = 0;   // FRNN_OPT_GRID_AXES
     int last_principal = 0;   // the last grid was on principal axes
@@ -653,18 +658,32 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
 // Queries [qb_begin*128, min(N, qb_end*128)) (all of them for a whole search),
 // results to rows q - qb_begin*128 of out[k*rows + row].
 int run_brute_tc(frnn_engine* e, const float* d_pts, int N, int dim, int K, float radius,
-                 int* out_idx, float* out_dist, int qb_begin, int qb_end, bool* done) {
+                 int* out_idx, float* out_dist, int qb_begin, int qb_end, bool* done,
+                 const float* d_q = nullptr, int M = 0) {
+    // d_q: a separate query set of M points (tiles [qb_begin, qb_end) of its
+    // own); the points themselves otherwise
     cudaStream_t s = e->stream;
     *done = false;
+    const bool sep = d_q != nullptr;
+    const int Q = sep ? M : N;
     const float r2 = radius * radius;
-    FRNN_GROW(e, e->tc_box, 512 * sizeof(float) + 16);
-    int* nonfinite = reinterpret_cast<int*>(e->tc_box.as<float>() + 512);
+    FRNN_GROW(e, e->tc_box, 1024 * sizeof(float) + 16);
+    int* nonfinite = reinterpret_cast<int*>(e->tc_box.as<float>() + 1024);
     stage_begin(e, ST_TC_PREP);
     FRNN_CHECK(e, cudaMemsetAsync(nonfinite, 0, sizeof(int), s), "memset non-finite flag");
     FRNN_CHECK(e, launch_tc_box(d_pts, N, dim, e->tc_box.as<float>(), nonfinite, s), "box launch");
     e->launches++;
+    if (sep) {
+        FRNN_CHECK(e, launch_tc_box(d_q, M, dim, e->tc_box.as<float>() + 512, nonfinite, s), "box launch");
+        e->launches++;
+    }
+    float* hq = static_cast<float*>(e->h_pca) + 6144;  // the query set's box
     FRNN_CHECK(e, cudaMemcpyAsync(e->h_tc, e->tc_box.p, 2 * dim * sizeof(float), cudaMemcpyDeviceToHost, s),
                "box readback");
+    if (sep)
+        FRNN_CHECK(e, cudaMemcpyAsync(hq, e->tc_box.as<float>() + 512, 2 * dim * sizeof(float),
+                                      cudaMemcpyDeviceToHost, s),
+                   "query box readback");
     FRNN_CHECK(e, cudaMemcpyAsync(e->h_tc + 2 * kMaxK, nonfinite, sizeof(int), cudaMemcpyDeviceToHost, s),
                "flag readback");
     FRNN_CHECK(e, cudaStreamSynchronize(s), "box sync");
@@ -672,12 +691,17 @@ int run_brute_tc(frnn_engine* e, const float* d_pts, int N, int dim, int K, floa
     std::memcpy(&flag, e->h_tc + 2 * kMaxK, sizeof(int));
     if (flag != 0) return FRNN_OK;
 
-    // centre = per-dimension midpoint; scale = 2^(14 - e) with max|x - c| < 2^e,
-    // so every scaled coordinate stays below 2^14 in magnitude (fp16 max 65504)
+    // centre = per-dimension midpoint of the box of points (and queries);
+    // scale = 2^(14 - e) with max|x - c| < 2^e, so every scaled coordinate
+    // stays below 2^14 in magnitude (fp16 max 65504)
     float* center = e->h_tc + 2 * kMaxK + 4;
     double hmax = 0.0;
     for (int d = 0; d < dim; ++d) {
-        const double lo = e->h_tc[2 * d], hi = e->h_tc[2 * d + 1];
+        double lo = e->h_tc[2 * d], hi = e->h_tc[2 * d + 1];
+        if (sep) {
+            lo = std::min(lo, (double)hq[2 * d]);
+            hi = std::max(hi, (double)hq[2 * d + 1]);
+        }
         center[d] = (float)(0.5 * (lo + hi));
         hmax = std::max(hmax, std::max(hi - (double)center[d], (double)center[d] - lo));
     }
@@ -693,7 +717,7 @@ int run_brute_tc(frnn_engine* e, const float* d_pts, int N, int dim, int K, floa
     const float one_minus_alpha = 1.0f - std::ldexp(1.0f, -8);
     const float eta_c = (float)(4.0 * eta * std::sqrt((double)dim));
 
-    const int ntiles = (N + 127) / 128;
+    const int ntiles = (N + 127) / 128, qtiles = (Q + 127) / 128;
     const int dp = tc_row_floats(dim);
     const int cap = tc_list_cap(K);
     FRNN_GROW(e, e->tc_center, (size_t)dim * 4);
@@ -701,9 +725,9 @@ int run_brute_tc(frnn_engine* e, const float* d_pts, int N, int dim, int K, floa
     FRNN_GROW(e, e->tc_rows, (size_t)N * dp * 4);
     FRNN_GROW(e, e->tc_qa, (size_t)ntiles * 128 * 4);
     FRNN_GROW(e, e->tc_pb, (size_t)ntiles * 128 * 4);
-    FRNN_GROW(e, e->lists, (size_t)N * cap * 4);
-    FRNN_GROW(e, e->list_counts, (size_t)N * 4);
-    FRNN_GROW(e, e->overflow, (size_t)N * 4);
+    FRNN_GROW(e, e->lists, (size_t)Q * cap * 4);
+    FRNN_GROW(e, e->list_counts, (size_t)Q * 4);
+    FRNN_GROW(e, e->overflow, (size_t)Q * 4);
     FRNN_GROW(e, e->n_overflow, 16);
     FRNN_CHECK(e, cudaMemcpyAsync(e->tc_center.p, center, (size_t)dim * 4, cudaMemcpyHostToDevice, s),
                "centre upload");
@@ -711,22 +735,38 @@ int run_brute_tc(frnn_engine* e, const float* d_pts, int N, int dim, int K, floa
                                  eta_c, rc, e->tc_tiles.as<uint8_t>(), e->tc_rows.as<float>(),
                                  e->tc_qa.as<float>(), e->tc_pb.as<float>(), s),
                "prep launch");
+    e->launches++;
+    const float* qa = e->tc_qa.as<float>();
+    if (sep) {
+        // the queries' tiles, rows and query-side terms (point-side terms unused)
+        FRNN_GROW(e, e->q_tiles, (size_t)qtiles * tc_tile_bytes(dim));
+        FRNN_GROW(e, e->q_rows32, (size_t)M * dp * 4);
+        FRNN_GROW(e, e->q_qa, (size_t)qtiles * 128 * 4);
+        FRNN_GROW(e, e->q_pb, (size_t)qtiles * 128 * 4);
+        FRNN_CHECK(e, launch_tc_prep(d_q, M, dim, e->tc_center.as<float>(), (float)scale, one_minus_alpha,
+                                     eta_c, rc, e->q_tiles.as<uint8_t>(), e->q_rows32.as<float>(),
+                                     e->q_qa.as<float>(), e->q_pb.as<float>(), s),
+                   "query prep launch");
+        e->launches++;
+        qa = e->q_qa.as<float>();
+    }
     stage_end(e, ST_TC_PREP);
-    const int q0 = qb_begin * 128, q1 = std::min(N, qb_end * 128), rows = q1 - q0;
+    const int q0 = qb_begin * 128, q1 = std::min(Q, qb_end * 128), rows = q1 - q0;
     FRNN_CHECK(e, cudaMemsetAsync(e->n_overflow.p, 0, 4, s), "memset overflow count");
     stage_begin(e, ST_TC_FILTER);
-    FRNN_CHECK(e, launch_tc_filter(e->tc_tiles.as<uint8_t>(), e->tc_qa.as<float>(), e->tc_pb.as<float>(), N,
-                                   dim, cap, e->lists.as<int>(), e->list_counts.as<int>(),
-                                   e->overflow.as<int>(), e->n_overflow.as<int>(), e->err_flag.as<int>(),
-                                   qb_begin, qb_end, s),
+    FRNN_CHECK(e, launch_tc_filter(e->tc_tiles.as<uint8_t>(), qa, e->tc_pb.as<float>(), N, dim, cap,
+                                   e->lists.as<int>(), e->list_counts.as<int>(), e->overflow.as<int>(),
+                                   e->n_overflow.as<int>(), e->err_flag.as<int>(), qb_begin, qb_end, s,
+                                   sep ? e->q_tiles.as<uint8_t>() : nullptr, Q),
                "filter launch");
     stage_end(e, ST_TC_FILTER);
     stage_begin(e, ST_TC_RERANK);
     FRNN_CHECK(e, launch_tc_rerank(e->tc_rows.as<float>(), dim, e->lists.as<int>(), e->list_counts.as<int>(),
-                                   cap, N, K, r2, out_idx, out_dist, q0, q1, s),
+                                   cap, Q, K, r2, out_idx, out_dist, q0, q1, s,
+                                   sep ? e->q_rows32.as<float>() : nullptr),
                "rerank launch");
     stage_end(e, ST_TC_RERANK);
-    e->launches += 3;
+    e->launches += 2;
     // queries with more candidates than their list holds: SIMT brute force
     int* h_nov = reinterpret_cast<int*>(e->h_tc + 2 * kMaxK + 1);
     FRNN_CHECK(e, cudaMemcpyAsync(h_nov, e->n_overflow.p, sizeof(int), cudaMemcpyDeviceToHost, s),
@@ -735,12 +775,229 @@ int run_brute_tc(frnn_engine* e, const float* d_pts, int N, int dim, int K, floa
     if (*h_nov > 0) {
         stage_begin(e, ST_BRUTE);
         FRNN_CHECK(e, launch_bruteforce(d_pts, N, dim, K, r2, 0, *h_nov, out_idx, out_dist, rows, s,
-                                        e->overflow.as<int>(), q0),
+                                        e->overflow.as<int>(), q0, d_q, M),
                    "overflow brute force launch");
         stage_end(e, ST_BRUTE);
         e->launches++;
     }
     *done = true;
+    return FRNN_OK;
+}
+
+// Cell histogram, prefix scan and counting-sort scatter of one point set
+// (points or queries) on plan P; the scan's status words and ticket are shared.
+int sort_into_cells(frnn_engine* e, const float* pts, const GridPlan& P, const float* proj, DevBuf& counts,
+                    DevBuf& starts, DevBuf& cellrank, DevBuf& rows, DevBuf& ids, DevBuf* inv,
+                    DevBuf* proj_s) {
+    cudaStream_t s = e->stream;
+    const int n = P.n;
+    FRNN_GROW(e, counts, (size_t)P.cells * 4);
+    FRNN_GROW(e, starts, ((size_t)P.cells + 1) * 4);
+    FRNN_GROW(e, e->scan_status, (size_t)scan_tiles(P.cells) * 8);
+    FRNN_GROW(e, cellrank, (size_t)n * 8);
+    FRNN_GROW(e, rows, (size_t)n * P.row * 4);
+    FRNN_GROW(e, ids, (size_t)n * 4);
+    if (inv) FRNN_GROW(e, *inv, (size_t)n * 4);
+    if (proj) FRNN_GROW(e, *proj_s, (size_t)n * kProjStride * 4);
+    FRNN_CHECK(e, cudaMemsetAsync(counts.p, 0, (size_t)P.cells * 4, s), "memset counts");
+    FRNN_CHECK(e, cudaMemsetAsync(e->scan_ticket.p, 0, 4, s), "memset scan ticket");
+    FRNN_CHECK(e, launch_hash_count(pts, P, counts.as<int>(), cellrank.as<int2>(), s, proj), "hash_count launch");
+    e->epoch = (e->epoch + 1) & 0x3fffffffu;
+    if (e->epoch == 0) {
+        FRNN_CHECK(e, cudaMemsetAsync(e->scan_status.p, 0, e->scan_status.bytes, s), "memset status");
+        e->epoch = 1;
+    }
+    FRNN_CHECK(e, launch_scan(counts.as<int>(), starts.as<int>(), P.cells, e->scan_status.as<unsigned long long>(),
+                              e->scan_ticket.as<int>(), e->epoch, e->err_flag.as<int>(), s),
+               "scan launch");
+    FRNN_CHECK(e, launch_scatter(pts, P, cellrank.as<int2>(), starts.as<int>(), rows.as<float>(), ids.as<int>(), s,
+                                 inv ? inv->as<int>() : nullptr, proj, proj ? proj_s->as<float>() : nullptr),
+               "scatter launch");
+    e->launches += 3;
+    return FRNN_OK;
+}
+
+// Grid search of a separate query set against the points: the queries are
+// sorted into the points' grid (the same plan) so that neighbouring queries
+// read the same candidate rows; results out[k*M + q] in query order.
+int run_grid_queries(frnn_engine* e, const float* d_pts, int N, const float* d_q, int M, int dim, int K,
+                     float r2, const GridPlan& P, const float* proj_p, const float* proj_q, int* out_idx,
+                     float* out_dist) {
+    cudaStream_t s = e->stream;
+    stage_begin(e, ST_HASH);
+    int st = sort_into_cells(e, d_pts, P, proj_p, e->counts, e->starts, e->cellrank, e->rows, e->ids, nullptr,
+                             &e->proj_s);
+    if (st != FRNN_OK) return st;
+    GridPlan Pq = P;
+    Pq.n = M;
+    st = sort_into_cells(e, d_q, Pq, proj_q, e->q_counts, e->q_starts, e->q_cellrank, e->q_rows, e->q_ids,
+                         &e->q_inv, &e->q_proj_s);
+    if (st != FRNN_OK) return st;
+    stage_end(e, ST_HASH);
+    const float* proj_s = proj_p ? e->proj_s.as<float>() : nullptr;
+    const float* qproj_s = proj_q ? e->q_proj_s.as<float>() : nullptr;
+    if (P.dim == 3 && P.g == 3 && K <= 32 && !proj_p) {
+        const int cap = K <= 16 ? 64 : 128;
+        FRNN_GROW(e, e->lists, (size_t)M * cap * 8);
+        FRNN_GROW(e, e->list_counts, (size_t)M * 4);
+        FRNN_GROW(e, e->overflow, (size_t)M * 4);
+        FRNN_GROW(e, e->n_overflow, 16);
+        FRNN_CHECK(e, cudaMemsetAsync(e->n_overflow.p, 0, 4, s), "memset overflow count");
+        stage_begin(e, ST_COLLECT);
+        FRNN_CHECK(e, launch_collect_d3(e->rows.as<float>(), e->starts.as<int>(), P, r2, cap,
+                                        e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
+                                        e->overflow.as<int>(), e->n_overflow.as<int>(), 0, M, s,
+                                        e->q_rows.as<float>()),
+                   "collect launch");
+        stage_end(e, ST_COLLECT);
+        stage_begin(e, ST_EMIT);
+        FRNN_CHECK(e, launch_emit_lists(e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
+                                        e->q_inv.as<int>(), 0, M, K, cap, r2, out_idx, out_dist, s),
+                   "emit launch");
+        FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(), P, K, r2, 0,
+                                         M, out_idx, out_dist, M, e->q_ids.as<int>(), s, e->overflow.as<int>(),
+                                         e->n_overflow.as<int>(), -1, nullptr, e->q_rows.as<float>(), nullptr),
+                   "overflow search launch");
+        stage_end(e, ST_EMIT);
+        e->launches += 3;
+        return FRNN_OK;
+    }
+    stage_begin(e, ST_SEARCH);
+    if ((long long)M * K * 8 <= e->direct_output_max_bytes) {
+        FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(), P, K, r2, 0,
+                                         M, out_idx, out_dist, M, e->q_ids.as<int>(), s, nullptr, nullptr, -1,
+                                         proj_s, e->q_rows.as<float>(), qproj_s),
+                   "grid search launch");
+        stage_end(e, ST_SEARCH);
+        e->launches++;
+        return FRNN_OK;
+    }
+    FRNN_GROW(e, e->tmp_idx, (size_t)M * K * 4);
+    FRNN_GROW(e, e->tmp_dist, (size_t)M * K * 4);
+    FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(), P, K, r2, 0, M,
+                                     e->tmp_idx.as<int>(), e->tmp_dist.as<float>(), M, nullptr, s, nullptr,
+                                     nullptr, -1, proj_s, e->q_rows.as<float>(), qproj_s),
+               "grid search launch");
+    stage_end(e, ST_SEARCH);
+    stage_begin(e, ST_UNPERMUTE);
+    FRNN_CHECK(e, launch_unpermute(e->tmp_idx.as<int>(), e->tmp_dist.as<float>(), e->q_ids.as<int>(), M, K,
+                                   out_idx, out_dist, s),
+               "unpermute launch");
+    stage_end(e, ST_UNPERMUTE);
+    e->launches += 2;
+    return FRNN_OK;
+}
+
+// A separate query set (M points, SoA) against the N points: the same paths
+// and arithmetic as the self-query; results out[k*M + q].
+int search_queries_core(frnn_engine* e, const float* d_pts, int N, const float* d_q, int M, int dim, int K,
+                        float radius) {
+    cudaStream_t s = e->stream;
+    const float r2 = radius * radius;
+    FRNN_GROW(e, e->out_idx, (size_t)M * K * 4);
+    FRNN_GROW(e, e->out_dist, (size_t)M * K * 4);
+    int* out_idx = e->out_idx.as<int>();
+    float* out_dist = e->out_dist.as<float>();
+    e->last_N = -1;
+    e->last_part_rows = -1;
+    for (int i = 0; i < FRNN_STAGES; ++i) e->stage_used[i] = false;
+    int path = e->forced_path;
+    if (path == FRNN_PATH_AUTO) {
+        const double work = (double)N * (double)M * dim;
+        if (dim > 32) path = N >= kTcMinPoints ? FRNN_PATH_BRUTE_TC : FRNN_PATH_BRUTE;
+        else if (work <= kBruteSmallWork) path = FRNN_PATH_BRUTE;
+        else path = FRNN_PATH_GRID;
+    }
+    if (path == FRNN_PATH_GRID && dim > 32) path = FRNN_PATH_BRUTE;
+
+    GridPlan P{};
+    bool grid_ok = false, principal = false;
+    if (path == FRNN_PATH_GRID) {
+        const int g = grid_axes_for(dim);
+        const int blocks = std::min(bbox_blocks(std::max(N, M), e->sms), kBoxMaxBlocks);
+        FRNN_GROW(e, e->q_box_out, 64);
+        stage_begin(e, ST_BBOX);
+        FRNN_CHECK(e, launch_bbox(d_pts, N, g, e->box_partial.as<float>(), e->box_ticket.as<unsigned>(),
+                                  e->box_out.as<float>(), blocks, s),
+                   "bbox launch");
+        FRNN_CHECK(e, launch_bbox(d_q, M, g, e->box_partial.as<float>(), e->box_ticket.as<unsigned>(),
+                                  e->q_box_out.as<float>(), blocks, s),
+                   "query bbox launch");
+        stage_end(e, ST_BBOX);
+        e->launches += 2;
+        float* hqb = static_cast<float*>(e->h_pca) + 6144;
+        FRNN_CHECK(e, cudaMemcpyAsync(e->h_box, e->box_out.p, 9 * sizeof(float), cudaMemcpyDeviceToHost, s),
+                   "bbox readback");
+        FRNN_CHECK(e, cudaMemcpyAsync(hqb, e->q_box_out.p, 9 * sizeof(float), cudaMemcpyDeviceToHost, s),
+                   "query bbox readback");
+        FRNN_CHECK(e, cudaStreamSynchronize(s), "bbox sync");
+        if (e->h_box[8] != 0.0f || hqb[8] != 0.0f)
+            return fail(e, FRNN_ERR_INVALID_ARG, "points or queries contain NaN or Inf coordinates");
+        // the grid covers the points; queries outside it clamp to the edge
+        // cells, whose shells still hold every point within r of them
+        grid_ok = make_plan(e->h_box, N, dim, radius, P);
+        if (dim > 4 && dim <= kMaxPcaDim && e->grid_axes_mode != FRNN_GRID_AXES_LEADING) {
+            int st = plan_principal(e, d_pts, N, dim, radius, grid_ok, P, &principal);
+            if (st != FRNN_OK) return st;
+            grid_ok |= principal;
+        }
+        if (!grid_ok) path = FRNN_PATH_BRUTE;
+    }
+    if (path == FRNN_PATH_GRID && principal) {
+        // the queries' projected coordinates on the same axes
+        const int axes = std::min(dim, kMaxGridAxes);
+        const int pblocks = std::min(bbox_blocks(M, e->sms), kBoxMaxBlocks);
+        const int pslots = pca_project_slots();
+        FRNN_GROW(e, e->q_proj_u, (size_t)M * kProjStride * 4);
+        FRNN_GROW(e, e->q_proj_partial, (size_t)pblocks * pslots * 4);
+        FRNN_GROW(e, e->q_proj_out, 64 * 4);
+        FRNN_CHECK(e, launch_pca_project(d_q, M, dim, axes, e->pca_mu.as<float>(), e->pca_pm.as<float>(),
+                                         e->q_proj_u.as<float>(), e->q_proj_partial.as<float>(),
+                                         e->proj_ticket.as<unsigned>(), e->q_proj_out.as<float>(), pblocks, s),
+                   "query project launch");
+        e->launches++;
+        float* hqp = static_cast<float*>(e->h_pca) + 6400;
+        FRNN_CHECK(e, cudaMemcpyAsync(hqp, e->q_proj_out.p, (size_t)pslots * 4, cudaMemcpyDeviceToHost, s),
+                   "query projection readback");
+        FRNN_CHECK(e, cudaStreamSynchronize(s), "query projection sync");
+        if (hqp[pslots - 1] != 0.0f)
+            return fail(e, FRNN_ERR_INVALID_ARG, "points or queries contain NaN or Inf coordinates");
+    }
+    if (path == FRNN_PATH_BRUTE_TC) {
+        bool done = false;
+        int st = run_brute_tc(e, d_pts, N, dim, K, radius, out_idx, out_dist, 0, (M + 127) / 128, &done, d_q, M);
+        if (st != FRNN_OK) return st;
+        if (!done) path = FRNN_PATH_BRUTE;
+    }
+    if (path == FRNN_PATH_GRID) {
+        int st = run_grid_queries(e, d_pts, N, d_q, M, dim, K, r2, P, principal ? e->proj_u.as<float>() : nullptr,
+                                  principal ? e->q_proj_u.as<float>() : nullptr, out_idx, out_dist);
+        if (st != FRNN_OK) return st;
+        e->last_g = P.g;
+        e->last_cells = P.cells;
+    } else {
+        e->last_g = 0;
+        e->last_cells = 0;
+        if (path == FRNN_PATH_BRUTE) {
+            stage_begin(e, ST_BRUTE);
+            FRNN_CHECK(e, launch_bruteforce(d_pts, N, dim, K, r2, 0, M, out_idx, out_dist, M, s, nullptr, 0, d_q, M),
+                       "bruteforce launch");
+            stage_end(e, ST_BRUTE);
+            e->launches++;
+        }
+    }
+    e->last_path = path;
+    e->last_principal = path == FRNN_PATH_GRID && principal;
+    FRNN_CHECK(e, cudaMemcpyAsync(e->h_err, e->err_flag.p, sizeof(int), cudaMemcpyDeviceToHost, s),
+               "error flag readback");
+    FRNN_CHECK(e, cudaStreamSynchronize(s), "search sync");
+    if (*e->h_err != 0) {
+        cudaMemsetAsync(e->err_flag.p, 0, sizeof(int), s);
+        cudaStreamSynchronize(s);
+        return fail(e, FRNN_ERR_TIMEOUT, "a bounded device-side wait gave up");
+    }
+    e->last_N = M;
+    e->last_K = K;
     return FRNN_OK;
 }
 
@@ -942,7 +1199,10 @@ int frnn_destroy(frnn_engine* e) {
                           &e->tc_box, &e->tc_center, &e->tc_tiles, &e->tc_rows, &e->tc_qa,
                           &e->tc_pb, &e->part_ids, &e->pca_partial, &e->pca_moments, &e->pca_mu,
                           &e->pca_pm, &e->proj_box_partial, &e->proj_ticket, &e->proj_out,
-                          &e->proj_u, &e->proj_s, &e->pca_smp, &e->pca_h, &e->pca_counts};
+                          &e->proj_u, &e->proj_s, &e->pca_smp, &e->pca_h, &e->pca_counts,
+                          &e->q_counts, &e->q_starts, &e->q_cellrank, &e->q_rows, &e->q_ids, &e->q_inv,
+                          &e->q_proj_u, &e->q_proj_s, &e->q_proj_partial, &e->q_proj_out, &e->q_box_out,
+                          &e->q_tiles, &e->q_rows32, &e->q_qa, &e->q_pb};
         for (DevBuf* b : bufs) free_buf(*b);
         for (cudaEvent_t& ev : e->ev)
             if (ev) cudaEventDestroy(ev);
@@ -1023,6 +1283,24 @@ int frnn_search_gpu(frnn_engine* e, const float* d_points_soa, int N, int dim, i
 int frnn_search_gpu_async(frnn_engine* e, const float* d_points_soa, int N, int dim, int K,
                           float radius, int** d_idxs, float** d_dists) {
     return search_gpu_impl(e, d_points_soa, N, dim, K, radius, d_idxs, d_dists, false);
+}
+
+int frnn_search_gpu_queries(frnn_engine* e, const float* d_points_soa, int N, const float* d_queries_soa, int M,
+                            int dim, int K, float radius, int** d_idxs, float** d_dists) {
+    int st = check_search_args(e, d_points_soa, N, dim, K, radius);
+    if (st != FRNN_OK) return st;
+    if (!d_queries_soa || M < 1) return fail(e, FRNN_ERR_INVALID_ARG, "queries must be a device array of M >= 1 points");
+    if (!d_idxs || !d_dists) return fail(e, FRNN_ERR_INVALID_ARG, "output pointers are null");
+    DeviceGuard g(e->device);
+    st = check_device_ptr(e, d_points_soa);
+    if (st != FRNN_OK) return st;
+    st = check_device_ptr(e, d_queries_soa);
+    if (st != FRNN_OK) return st;
+    st = search_queries_core(e, d_points_soa, N, d_queries_soa, M, dim, K, radius);
+    if (st != FRNN_OK) return st;
+    *d_idxs = e->out_idx.as<int>();
+    *d_dists = e->out_dist.as<float>();
+    return FRNN_OK;
 }
 
 int frnn_search_gpu_part(frnn_engine* e, const float* d_points_soa, int N, int dim, int K, float radius,

@@ -37,20 +37,25 @@ cudaError_t launch_scatter(const float* pts, const GridPlan& P, const int2* cell
 // row_base (>= 0): without scatter_ids, sorted position sq goes to row
 // sq - row_base instead of sq - q0 (for query lists).  proj (optional): the
 // grid axes are the sorted projected coordinates proj[sq*kProjStride + d].
+// qrows / qproj (optional): a separate query set's rows and projected
+// coordinates in the same grid's cell order (sq indexes them).
 cudaError_t launch_grid_search(const float* rows, const int* ids, const int* starts,
                                const GridPlan& P, int K, float r2, int q0, int q1, int* oidx,
                                float* odist, long long ostride, const int* scatter_ids,
                                cudaStream_t s, const int* qlist = nullptr,
                                const int* qcount = nullptr, long long row_base = -1,
-                               const float* proj = nullptr);
+                               const float* proj = nullptr, const float* qrows = nullptr,
+                               const float* qproj = nullptr);
 
 // grid_collect.cu -- D = 3 two-kernel search (K <= 32).
 // collect: for sorted queries sq in [q0, q1), every in-radius key goes to
 // lists[sq*cap + j]; counts[sq] = number found; queries with more than cap are
-// appended to overflow[0..*n_overflow).
+// appended to overflow[0..*n_overflow).  qrows (optional): a separate query
+// set's rows in the grid's cell order.
 cudaError_t launch_collect_d3(const float* rows, const int* starts, const GridPlan& P, float r2,
                               int cap, unsigned long long* lists, int* counts, int* overflow,
-                              int* n_overflow, int q0, int q1, cudaStream_t s);
+                              int* n_overflow, int q0, int q1, cudaStream_t s,
+                              const float* qrows = nullptr);
 // emit: for output rows q < n -- sorted position map[q] (map = inv: rows in
 // original order), or q0 + q without map -- whose count is at most cap, the K
 // smallest keys ascending to out[k*n + q], padded (-1, r2).
@@ -65,9 +70,11 @@ cudaError_t launch_unpermute(const int* in_idx, const float* in_dist, const int*
 // Queries [q0, q1) of the SoA cloud against all n points; results of query q
 // go to out[k*ostride + (q - q0)].  With qlist (device), the queries are
 // qlist[q0..q1) instead and query q's results go to out[k*ostride + q - row_base].
+// qpts (optional): the queries are a separate SoA set of qn points.
 cudaError_t launch_bruteforce(const float* pts, int n, int dim, int K, float r2, int q0, int q1,
                               int* oidx, float* odist, long long ostride, cudaStream_t s,
-                              const int* qlist = nullptr, int row_base = 0);
+                              const int* qlist = nullptr, int row_base = 0,
+                              const float* qpts = nullptr, int qn = 0);
 
 // grid_pca.cu -- principal axes for the grid (5 <= dim <= 32).
 int pca_slots(int dim);            // dim sums + dim*(dim+1)/2 products
@@ -104,13 +111,17 @@ cudaError_t launch_tc_prep(const float* pts, int n, int dim, const float* center
                            float* qa, float* pb, cudaStream_t s);
 // counts[q] = candidates of query q (all q < n); the first cap of them in
 // lists[q*cap ..]; queries with more go to overflow[0..*n_overflow)
+// qtiles (optional): a separate query set of m points (its own tiles; qa then
+// holds its terms), searched against the n points of tiles / pb
 cudaError_t launch_tc_filter(const uint8_t* tiles, const float* qa, const float* pb, int n, int dim,
                              int cap, int* lists, int* counts, int* overflow, int* n_overflow, int* err,
-                             int qb_begin, int qb_end, cudaStream_t s);
+                             int qb_begin, int qb_end, cudaStream_t s, const uint8_t* qtiles = nullptr,
+                             int m = 0);
 // exact results for the queries q in [q0, q1) with counts[q] <= cap, to row
 // q - q0 of out[k*(q1-q0) + row]
+// qrows32 (optional): the separate query set's fp32 rows (n = its size)
 cudaError_t launch_tc_rerank(const float* rows32, int dim, const int* lists, const int* counts, int cap,
                              int n, int K, float r2, int* oidx, float* odist, int q0, int q1,
-                             cudaStream_t s);
+                             cudaStream_t s, const float* qrows32 = nullptr);
 
 }  // namespace frnn

@@ -34,10 +34,13 @@ __global__ void __launch_bounds__(256)
     collect_d3_kernel(const float4* __restrict__ rows, const int* __restrict__ starts, GridPlan P,
                       float r2, int cap, unsigned long long* __restrict__ lists,
                       int* __restrict__ counts, int* __restrict__ overflow,
-                      int* __restrict__ n_overflow, int q0, int q1) {
+                      int* __restrict__ n_overflow, int q0, int q1,
+                      const float4* __restrict__ qrows) {
+    // queries: the points themselves (qrows == rows) or a separate set in
+    // the same grid's cell order
     const int sq = q0 + blockIdx.x * blockDim.x + threadIdx.x;
     if (sq >= q1) return;
-    const float4 q = __ldg(&rows[sq]);
+    const float4 q = __ldg(&qrows[sq]);
     const float cs = P.cell, eps = P.eps;
     const int gx = cell_coord(q.x, P.origin[0], P.inv_cell, P.res[0]);
     const int gy = cell_coord(q.y, P.origin[1], P.inv_cell, P.res[1]);
@@ -57,19 +60,27 @@ __global__ void __launch_bounds__(256)
             // clamped to [0, n): a corrupt start table never reads out of bounds
             int j = min(max(__ldg(&starts[rb + xlo]), 0), P.n);
             const int e = min(max(__ldg(&starts[rb + xhi + 1]), j), P.n);
+            for (; j + 3 < e; j += 4) {
+                const float4 p0 = __ldg(&rows[j]);
+                const float4 p1 = __ldg(&rows[j + 1]);
+                const float4 p2 = __ldg(&rows[j + 2]);
+                const float4 p3 = __ldg(&rows[j + 3]);
+                const float d0 = dist2_d3(q.x, q.y, q.z, p0.x, p0.y, p0.z);
+                const float d1 = dist2_d3(q.x, q.y, q.z, p1.x, p1.y, p1.z);
+                const float d2 = dist2_d3(q.x, q.y, q.z, p2.x, p2.y, p2.z);
+                const float d3 = dist2_d3(q.x, q.y, q.z, p3.x, p3.y, p3.z);
+                if (d0 < r2) { if (n < cap) mine[n] = make_key(d0, __float_as_int(p0.w)); ++n; }
+                if (d1 < r2) { if (n < cap) mine[n] = make_key(d1, __float_as_int(p1.w)); ++n; }
+                if (d2 < r2) { if (n < cap) mine[n] = make_key(d2, __float_as_int(p2.w)); ++n; }
+                if (d3 < r2) { if (n < cap) mine[n] = make_key(d3, __float_as_int(p3.w)); ++n; }
+            }
             for (; j + 1 < e; j += 2) {
                 const float4 p0 = __ldg(&rows[j]);
                 const float4 p1 = __ldg(&rows[j + 1]);
                 const float d0 = dist2_d3(q.x, q.y, q.z, p0.x, p0.y, p0.z);
                 const float d1 = dist2_d3(q.x, q.y, q.z, p1.x, p1.y, p1.z);
-                if (d0 < r2) {
-                    if (n < cap) mine[n] = make_key(d0, __float_as_int(p0.w));
-                    ++n;
-                }
-                if (d1 < r2) {
-                    if (n < cap) mine[n] = make_key(d1, __float_as_int(p1.w));
-                    ++n;
-                }
+                if (d0 < r2) { if (n < cap) mine[n] = make_key(d0, __float_as_int(p0.w)); ++n; }
+                if (d1 < r2) { if (n < cap) mine[n] = make_key(d1, __float_as_int(p1.w)); ++n; }
             }
             if (j < e) {
                 const float4 p = __ldg(&rows[j]);
@@ -130,8 +141,11 @@ __device__ __forceinline__ void top_keys(const unsigned long long* list, int cnt
 
 constexpr int kEmitClasses = 10;  // 16-key batch counts 0..8 (lists up to 128), and overflow
 
+// At most 102 registers (5 blocks of 128 threads per SM): the few spills this
+// costs in the batch loop are cheaper than 4 blocks' latency hiding (B200,
+// cfg2: 0.314 against 0.336 ms).
 template <int KN>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(128, 5)
     emit_lists_kernel(const unsigned long long* __restrict__ lists, const int* __restrict__ counts,
                       const int* __restrict__ map, int q0, int n, int K, int cap, float r2,
                       int* __restrict__ oidx, float* __restrict__ odist) {
@@ -181,11 +195,11 @@ __global__ void __launch_bounds__(128)
 
 cudaError_t launch_collect_d3(const float* rows, const int* starts, const GridPlan& P, float r2,
                               int cap, unsigned long long* lists, int* counts, int* overflow,
-                              int* n_overflow, int q0, int q1, cudaStream_t s) {
+                              int* n_overflow, int q0, int q1, cudaStream_t s, const float* qrows) {
     if (q1 <= q0) return cudaSuccess;
-    collect_d3_kernel<<<(q1 - q0 + 255) / 256, 256, 0, s>>>(reinterpret_cast<const float4*>(rows),
-                                                            starts, P, r2, cap, lists, counts,
-                                                            overflow, n_overflow, q0, q1);
+    collect_d3_kernel<<<(q1 - q0 + 255) / 256, 256, 0, s>>>(
+        reinterpret_cast<const float4*>(rows), starts, P, r2, cap, lists, counts, overflow, n_overflow,
+        q0, q1, reinterpret_cast<const float4*>(qrows ? qrows : rows));
     return cudaGetLastError();
 }
 

@@ -229,7 +229,10 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
                      int* __restrict__ oidx, float* __restrict__ odist, long long ostride,
                      const int* __restrict__ scatter_ids, const int* __restrict__ qlist,
                      const int* __restrict__ qcount, long long row_base,
-                     const float4* __restrict__ proj) {
+                     const float4* __restrict__ proj, const float4* __restrict__ queries,
+                     const float4* __restrict__ qproj) {
+    // queries / qproj: the queries' rows and projected coordinates (a
+    // separate query set in the same grid's cell order, or the points' own)
     extern __shared__ __align__(16) unsigned char smem[];
     if (qcount) q1 = min(q1, q0 + __ldg(qcount));  // list length known only on the device
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -252,14 +255,14 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
     const long long mysq = lane < nq ? (qlist ? __ldg(&qlist[base + lane]) : base + lane) : 0;
 #pragma unroll
     for (int v = 0; v < NV; ++v)
-        myq[v] = lane < nq ? __ldg(&rows[mysq * NV + v]) : make_float4(0, 0, 0, 0);
+        myq[v] = lane < nq ? __ldg(&queries[mysq * NV + v]) : make_float4(0, 0, 0, 0);
     {
         // grid coordinates: the leading coordinates of the row, or the
         // query's projected (principal-axis) coordinates
         long long c = 0;
 #pragma unroll
         for (int a = 0; a < G; ++a) {
-            const float4 f = proj ? __ldg(&proj[mysq * (kProjStride / 4) + (a >> 2)]) : myq[a >> 2];
+            const float4 f = qproj ? __ldg(&qproj[mysq * (kProjStride / 4) + (a >> 2)]) : myq[a >> 2];
             const float x = (a & 3) == 0 ? f.x : (a & 3) == 1 ? f.y : (a & 3) == 2 ? f.z : f.w;
             mygc[a] = cell_coord(x, P.origin[a], P.inv_cell, P.res[a]);
             c += (long long)mygc[a] * P.stride[a];

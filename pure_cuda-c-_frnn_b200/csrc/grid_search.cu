@@ -71,6 +71,8 @@ struct CoopArgs {
     const int* qcount;
     long long row_base;
     const float* proj;
+    const float* qrows;
+    const float* qproj;
 };
 
 template <int NV, int G, bool D3>
@@ -83,7 +85,8 @@ cudaError_t launch_coop(const CoopArgs& a, cudaStream_t s) {
     coop::grid_coop_kernel<NV, G, D3><<<blocks, coop::kWarps * 32, smem, s>>>(
         reinterpret_cast<const float4*>(a.rows), a.ids, a.starts, a.P, a.K, a.r2, a.q0, a.q1, a.oidx,
         a.odist, a.ostride, a.scatter_ids, a.qlist, a.qcount, a.row_base,
-        reinterpret_cast<const float4*>(a.proj));
+        reinterpret_cast<const float4*>(a.proj), reinterpret_cast<const float4*>(a.qrows ? a.qrows : a.rows),
+        reinterpret_cast<const float4*>(a.qrows ? a.qproj : a.proj));
     return cudaGetLastError();
 }
 
@@ -93,10 +96,11 @@ cudaError_t launch_grid_search(const float* rows, const int* ids, const int* sta
                                const GridPlan& P, int K, float r2, int q0, int q1, int* oidx,
                                float* odist, long long ostride, const int* scatter_ids,
                                cudaStream_t s, const int* qlist, const int* qcount,
-                               long long row_base, const float* proj) {
+                               long long row_base, const float* proj, const float* qrows,
+                               const float* qproj) {
     if (q1 <= q0) return cudaSuccess;
     const CoopArgs a{rows, ids, starts, P, K, r2, q0, q1, oidx, odist, ostride, scatter_ids,
-                     qlist, qcount, row_base < 0 ? (long long)q0 : row_base, proj};
+                     qlist, qcount, row_base < 0 ? (long long)q0 : row_base, proj, qrows, qproj};
     if (P.dim == 3 && P.g == 3 && !proj) return launch_coop<1, 3, true>(a, s);
     // (row float4s, grid axes) pairs the planner produces: leading coordinates
     // G = min(D, 4); principal axes (D > 4) G in 2..6

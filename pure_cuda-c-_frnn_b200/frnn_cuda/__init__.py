@@ -63,6 +63,7 @@ def load_library() -> ctypes.CDLL:
         "frnn_search_gpu_async": (I, [P, P, I, I, I, F, ctypes.POINTER(P), ctypes.POINTER(P)]),
         "frnn_search_gpu_part": (I, [P, P, I, I, I, F, I, I, ctypes.POINTER(I), ctypes.POINTER(P),
                                      ctypes.POINTER(P), ctypes.POINTER(P)]),
+        "frnn_search_gpu_queries": (I, [P, P, I, P, I, I, I, F, ctypes.POINTER(P), ctypes.POINTER(P)]),
         "frnn_search": (I, [P, P, L, I, F, P, P]),
         "frnn_search_host_soa": (I, [P, P, I, I, I, F, P, P]),
         "frnn_get_results": (I, [P, I, I, P, P]),
@@ -212,6 +213,20 @@ class FRNNEngine:
                                              ctypes.byref(pd))
         self._check(st, "search_gpu_async")
         return int(pi.value), int(pd.value)
+
+    def search_gpu_queries(self, points_ptr: int, N: int, queries_ptr: int, M: int, dim: int, K: int,
+                           radius: float):
+        """A separate query set (frnn_search_gpu_queries): M SoA queries at
+        ``queries_ptr`` against the N SoA points at ``points_ptr``.  Returns
+        device pointers to SoA ``[k*M + q]`` results (engine-owned);
+        ``get_results(M, K)`` copies them."""
+        pi, pd = ctypes.c_void_p(), ctypes.c_void_p()
+        self._check(self._lib.frnn_search_gpu_queries(self._eng, ctypes.c_void_p(int(points_ptr)), int(N),
+                                                      ctypes.c_void_p(int(queries_ptr)), int(M), int(dim),
+                                                      int(K), float(radius), ctypes.byref(pi),
+                                                      ctypes.byref(pd)),
+                    "search_gpu_queries")
+        return pi.value, pd.value
 
     def search_gpu_part(self, dev_ptr: int, N: int, dim: int, K: int, radius: float, part: int,
                         nparts: int):

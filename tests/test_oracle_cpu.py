@@ -176,3 +176,31 @@ def test_calibration_hits_target_on_small_cloud():
     q = rng.choice(len(P), 256, replace=False)
     cnt = [(((P - P[i]) ** 2).sum(1) <= r * r).sum() for i in q]
     assert 18 < np.mean(cnt) < 30
+
+
+@pytest.mark.parametrize("D", [3, 7, 40])
+def test_oracle_query_set(oracle_mod, D):
+    oracle = oracle_mod
+    # queries identical to the points reproduce the self-search bit for bit;
+    # a separate query set matches a float64 brute force (boundary cases and
+    # ties at the K-th distance aside)
+    rng = np.random.default_rng(D)
+    N, M, K = 3000, 900, 12
+    P = rng.random((D, N), dtype=np.float64).astype(np.float32)
+    r = 0.25 if D == 3 else (0.6 if D == 7 else 1.6)
+    a = oracle.search(P, K, r)
+    b = oracle.search_queries(P, P, K, r)
+    assert np.array_equal(a[0], b[0]) and np.array_equal(a[1].view(np.int32), b[1].view(np.int32))
+    Q = (rng.random((D, M)) * 1.2 - 0.1).astype(np.float32)
+    idx, dist, _ = oracle.search_queries(P, Q, K, r)
+    d2 = ((Q.T.astype(np.float64)[:, None, :] - P.T.astype(np.float64)[None, :, :]) ** 2).sum(-1)
+    r2 = float(np.float32(r) * np.float32(r))
+    for t in range(M):
+        row = d2[t]
+        inside = np.where(row < r2 * (1 - 1e-5))[0]
+        near = np.abs(row - r2) <= r2 * 1e-5
+        got = idx[:, t][idx[:, t] >= 0]
+        if len(inside) + near.sum() <= K:
+            assert set(inside) <= set(got) <= set(inside) | set(np.where(near)[0])
+        else:
+            assert len(got) == K
