@@ -60,6 +60,18 @@ __global__ void __launch_bounds__(256)
             // clamped to [0, n): a corrupt start table never reads out of bounds
             int j = min(max(__ldg(&starts[rb + xlo]), 0), P.n);
             const int e = min(max(__ldg(&starts[rb + xhi + 1]), j), P.n);
+            // eight row loads in flight per pass (B200, cfg2: 0.302 ms, against
+            // 0.316 with four and 0.340 with two), then the tail
+            for (; j + 7 < e; j += 8) {
+                float4 p[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) p[u] = __ldg(&rows[j + u]);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const float d = dist2_d3(q.x, q.y, q.z, p[u].x, p[u].y, p[u].z);
+                    if (d < r2) { if (n < cap) mine[n] = make_key(d, __float_as_int(p[u].w)); ++n; }
+                }
+            }
             for (; j + 3 < e; j += 4) {
                 const float4 p0 = __ldg(&rows[j]);
                 const float4 p1 = __ldg(&rows[j + 1]);
