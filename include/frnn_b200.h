@@ -127,6 +127,22 @@ int frnn_search_gpu_async(frnn_engine* e, const float* d_points_soa, int N, int 
 int frnn_search_gpu_queries(frnn_engine* e, const float* d_points_soa, int N, const float* d_queries_soa, int M,
                             int dim, int K, float radius, int** d_idxs, float** d_dists);
 
+/* Grid reuse: build once, query many.  frnn_build_grid plans and builds the
+ * search structure for N points and a radius (on the grid path: the cell
+ * plan, principal axes if chosen, and the cell-sorted points); every
+ * frnn_query_grid call then searches a query set (SoA d_queries_soa[d*M + q],
+ * the points' dim) against it with its own K, exactly like
+ * frnn_search_gpu_queries, without rebuilding.  On the brute-force paths
+ * nothing is built and each query call reads the points again, so they must
+ * stay valid; the grid path does not read them after the build.  Any other
+ * search on the engine (frnn_search_gpu, _queries, _part, frnn_search)
+ * discards the built grid; frnn_query_grid then returns FRNN_ERR_STATE.  Results
+ * SoA [k*M + q] in engine-owned buffers; frnn_get_results(e, M, K) copies them.
+ * No counterpart in the reference engine, which rebuilds its grid on every
+ * search (python_interface/frnn_engine.cu:195-250).  Blocking. */
+int frnn_build_grid(frnn_engine* e, const float* d_points_soa, int N, int dim, float radius);
+int frnn_query_grid(frnn_engine* e, const float* d_queries_soa, int M, int K, int** d_idxs, float** d_dists);
+
 /* Part of a search, for sharding the queries of one cloud over several
  * engines (one per GPU).  No counterpart in the reference, whose engine only
  * searches whole clouds; SURVEY-style query sharding splits the reference's

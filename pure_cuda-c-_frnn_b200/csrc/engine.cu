@@ -76,6 +76,16 @@ struct frnn_engine {
     DevBuf q_tiles, q_rows32, q_qa, q_pb;
     void* h_pca = nullptr;    // pinned, 32 KiB
     int grid_axes_mode = 0;   // FRNN_OPT_GRID_AXES
+    // a point set kept for frnn_query_grid: on the grid path its sorted rows,
+    // ids, cell starts (and projected coordinates) stay in the point buffers
+    struct {
+        bool valid = false;
+        const float* pts = nullptr;
+        int N = 0, dim = 0, path = 0;
+        float radius = 0.0f;
+        bool principal = false;
+        GridPlan P{};
+    } built;
     int last_principal = 0;   // the last grid was on principal axes
     int last_part_rows = -1;  // rows of the last part search (-1: last search was whole)
     float* h_box = nullptr;   // pinned, 9 floats
@@ -820,18 +830,16 @@ int sort_into_cells(frnn_engine* e, const float* pts, const GridPlan& P, const f
 // Grid search of a separate query set against the points: the queries are
 // sorted into the points' grid (the same plan) so that neighbouring queries
 // read the same candidate rows; results out[k*M + q] in query order.
-int run_grid_queries(frnn_engine* e, const float* d_pts, int N, const float* d_q, int M, int dim, int K,
-                     float r2, const GridPlan& P, const float* proj_p, const float* proj_q, int* out_idx,
-                     float* out_dist) {
+// The second half: the points are already sorted into P's cells (rows, ids,
+// starts, and their projected coordinates when proj_p).
+int search_sorted_queries(frnn_engine* e, const float* d_q, int M, int K, float r2, const GridPlan& P,
+                          bool proj_p, const float* proj_q, int* out_idx, float* out_dist) {
     cudaStream_t s = e->stream;
-    stage_begin(e, ST_HASH);
-    int st = sort_into_cells(e, d_pts, P, proj_p, e->counts, e->starts, e->cellrank, e->rows, e->ids, nullptr,
-                             &e->proj_s);
-    if (st != FRNN_OK) return st;
     GridPlan Pq = P;
     Pq.n = M;
-    st = sort_into_cells(e, d_q, Pq, proj_q, e->q_counts, e->q_starts, e->q_cellrank, e->q_rows, e->q_ids,
-                         &e->q_inv, &e->q_proj_s);
+    stage_begin(e, ST_HASH);
+    int st = sort_into_cells(e, d_q, Pq, proj_q, e->q_counts, e->q_starts, e->q_cellrank, e->q_rows, e->q_ids,
+                             &e->q_inv, &e->q_proj_s);
     if (st != FRNN_OK) return st;
     stage_end(e, ST_HASH);
     const float* proj_s = proj_p ? e->proj_s.as<float>() : nullptr;
@@ -888,6 +896,67 @@ int run_grid_queries(frnn_engine* e, const float* d_pts, int N, const float* d_q
     return FRNN_OK;
 }
 
+int run_grid_queries(frnn_engine* e, const float* d_pts, int N, const float* d_q, int M, int dim, int K,
+                     float r2, const GridPlan& P, const float* proj_p, const float* proj_q, int* out_idx,
+                     float* out_dist) {
+    stage_begin(e, ST_SCATTER);
+    int st = sort_into_cells(e, d_pts, P, proj_p, e->counts, e->starts, e->cellrank, e->rows, e->ids, nullptr,
+                             &e->proj_s);
+    if (st != FRNN_OK) return st;
+    stage_end(e, ST_SCATTER);
+    return search_sorted_queries(e, d_q, M, K, r2, P, proj_p != nullptr, proj_q, out_idx, out_dist);
+}
+
+// Checks a query set for NaN/Inf (the grid's leading coordinates; all of them
+// through the projection when the grid is on principal axes) and projects it
+// on the principal axes planned for the points.
+int prepare_queries(frnn_engine* e, const float* d_q, int M, int dim, bool principal) {
+    cudaStream_t s = e->stream;
+    const int g = grid_axes_for(dim);
+    const int blocks = std::min(bbox_blocks(M, e->sms), kBoxMaxBlocks);
+    FRNN_GROW(e, e->q_box_out, 64);
+    FRNN_CHECK(e, launch_bbox(d_q, M, g, e->box_partial.as<float>(), e->box_ticket.as<unsigned>(),
+                              e->q_box_out.as<float>(), blocks, s),
+               "query bbox launch");
+    e->launches++;
+    float* hqb = static_cast<float*>(e->h_pca) + 6144;
+    FRNN_CHECK(e, cudaMemcpyAsync(hqb, e->q_box_out.p, 9 * sizeof(float), cudaMemcpyDeviceToHost, s),
+               "query bbox readback");
+    FRNN_CHECK(e, cudaStreamSynchronize(s), "query bbox sync");
+    if (hqb[8] != 0.0f) return fail(e, FRNN_ERR_INVALID_ARG, "queries contain NaN or Inf coordinates");
+    if (!principal) return FRNN_OK;
+    const int axes = std::min(dim, kMaxGridAxes);
+    const int pslots = pca_project_slots();
+    FRNN_GROW(e, e->q_proj_u, (size_t)M * kProjStride * 4);
+    FRNN_GROW(e, e->q_proj_partial, (size_t)blocks * pslots * 4);
+    FRNN_GROW(e, e->q_proj_out, 64 * 4);
+    FRNN_CHECK(e, launch_pca_project(d_q, M, dim, axes, e->pca_mu.as<float>(), e->pca_pm.as<float>(),
+                                     e->q_proj_u.as<float>(), e->q_proj_partial.as<float>(),
+                                     e->proj_ticket.as<unsigned>(), e->q_proj_out.as<float>(), blocks, s),
+               "query project launch");
+    e->launches++;
+    float* hqp = static_cast<float*>(e->h_pca) + 6400;
+    FRNN_CHECK(e, cudaMemcpyAsync(hqp, e->q_proj_out.p, (size_t)pslots * 4, cudaMemcpyDeviceToHost, s),
+               "query projection readback");
+    FRNN_CHECK(e, cudaStreamSynchronize(s), "query projection sync");
+    if (hqp[pslots - 1] != 0.0f) return fail(e, FRNN_ERR_INVALID_ARG, "queries contain NaN or Inf coordinates");
+    return FRNN_OK;
+}
+
+// Blocking end of a search: the bounded device waits' error flag.
+int finish_search(frnn_engine* e) {
+    cudaStream_t s = e->stream;
+    FRNN_CHECK(e, cudaMemcpyAsync(e->h_err, e->err_flag.p, sizeof(int), cudaMemcpyDeviceToHost, s),
+               "error flag readback");
+    FRNN_CHECK(e, cudaStreamSynchronize(s), "search sync");
+    if (*e->h_err != 0) {
+        cudaMemsetAsync(e->err_flag.p, 0, sizeof(int), s);
+        cudaStreamSynchronize(s);
+        return fail(e, FRNN_ERR_TIMEOUT, "a bounded device-side wait gave up");
+    }
+    return FRNN_OK;
+}
+
 // A separate query set (M points, SoA) against the N points: the same paths
 // and arithmetic as the self-query; results out[k*M + q].
 int search_queries_core(frnn_engine* e, const float* d_pts, int N, const float* d_q, int M, int dim, int K,
@@ -900,6 +969,7 @@ int search_queries_core(frnn_engine* e, const float* d_pts, int N, const float* 
     float* out_dist = e->out_dist.as<float>();
     e->last_N = -1;
     e->last_part_rows = -1;
+    e->built.valid = false;  // the point buffers are about to be overwritten
     for (int i = 0; i < FRNN_STAGES; ++i) e->stage_used[i] = false;
     int path = e->forced_path;
     if (path == FRNN_PATH_AUTO) {
@@ -1018,6 +1088,7 @@ int search_core(frnn_engine* e, const float* d_pts, int N, int dim, int K, float
     float* out_dist = e->out_dist.as<float>();
     e->last_N = -1;
     e->last_part_rows = -1;
+    e->built.valid = false;  // the point buffers are about to be overwritten
 
     for (int i = 0; i < FRNN_STAGES; ++i) e->stage_used[i] = false;
     int path = e->forced_path;
@@ -1298,6 +1369,109 @@ int frnn_search_gpu_queries(frnn_engine* e, const float* d_points_soa, int N, co
     if (st != FRNN_OK) return st;
     st = search_queries_core(e, d_points_soa, N, d_queries_soa, M, dim, K, radius);
     if (st != FRNN_OK) return st;
+    *d_idxs = e->out_idx.as<int>();
+    *d_dists = e->out_dist.as<float>();
+    return FRNN_OK;
+}
+
+int frnn_build_grid(frnn_engine* e, const float* d_points_soa, int N, int dim, float radius) {
+    int st = check_search_args(e, d_points_soa, N, dim, 1, radius);
+    if (st != FRNN_OK) return st;
+    DeviceGuard g(e->device);
+    st = check_device_ptr(e, d_points_soa);
+    if (st != FRNN_OK) return st;
+    cudaStream_t s = e->stream;
+    e->built.valid = false;
+    e->last_N = -1;
+    e->last_part_rows = -1;
+    for (int i = 0; i < FRNN_STAGES; ++i) e->stage_used[i] = false;
+    int path = e->forced_path;
+    if (path == FRNN_PATH_AUTO)
+        path = dim > 32 ? (N >= kTcMinPoints ? FRNN_PATH_BRUTE_TC : FRNN_PATH_BRUTE) : FRNN_PATH_GRID;
+    if (path == FRNN_PATH_GRID && dim > 32) path = FRNN_PATH_BRUTE;
+    GridPlan P{};
+    bool principal = false;
+    if (path == FRNN_PATH_GRID) {
+        const int blocks = std::min(bbox_blocks(N, e->sms), kBoxMaxBlocks);
+        stage_begin(e, ST_BBOX);
+        FRNN_CHECK(e, launch_bbox(d_points_soa, N, grid_axes_for(dim), e->box_partial.as<float>(),
+                                  e->box_ticket.as<unsigned>(), e->box_out.as<float>(), blocks, s),
+                   "bbox launch");
+        stage_end(e, ST_BBOX);
+        e->launches++;
+        FRNN_CHECK(e, cudaMemcpyAsync(e->h_box, e->box_out.p, 9 * sizeof(float), cudaMemcpyDeviceToHost, s),
+                   "bbox readback");
+        FRNN_CHECK(e, cudaStreamSynchronize(s), "bbox sync");
+        if (e->h_box[8] != 0.0f) return fail(e, FRNN_ERR_INVALID_ARG, "points contain NaN or Inf coordinates");
+        bool ok = make_plan(e->h_box, N, dim, radius, P);
+        if (dim > 4 && dim <= kMaxPcaDim && e->grid_axes_mode != FRNN_GRID_AXES_LEADING) {
+            st = plan_principal(e, d_points_soa, N, dim, radius, ok, P, &principal);
+            if (st != FRNN_OK) return st;
+            ok |= principal;
+        }
+        if (!ok) {
+            path = FRNN_PATH_BRUTE;
+        } else {
+            stage_begin(e, ST_SCATTER);
+            st = sort_into_cells(e, d_points_soa, P, principal ? e->proj_u.as<float>() : nullptr, e->counts,
+                                 e->starts, e->cellrank, e->rows, e->ids, nullptr, &e->proj_s);
+            if (st != FRNN_OK) return st;
+            stage_end(e, ST_SCATTER);
+            st = finish_search(e);
+            if (st != FRNN_OK) return st;
+        }
+    }
+    e->built.pts = d_points_soa;
+    e->built.N = N;
+    e->built.dim = dim;
+    e->built.radius = radius;
+    e->built.path = path;
+    e->built.principal = principal;
+    e->built.P = P;
+    e->built.valid = true;
+    return FRNN_OK;
+}
+
+int frnn_query_grid(frnn_engine* e, const float* d_queries_soa, int M, int K, int** d_idxs, float** d_dists) {
+    if (!e) return FRNN_ERR_INVALID_ARG;
+    if (!e->built.valid)
+        return fail(e, FRNN_ERR_STATE, "no grid: call frnn_build_grid first (any other search discards it)");
+    if (K < 1 || K > kMaxK) return fail(e, FRNN_ERR_INVALID_ARG, "K must be in [1, 128]");
+    if (!d_queries_soa || M < 1) return fail(e, FRNN_ERR_INVALID_ARG, "queries must be a device array of M >= 1 points");
+    if (!d_idxs || !d_dists) return fail(e, FRNN_ERR_INVALID_ARG, "output pointers are null");
+    DeviceGuard g(e->device);
+    int st = check_device_ptr(e, d_queries_soa);
+    if (st != FRNN_OK) return st;
+    const auto b = e->built;
+    if (b.path != FRNN_PATH_GRID) {
+        // brute force keeps nothing between calls: search the kept points
+        const int forced = e->forced_path;
+        e->forced_path = b.path;
+        st = search_queries_core(e, b.pts, b.N, d_queries_soa, M, b.dim, K, b.radius);
+        e->forced_path = forced;
+        e->built = b;  // the point set stays kept
+        if (st != FRNN_OK) return st;
+    } else {
+        FRNN_GROW(e, e->out_idx, (size_t)M * K * 4);
+        FRNN_GROW(e, e->out_dist, (size_t)M * K * 4);
+        e->last_N = -1;
+        e->last_part_rows = -1;
+        for (int i = 0; i < FRNN_STAGES; ++i) e->stage_used[i] = false;
+        st = prepare_queries(e, d_queries_soa, M, b.dim, b.principal);
+        if (st != FRNN_OK) return st;
+        st = search_sorted_queries(e, d_queries_soa, M, K, b.radius * b.radius, b.P, b.principal,
+                                   b.principal ? e->q_proj_u.as<float>() : nullptr, e->out_idx.as<int>(),
+                                   e->out_dist.as<float>());
+        if (st != FRNN_OK) return st;
+        st = finish_search(e);
+        if (st != FRNN_OK) return st;
+        e->last_path = FRNN_PATH_GRID;
+        e->last_principal = b.principal;
+        e->last_g = b.P.g;
+        e->last_cells = b.P.cells;
+        e->last_N = M;
+        e->last_K = K;
+    }
     *d_idxs = e->out_idx.as<int>();
     *d_dists = e->out_dist.as<float>();
     return FRNN_OK;

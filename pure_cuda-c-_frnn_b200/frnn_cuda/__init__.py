@@ -64,6 +64,8 @@ def load_library() -> ctypes.CDLL:
         "frnn_search_gpu_part": (I, [P, P, I, I, I, F, I, I, ctypes.POINTER(I), ctypes.POINTER(P),
                                      ctypes.POINTER(P), ctypes.POINTER(P)]),
         "frnn_search_gpu_queries": (I, [P, P, I, P, I, I, I, F, ctypes.POINTER(P), ctypes.POINTER(P)]),
+        "frnn_build_grid": (I, [P, P, I, I, F]),
+        "frnn_query_grid": (I, [P, P, I, I, ctypes.POINTER(P), ctypes.POINTER(P)]),
         "frnn_search": (I, [P, P, L, I, F, P, P]),
         "frnn_search_host_soa": (I, [P, P, I, I, I, F, P, P]),
         "frnn_get_results": (I, [P, I, I, P, P]),
@@ -226,6 +228,22 @@ class FRNNEngine:
                                                       int(K), float(radius), ctypes.byref(pi),
                                                       ctypes.byref(pd)),
                     "search_gpu_queries")
+        return pi.value, pd.value
+
+    def build_grid(self, points_ptr: int, N: int, dim: int, radius: float) -> None:
+        """Build the search structure for N SoA points once (frnn_build_grid);
+        query sets then go through ``query_grid``.  Any other search discards it."""
+        self._check(self._lib.frnn_build_grid(self._eng, ctypes.c_void_p(int(points_ptr)), int(N), int(dim),
+                                              float(radius)),
+                    "build_grid")
+
+    def query_grid(self, queries_ptr: int, M: int, K: int):
+        """Search M SoA queries against the built grid (frnn_query_grid);
+        returns device pointers to SoA ``[k*M + q]`` results."""
+        pi, pd = ctypes.c_void_p(), ctypes.c_void_p()
+        self._check(self._lib.frnn_query_grid(self._eng, ctypes.c_void_p(int(queries_ptr)), int(M), int(K),
+                                              ctypes.byref(pi), ctypes.byref(pd)),
+                    "query_grid")
         return pi.value, pd.value
 
     def search_gpu_part(self, dev_ptr: int, N: int, dim: int, K: int, radius: float, part: int,

@@ -107,3 +107,35 @@ def test_query_set_rejects_bad_arguments(frnn):
     pts = torch.rand(3, 100, device="cuda")
     with pytest.raises(ValueError):
         eng.search_gpu_queries(pts.data_ptr(), 100, qn.data_ptr(), 10, 3, 4, 0.2)
+
+
+@pytest.mark.parametrize("kind,D,N,path", [("uniform", 3, 30000, "grid"), ("lowrank6", 16, 20000, "grid"),
+                                           ("mixture", 5, 20000, "grid"), ("sphere", 64, 5000, "brute_tc")])
+def test_build_once_query_many(frnn, oracle_mod, kind, D, N, path):
+    pts = datagen.generate(kind, N, D, seed=N + 2 * D)
+    r = datagen.calibrate_radius(pts, 20, sample=512, seed=4)
+    eng = frnn.FRNNEngine(max_points=N)
+    xp = torch.from_numpy(datagen.soa(pts)).cuda()
+    eng.build_grid(xp.data_ptr(), N, D, r)
+    for t, (M, K) in enumerate([(7000, 16), (2500, 40), (9000, 1)]):
+        q = queries_for(pts, M, r, seed=10 * D + t)
+        xq = torch.from_numpy(datagen.soa(q)).cuda()
+        eng.query_grid(xq.data_ptr(), M, K)
+        i, d = eng.get_results_arrays(M, K)
+        assert eng.last_plan()["path"] == path
+        oi, od, _ = oracle_mod.search_queries(datagen.soa(pts), datagen.soa(q), K, r)
+        assert_bit_exact(i, d, oi, od, f"{kind} D={D} M={M} K={K}")
+
+
+def test_other_search_discards_the_built_grid(frnn):
+    N, D = 20000, 3
+    pts = torch.rand(D, N, device="cuda")
+    q = torch.rand(D, 100, device="cuda")
+    eng = frnn.FRNNEngine(max_points=N)
+    with pytest.raises(frnn.FRNNError):
+        eng.query_grid(q.data_ptr(), 100, 4)
+    eng.build_grid(pts.data_ptr(), N, D, 0.02)
+    eng.query_grid(q.data_ptr(), 100, 4)
+    eng.search_gpu(pts.data_ptr(), N, D, 4, 0.02)
+    with pytest.raises(frnn.FRNNError):
+        eng.query_grid(q.data_ptr(), 100, 4)
