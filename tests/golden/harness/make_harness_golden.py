@@ -3,12 +3,12 @@
 Run in a container that has the reference checkout (it is not needed to run the
 tests):
 
-    python tests/golden/make_harness_golden.py /path/to/reference
+    python tests/golden/harness/make_harness_golden.py /path/to/reference
 
 It compiles only the definitions of gen_points, radius_for and calibrate_radius
 from Tests/scripts/benchmark_vs_libfrnn.py (the module's top level, which runs
 the GPU sweep, is not executed), evaluates them on small seeded cases and writes
-tests/golden/harness_golden.npz.
+tests/golden/harness/harness_golden.npz.
 """
 
 import ast

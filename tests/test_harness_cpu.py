@@ -2,7 +2,7 @@
 
 tests/golden/harness_golden.npz holds the outputs of the reference's
 gen_points, calibrate_radius and radius_for on small seeded cases
-(tests/golden/make_harness_golden.py); the restated functions must reproduce
+(tests/golden/harness/make_harness_golden.py); the restated functions must reproduce
 them exactly.  The sweep driver is run with a fake search to check the JSON
 shape."""
 
@@ -14,7 +14,7 @@ import pytest
 
 from frnn_cuda import harness
 
-GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "harness_golden.npz")
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "harness", "harness_golden.npz")
 
 
 @pytest.fixture(scope="module")
