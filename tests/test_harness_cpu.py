@@ -1,6 +1,6 @@
 """frnn_cuda.harness against the reference benchmark script's own functions.
 
-tests/golden/harness_golden.npz holds the outputs of the reference's
+tests/golden/harness/harness_golden.npz holds the outputs of the reference's
 gen_points, calibrate_radius and radius_for on small seeded cases
 (tests/golden/harness/make_harness_golden.py); the restated functions must reproduce
 them exactly.  The sweep driver is run with a fake search to check the JSON
