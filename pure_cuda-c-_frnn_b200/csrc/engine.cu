@@ -289,7 +289,8 @@ int row_floats(int dim) {
 // Plan a grid on g axes whose bounding box is box[2d], box[2d+1]; `extra` is
 // an absolute allowance added to the cell edge (the rounding bound of
 // projected coordinates; 0 for the data's own coordinates).
-bool make_plan_axes(const float* box, int g, int N, int dim, float radius, double extra, GridPlan& P) {
+bool make_plan_axes(const float* box, int g, int N, int dim, float radius, double extra, GridPlan& P,
+                    long long cells_per_point = 32) {
     double ext_max = 0.0, mag = 0.0;
     for (int d = 0; d < g; ++d) {
         double lo = box[2 * d], hi = box[2 * d + 1];
@@ -301,10 +302,11 @@ bool make_plan_axes(const float* box, int g, int N, int dim, float radius, doubl
     // (|error| of (x-origin)*inv_cell is a few ulps of the cell index).
     const double u = 1.0 / 16777216.0;
     double cell = (double)radius * (1.0 + 1e-5 + 8.0 * u * (ext_max / radius + 2.0)) + extra;
-    // Dense cell table budget: 32 cells per point (12 bytes of build traffic
-    // per cell); sparse clouds such as Gaussian mixtures leave most cells
-    // empty, and coarser cells would multiply the candidates of every query.
-    const long long budget = std::min<long long>(std::max<long long>(1LL << 22, 32LL * N),
+    // Dense cell table budget: 32 cells per point by default (12 bytes of
+    // build traffic per cell); sparse clouds such as Gaussian mixtures leave
+    // most cells empty, and coarser cells would multiply the candidates of
+    // every query.
+    const long long budget = std::min<long long>(std::max<long long>(1LL << 22, cells_per_point * N),
                                                  (1LL << 31) - 2);
     long long res[kMaxGridAxes];
     long long cells = 1;
@@ -357,6 +359,8 @@ bool make_plan_axes(const float* box, int g, int N, int dim, float radius, doubl
 bool make_plan(const float* box, int N, int dim, float radius, GridPlan& P) {
     return make_plan_axes(box, grid_axes_for(dim), N, dim, radius, 0.0, P);
 }
+
+constexpr long long kPrincipalCellsPerPoint = 128;
 
 // Eigen-decomposition of a symmetric n x n matrix (row-major, destroyed) by
 // cyclic Jacobi rotations in double: w[i] eigenvalues, column i of V (row-major
@@ -485,7 +489,10 @@ int plan_principal(frnn_engine* e, const float* d_pts, int N, int dim, float rad
     const double extra = 2.0 * (dim + 2) * std::ldexp(nmax, -24) + (double)radius * std::ldexp(1.0, -20);
     GridPlan cand[kMaxGridAxes + 1];
     bool ok[kMaxGridAxes + 1] = {};
-    for (int g = 2; g <= axes; ++g) ok[g] = make_plan_axes(hbox, g, N, dim, radius, extra, cand[g]);
+    // principal-axis grids serve D > 4 clouds, whose search costs far more
+    // than the build: a finer table (up to 128 cells per point) is worth it
+    for (int g = 2; g <= axes; ++g)
+        ok[g] = make_plan_axes(hbox, g, N, dim, radius, extra, cand[g], kPrincipalCellsPerPoint);
 
     // sampled shell counts
     const int m = std::min(N, 16384), nq = std::min(m, 256);
