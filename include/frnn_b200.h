@@ -170,9 +170,10 @@ int frnn_search_host_soa(frnn_engine* e, const float* h_points_soa, int N, int d
 
 /* Tuning options (frnn_set_option). */
 enum frnn_option {
-    /* Result sets up to this many bytes (N*K*8) are written straight to
-     * original query order from the search kernel; larger ones are written in
-     * cell order and unpermuted one output row at a time.  Default 48 MiB. */
+    /* D = 3 searches with K > 32: result sets up to this many bytes (N*K*8)
+     * are written straight to original query order from the search kernel;
+     * larger ones are written in cell order and unpermuted one output row at
+     * a time.  Default 48 MiB.  Other searches always write directly. */
     FRNN_OPT_DIRECT_OUTPUT_MAX_BYTES = 1,
     /* Grid axes for D > 4 (FRNN_GRID_AXES_*).  The reference grids the first
      * coordinates (python_interface/frnn_engine.cu:64-102); the engine may

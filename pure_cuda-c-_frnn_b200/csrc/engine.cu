@@ -641,7 +641,9 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
                    "grid search launch");
         stage_end(e, ST_SEARCH);
         e->launches++;
-    } else if (out_bytes <= e->direct_output_max_bytes) {
+    } else if (out_bytes <= e->direct_output_max_bytes || P.dim > 3) {
+        // D > 3 always writes directly (B200, cfg3: 2.30 against 2.38 ms with
+        // the unpermute pass; cfg4 equal)
         stage_begin(e, ST_SEARCH);
         FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(), P, K,
                                          r2, 0, N, out_idx, out_dist, N, e->ids.as<int>(), s, nullptr,

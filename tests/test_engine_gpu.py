@@ -259,3 +259,19 @@ def test_dense_lists_overflow_to_cooperative_pass(frnn, oracle_mod, K):
     idx, dist, plan = run_engine(frnn, soa, K, 0.01, path="grid")
     oi, od, _ = oracle_mod.search(soa, K, 0.01)
     assert_bit_exact(idx, dist, oi, od, f"overflow K={K}")
+
+
+@pytest.mark.parametrize("limit", [0, 1 << 40])
+def test_d3_cooperative_unpermute_and_direct(frnn, oracle_mod, limit):
+    # D = 3 with K > 32 runs the cooperative kernel; results go through the
+    # unpermute pass when larger than FRNN_OPT_DIRECT_OUTPUT_MAX_BYTES
+    c = datagen.config(2)
+    pts, r = datagen.cloud(2, 30000)
+    soa = datagen.soa(pts)
+    eng = frnn.FRNNEngine(max_points=30000)
+    eng.set_option(eng.OPT_DIRECT_OUTPUT_MAX_BYTES, limit)
+    eng.set_timing(True)
+    idx, dist, plan = run_engine(frnn, soa, 48, r, path="grid", engine=eng)
+    assert ("unpermute" in eng.stage_times()) == (limit == 0)
+    oi, od, _ = oracle_mod.search(soa, 48, r)
+    assert_bit_exact(idx, dist, oi, od, f"K=48 limit={limit}")
