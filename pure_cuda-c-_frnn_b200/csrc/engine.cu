@@ -548,7 +548,8 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
     const long long tiles = scan_tiles(P.cells);
     FRNN_GROW(e, e->scan_status, (size_t)tiles * 8);
     FRNN_GROW(e, e->cellrank, (size_t)N * 8);
-    FRNN_GROW(e, e->rows, (size_t)N * P.row * 4);
+    // padded: the D = 3 collect kernel reads whole 8-row passes
+    FRNN_GROW(e, e->rows, ((size_t)N + kCollectRowPad) * P.row * 4);
     FRNN_GROW(e, e->ids, (size_t)N * 4);
 
     FRNN_CHECK(e, cudaMemsetAsync(e->counts.p, 0, (size_t)P.cells * 4, s), "memset counts");

@@ -48,10 +48,13 @@ cudaError_t launch_grid_search(const float* rows, const int* ids, const int* sta
                                const float* qproj = nullptr);
 
 // grid_collect.cu -- D = 3 two-kernel search (K <= 32).
+constexpr int kCollectRowPad = 8;
+
 // collect: for sorted queries sq in [q0, q1), every in-radius key goes to
 // lists[sq*cap + j]; counts[sq] = number found; queries with more than cap are
 // appended to overflow[0..*n_overflow).  qrows (optional): a separate query
-// set's rows in the grid's cell order.
+// set's rows in the grid's cell order.  rows must be readable kCollectRowPad
+// rows past P.n (the kernel loads whole 8-row passes and masks the excess).
 cudaError_t launch_collect_d3(const float* rows, const int* starts, const GridPlan& P, float r2,
                               int cap, unsigned long long* lists, int* counts, int* overflow,
                               int* n_overflow, int q0, int q1, cudaStream_t s,

@@ -30,6 +30,19 @@
 namespace frnn {
 namespace {
 
+// Appends the key (d, idx) to a list when ok, as a predicated store.  A list
+// that overflows keeps overwriting its last slot: its query is searched again
+// by the cooperative kernel, so the slot's content no longer matters.
+__device__ __forceinline__ void append_if(bool ok, unsigned long long* list, int& n, int cap, float d, int idx) {
+    unsigned long long* dst = list + min(n, cap - 1);
+    const unsigned long long key = make_key(d, idx);
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %2, 0;\n\t@p st.global.u64 [%0], %1;\n\t}" ::"l"(dst),
+        "l"(key), "r"((int)ok)
+        : "memory");
+    n += ok ? 1 : 0;
+}
+
 __global__ void __launch_bounds__(256)
     collect_d3_kernel(const float4* __restrict__ rows, const int* __restrict__ starts, GridPlan P,
                       float r2, int cap, unsigned long long* __restrict__ lists,
@@ -60,46 +73,19 @@ __global__ void __launch_bounds__(256)
             // clamped to [0, n): a corrupt start table never reads out of bounds
             int j = min(max(__ldg(&starts[rb + xlo]), 0), P.n);
             const int e = min(max(__ldg(&starts[rb + xhi + 1]), j), P.n);
-            // eight row loads in flight per pass (B200, cfg2: 0.302 ms, against
-            // 0.316 with four and 0.340 with two), then the tail
-            for (; j + 7 < e; j += 8) {
-                float4 p[8];
+            // one loop per span, eight row loads in flight per pass; the last pass
+            // reads up to seven rows past the span (the row array is padded by
+            // kCollectRowPad rows) and masks them.  Appends are predicated
+            // stores: no branch per candidate (B200, cfg2: 0.290 ms against
+            // 0.301 with 8/4/2/1-wide loops and branches around every append)
+            for (; j < e; j += kCollectRowPad) {
+                float4 p[kCollectRowPad];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) p[u] = __ldg(&rows[j + u]);
+                for (int u = 0; u < kCollectRowPad; ++u) p[u] = __ldg(&rows[j + u]);
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
+                for (int u = 0; u < kCollectRowPad; ++u) {
                     const float d = dist2_d3(q.x, q.y, q.z, p[u].x, p[u].y, p[u].z);
-                    if (d < r2) { if (n < cap) mine[n] = make_key(d, __float_as_int(p[u].w)); ++n; }
-                }
-            }
-            for (; j + 3 < e; j += 4) {
-                const float4 p0 = __ldg(&rows[j]);
-                const float4 p1 = __ldg(&rows[j + 1]);
-                const float4 p2 = __ldg(&rows[j + 2]);
-                const float4 p3 = __ldg(&rows[j + 3]);
-                const float d0 = dist2_d3(q.x, q.y, q.z, p0.x, p0.y, p0.z);
-                const float d1 = dist2_d3(q.x, q.y, q.z, p1.x, p1.y, p1.z);
-                const float d2 = dist2_d3(q.x, q.y, q.z, p2.x, p2.y, p2.z);
-                const float d3 = dist2_d3(q.x, q.y, q.z, p3.x, p3.y, p3.z);
-                if (d0 < r2) { if (n < cap) mine[n] = make_key(d0, __float_as_int(p0.w)); ++n; }
-                if (d1 < r2) { if (n < cap) mine[n] = make_key(d1, __float_as_int(p1.w)); ++n; }
-                if (d2 < r2) { if (n < cap) mine[n] = make_key(d2, __float_as_int(p2.w)); ++n; }
-                if (d3 < r2) { if (n < cap) mine[n] = make_key(d3, __float_as_int(p3.w)); ++n; }
-            }
-            for (; j + 1 < e; j += 2) {
-                const float4 p0 = __ldg(&rows[j]);
-                const float4 p1 = __ldg(&rows[j + 1]);
-                const float d0 = dist2_d3(q.x, q.y, q.z, p0.x, p0.y, p0.z);
-                const float d1 = dist2_d3(q.x, q.y, q.z, p1.x, p1.y, p1.z);
-                if (d0 < r2) { if (n < cap) mine[n] = make_key(d0, __float_as_int(p0.w)); ++n; }
-                if (d1 < r2) { if (n < cap) mine[n] = make_key(d1, __float_as_int(p1.w)); ++n; }
-            }
-            if (j < e) {
-                const float4 p = __ldg(&rows[j]);
-                const float d = dist2_d3(q.x, q.y, q.z, p.x, p.y, p.z);
-                if (d < r2) {
-                    if (n < cap) mine[n] = make_key(d, __float_as_int(p.w));
-                    ++n;
+                    append_if(j + u < e && d < r2, mine, n, cap, d, __float_as_int(p[u].w));
                 }
             }
         }
@@ -125,11 +111,45 @@ __device__ __forceinline__ void bitonic_merge(unsigned long long (&a)[N]) {
     }
 }
 
+__device__ __forceinline__ void cas_key(unsigned long long& x, unsigned long long& y) {
+    const unsigned long long u = x, v = y;
+    x = u < v ? u : v;
+    y = u < v ? v : u;
+}
+
+// Batcher's odd-even merge sort over a[LO, LO + N), N a power of two, unrolled
+// at compile time: 63 compare-exchanges for 16 keys, against 80 for the
+// bitonic network.  oe_merge merges the two sorted halves of a[LO, LO + N)
+// by comparing elements R apart.
+template <int S, int LO, int N, int R>
+__device__ __forceinline__ void oe_merge(unsigned long long (&a)[S]) {
+    constexpr int M = 2 * R;
+    if constexpr (M < N) {
+        oe_merge<S, LO, N, M>(a);
+        oe_merge<S, LO + R, N, M>(a);
+#pragma unroll
+        for (int i = LO + R; i + R < LO + N; i += M) cas_key(a[i], a[i + R]);
+    } else {
+        cas_key(a[LO], a[LO + R]);
+    }
+}
+template <int S, int LO, int N>
+__device__ __forceinline__ void oe_sort(unsigned long long (&a)[S]) {
+    if constexpr (N > 1) {
+        oe_sort<S, LO, N / 2>(a);
+        oe_sort<S, LO + N / 2, N / 2>(a);
+        oe_merge<S, LO, N, 1>(a);
+    }
+}
+
 // The KN smallest keys of list[0..cnt) ascending in registers, folded in
-// batches of 16 into an all-~0 start.  One sort-16 / merge-KN body for every
-// batch keeps the kernel's code small enough for the instruction cache (a
-// separate KN-wide first sort doubled it, and nearly every warp has a lane
-// with more than KN keys, so every warp ran both bodies).
+// batches of 16.  One sort-16 / merge-KN body for every batch keeps the
+// kernel's code small enough for the instruction cache (a separate KN-wide
+// first sort doubled it, and nearly every warp has a lane with more than KN
+// keys, so every warp ran both bodies).  The first batch, the same loop
+// iteration for every lane, fills the top keys directly instead of merging
+// into an empty set (B200, cfg2: emit 0.284 ms against 0.316 with a merge on
+// every batch and bitonic batch sorts).
 template <int KN>
 __device__ __forceinline__ void top_keys(const unsigned long long* list, int cnt,
                                          unsigned long long (&a)[KN]) {
@@ -139,7 +159,12 @@ __device__ __forceinline__ void top_keys(const unsigned long long* list, int cnt
         unsigned long long b[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) b[i] = base + i < cnt ? list[base + i] : ~0ull;
-        bitonic_sort<16>(b);
+        oe_sort<16, 0, 16>(b);
+        if (base == 0) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) a[i] = b[i];
+            continue;
+        }
         // a ascending, b ascending padded with ~0 to KN: min(a[i], b'[KN-1-i])
         // is bitonic and holds the KN smallest of both
 #pragma unroll
