@@ -26,8 +26,9 @@ constexpr int kBoxThreads = 256;
 constexpr int kBoxAxes = 4;                     // leading coordinates boxed (g <= 4)
 constexpr int kBoxSlots = 2 * kBoxAxes + 1;     // (min,max) per axis + non-finite flag
 
-// Per-axis min/max of the grid axes.  Each block writes a partial; the last
-// block to finish (atomic ticket) folds the partials into out[0..8]:
+// Per-axis min/max of the grid axes, four grid-stride iterations' loads in
+// flight per thread.  Each block writes a partial; the last block to finish
+// (atomic ticket) folds the partials with all its threads into out[0..8]:
 // out[2d] = min, out[2d+1] = max, out[8] = 1 if any coordinate is NaN or Inf.
 __global__ void __launch_bounds__(kBoxThreads) bbox_kernel(const float* __restrict__ pts, int n, int g,
                                                            float* __restrict__ partial,
@@ -37,7 +38,26 @@ __global__ void __launch_bounds__(kBoxThreads) bbox_kernel(const float* __restri
     bool bad = false;
 #pragma unroll
     for (int d = 0; d < kBoxAxes; ++d) { mn[d] = INFINITY; mx[d] = -INFINITY; }
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int stride = gridDim.x * blockDim.x;
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    for (; i + 3 * stride < n; i += 4 * stride) {
+        float v[4][kBoxAxes];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int d = 0; d < kBoxAxes; ++d) v[u][d] = d < g ? __ldg(&pts[(long long)d * n + i + u * stride]) : 0.0f;
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int d = 0; d < kBoxAxes; ++d) {
+                if (d < g) {
+                    bad |= !isfinite(v[u][d]);
+                    mn[d] = fminf(mn[d], v[u][d]);
+                    mx[d] = fmaxf(mx[d], v[u][d]);
+                }
+            }
+    }
+    for (; i < n; i += stride) {
 #pragma unroll
         for (int d = 0; d < kBoxAxes; ++d) {
             if (d < g) {
@@ -77,15 +97,36 @@ __global__ void __launch_bounds__(kBoxThreads) bbox_kernel(const float* __restri
     __syncthreads();
     if (!last) return;
     __threadfence();
-    if (threadIdx.x < kBoxSlots) {
-        int t = threadIdx.x;
-        bool is_max = (t & 1) || t == kBoxSlots - 1;
-        float acc = is_max ? -INFINITY : INFINITY;
-        for (int b = 0; b < (int)gridDim.x; ++b) {
-            float v = ((volatile float*)partial)[(long long)b * kBoxSlots + t];
-            acc = is_max ? fmaxf(acc, v) : fminf(acc, v);
+    // every thread folds a strided share of the partials (L2 loads, all in
+    // flight together), then the block reduces the shares
+    float acc[kBoxSlots];
+#pragma unroll
+    for (int t = 0; t < kBoxSlots; ++t) acc[t] = ((t & 1) || t == kBoxSlots - 1) ? -INFINITY : INFINITY;
+    for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) {
+#pragma unroll
+        for (int t = 0; t < kBoxSlots; ++t) {
+            const float v = __ldcg(&partial[(long long)b * kBoxSlots + t]);
+            acc[t] = ((t & 1) || t == kBoxSlots - 1) ? fmaxf(acc[t], v) : fminf(acc[t], v);
         }
-        out[t] = acc;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < kBoxSlots; ++t) {
+        float a = acc[t];
+        const bool is_max = (t & 1) || t == kBoxSlots - 1;
+        for (int o = 16; o > 0; o >>= 1) {
+            const float w = __shfl_xor_sync(0xffffffffu, a, o);
+            a = is_max ? fmaxf(a, w) : fminf(a, w);
+        }
+        if (lane == 0) sred[t][warp] = a;
+    }
+    __syncthreads();
+    if (threadIdx.x < kBoxSlots) {
+        const int t = threadIdx.x;
+        const bool is_max = (t & 1) || t == kBoxSlots - 1;
+        float a = sred[t][0];
+        for (int w = 1; w < kBoxThreads / 32; ++w) a = is_max ? fmaxf(a, sred[t][w]) : fminf(a, sred[t][w]);
+        out[t] = a;
     }
     if (threadIdx.x == 0) *ticket = 0u;  // ready for the next launch
 }
