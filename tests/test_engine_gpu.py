@@ -110,6 +110,31 @@ def test_duplicate_points_ties_break_by_index(frnn, oracle_mod, path):
     assert np.all(dist == 0.0)
 
 
+@pytest.mark.parametrize("K", [8, 16, 20, 32])
+@pytest.mark.parametrize("path", ["grid", "brute"])
+def test_lattice_ties_at_the_kth_distance(frnn, oracle_mod, K, path):
+    # A lattice with spacing 2^-6: coordinates, differences and squared
+    # distances are exact in fp32, so the 26 neighbours of an inner point sit at
+    # exactly three distances (6, 12 and 8 of them) and the K-th slot (the
+    # point itself is the first) falls inside a tie for K = 8, 16 and 20; ties
+    # resolve to the smaller index.
+    g = np.arange(16, dtype=np.float32) / 64.0
+    pts = np.stack(np.meshgrid(g, g, g, indexing="ij"), axis=-1).reshape(-1, 3)
+    pts = pts[np.random.default_rng(1).permutation(len(pts))]
+    soa = datagen.soa(pts)
+    r = 1.8 / 64.0
+    idx, dist, _ = run_engine(frnn, soa, K, r, path=path)
+    oi, od, _ = oracle_mod.search(soa, K, r)
+    assert_bit_exact(idx, dist, oi, od, f"lattice K={K}")
+    # an inner point keeps itself and its K - 1 nearest lattice neighbours,
+    # ties by index
+    inner = np.flatnonzero(np.all((pts > 0) & (pts < g[-1]), axis=1))[0]
+    d = ((pts - pts[inner]) ** 2).sum(axis=1)
+    order = np.lexsort((np.arange(len(pts)), d))
+    want = [int(j) for j in order if d[j] < np.float32(r) * np.float32(r)][:K]
+    assert idx[:, inner].tolist() == want + [-1] * (K - len(want))
+
+
 def test_all_points_identical(frnn, oracle_mod):
     soa = np.full((3, 3000), 0.3, np.float32)
     idx, dist, _ = run_engine(frnn, soa, 8, 0.01, path="grid")
