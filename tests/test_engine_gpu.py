@@ -230,6 +230,30 @@ def test_host_soa_path(frnn, oracle_mod):
     assert_bit_exact(i, d, oi, od, "host soa")
 
 
+@pytest.mark.parametrize("N,K,r", [(300, 8, 0.2), (20011, 16, 0.03), (40000, 32, 0.02), (20000, 32, 0.08)])
+def test_host_soa_d3(frnn, oracle_mod, N, K, r):
+    # the D = 3 collect/emit path through the host-buffer entry point: both
+    # emit widths, ragged sizes, and lists that overflow into the cooperative
+    # pass (a few, most, nearly all); pinned and pageable outputs
+    pts = datagen.generate("mixture", N, 3, seed=N)
+    soa = datagen.soa(pts)
+    eng = frnn.FRNNEngine(max_points=N)
+    eng.set_path("grid")
+    hi = torch.empty((K, N), dtype=torch.int32).pin_memory().numpy()
+    hd = torch.empty((K, N), dtype=torch.float32).pin_memory().numpy()
+    i, d = eng.search_soa_host(soa, K, r, hi, hd)
+    assert eng.last_plan()["path"] == "grid"
+    oi, od, _ = oracle_mod.search(soa, K, r)
+    assert_bit_exact(i, d, oi, od, f"host soa N={N} K={K}")
+    i2, d2 = eng.search_soa_host(soa, K, r)
+    assert np.array_equal(i2, i) and np.array_equal(d2.view(np.int32), d.view(np.int32))
+    # the device-pointer entry point afterwards still returns the same rows
+    x = torch.from_numpy(soa).cuda()
+    eng.search_gpu(x.data_ptr(), N, 3, K, r)
+    gi, gd = eng.get_results_arrays(N, K)
+    assert np.array_equal(gi, i) and np.array_equal(gd.view(np.int32), d.view(np.int32))
+
+
 # ---- errors are reported, not undefined -------------------------------------------
 
 
