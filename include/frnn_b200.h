@@ -180,7 +180,18 @@ enum frnn_option {
      * instead grid the data's principal axes (up to 6), which finds the same
      * neighbours with fewer candidates on correlated data.  Default AUTO: a
      * sampled estimate of candidates per query decides. */
-    FRNN_OPT_GRID_AXES = 2
+    FRNN_OPT_GRID_AXES = 2,
+    /* Grid searches with D != 3 and K <= 32 (FRNN_LIST_SEARCH_*): the list
+     * search (one thread per query appends every in-radius key to its own
+     * list, then a register sort emits the K smallest in original order, as
+     * for D = 3) or the warp-cooperative search.  Default AUTO: the list
+     * search for D <= 12.  No reference counterpart. */
+    FRNN_OPT_LIST_SEARCH = 3
+};
+enum frnn_list_search {
+    FRNN_LIST_SEARCH_AUTO = 0,     /* list search for D <= 12               */
+    FRNN_LIST_SEARCH_ALWAYS = 1,   /* list search for every D != 3          */
+    FRNN_LIST_SEARCH_NEVER = 2     /* warp-cooperative search for D != 3    */
 };
 enum frnn_grid_axes {
     FRNN_GRID_AXES_AUTO = 0,       /* cheaper of the two by the estimate    */

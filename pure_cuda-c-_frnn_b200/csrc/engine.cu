@@ -76,6 +76,7 @@ struct frnn_engine {
     DevBuf q_tiles, q_rows32, q_qa, q_pb;
     void* h_pca = nullptr;    // pinned, 32 KiB
     int grid_axes_mode = 0;   // FRNN_OPT_GRID_AXES
+    int list_search = 0;      // FRNN_OPT_LIST_SEARCH
     // a point set kept for frnn_query_grid: on the grid path its sorted rows,
     // ids, cell starts (and projected coordinates) stay in the point buffers
     struct {
@@ -539,6 +540,18 @@ int plan_principal(frnn_engine* e, const float* d_pts, int N, int dim, float rad
 // out[k*N + q].  Part search: the queries at sorted positions [s0, s1) only,
 // row j = sorted position s0 + j of out[k*(s1-s0) + j].
 // proj: the points' projected coordinates when P is a principal-axis grid.
+// Whether a grid search with D != 3 and K <= 32 takes the list search
+// (collect + emit) rather than the warp-cooperative kernel.  AUTO: rows of at
+// most 12 floats (B200, 12 clouds: the list search is 1.2-3x faster for
+// D <= 12 on every grid but one dense five-dimensional mixture, and 1.3-1.6x
+// slower at D = 16 and 24 on six principal axes, where the cooperative
+// kernel's shared candidate loads pay).
+bool list_search_nd(const frnn_engine* e, const GridPlan& P) {
+    if (e->list_search == FRNN_LIST_SEARCH_ALWAYS) return true;
+    if (e->list_search == FRNN_LIST_SEARCH_NEVER) return false;
+    return P.row <= 12;
+}
+
 int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2,
              const GridPlan& P, int* out_idx, float* out_dist, bool part, int& s0, int& s1,
              const float* proj) {
@@ -583,7 +596,11 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
         s0 = s0 >= N ? N : h[0];
         s1 = s1 >= N ? N : h[1];
     }
-    const bool two_kernel = P.dim == 3 && P.g == 3 && K <= 32;
+    // K <= 32: collect every in-radius key per query into a list, then sort and
+    // emit in original order (D = 3 always; other dimensions as
+    // list_search_nd decides)
+    const bool d3 = P.dim == 3 && P.g == 3 && !proj;
+    const bool two_kernel = K <= 32 && (d3 || list_search_nd(e, P));
     if (two_kernel) FRNN_GROW(e, e->inv, (size_t)N * 4);
     const float* proj_s = nullptr;
     if (proj) {
@@ -610,10 +627,17 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
         FRNN_CHECK(e, cudaMemsetAsync(e->n_overflow.p, 0, 4, s), "memset overflow count");
         const int q0 = part ? s0 : 0, q1 = part ? s1 : N, rows = q1 - q0;
         stage_begin(e, ST_COLLECT);
-        FRNN_CHECK(e, launch_collect_d3(e->rows.as<float>(), e->starts.as<int>(), P, r2, cap,
-                                        e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
-                                        e->overflow.as<int>(), e->n_overflow.as<int>(), q0, q1, s),
-                   "collect launch");
+        if (d3)
+            FRNN_CHECK(e, launch_collect_d3(e->rows.as<float>(), e->starts.as<int>(), P, r2, cap,
+                                            e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
+                                            e->overflow.as<int>(), e->n_overflow.as<int>(), q0, q1, s),
+                       "collect launch");
+        else
+            FRNN_CHECK(e, launch_collect_nd(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(), P, r2,
+                                            cap, e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
+                                            e->overflow.as<int>(), e->n_overflow.as<int>(), q0, q1, s, nullptr,
+                                            proj_s),
+                       "collect launch");
         stage_end(e, ST_COLLECT);
         stage_begin(e, ST_EMIT);
         // whole: rows in original order through inv; part: rows in sorted order
@@ -624,7 +648,7 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
         FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(),
                                          P, K, r2, 0, N, out_idx, out_dist, rows,
                                          part ? nullptr : e->ids.as<int>(), s, e->overflow.as<int>(),
-                                         e->n_overflow.as<int>(), q0),
+                                         e->n_overflow.as<int>(), q0, proj_s),
                    "overflow search launch");
         stage_end(e, ST_EMIT);
         e->launches += 3;
@@ -854,7 +878,8 @@ int search_sorted_queries(frnn_engine* e, const float* d_q, int M, int K, float 
     stage_end(e, ST_HASH);
     const float* proj_s = proj_p ? e->proj_s.as<float>() : nullptr;
     const float* qproj_s = proj_q ? e->q_proj_s.as<float>() : nullptr;
-    if (P.dim == 3 && P.g == 3 && K <= 32 && !proj_p) {
+    const bool d3 = P.dim == 3 && P.g == 3 && !proj_p;
+    if (K <= 32 && (d3 || list_search_nd(e, P))) {
         const int cap = K <= 16 ? 64 : 128;
         FRNN_GROW(e, e->lists, (size_t)M * cap * 8);
         FRNN_GROW(e, e->list_counts, (size_t)M * 4);
@@ -862,11 +887,18 @@ int search_sorted_queries(frnn_engine* e, const float* d_q, int M, int K, float 
         FRNN_GROW(e, e->n_overflow, 16);
         FRNN_CHECK(e, cudaMemsetAsync(e->n_overflow.p, 0, 4, s), "memset overflow count");
         stage_begin(e, ST_COLLECT);
-        FRNN_CHECK(e, launch_collect_d3(e->rows.as<float>(), e->starts.as<int>(), P, r2, cap,
-                                        e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
-                                        e->overflow.as<int>(), e->n_overflow.as<int>(), 0, M, s,
-                                        e->q_rows.as<float>()),
-                   "collect launch");
+        if (d3)
+            FRNN_CHECK(e, launch_collect_d3(e->rows.as<float>(), e->starts.as<int>(), P, r2, cap,
+                                            e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
+                                            e->overflow.as<int>(), e->n_overflow.as<int>(), 0, M, s,
+                                            e->q_rows.as<float>()),
+                       "collect launch");
+        else
+            FRNN_CHECK(e, launch_collect_nd(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(), P, r2,
+                                            cap, e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
+                                            e->overflow.as<int>(), e->n_overflow.as<int>(), 0, M, s,
+                                            e->q_rows.as<float>(), qproj_s),
+                       "collect launch");
         stage_end(e, ST_COLLECT);
         stage_begin(e, ST_EMIT);
         FRNN_CHECK(e, launch_emit_lists(e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
@@ -874,7 +906,7 @@ int search_sorted_queries(frnn_engine* e, const float* d_q, int M, int K, float 
                    "emit launch");
         FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(), P, K, r2, 0,
                                          M, out_idx, out_dist, M, e->q_ids.as<int>(), s, e->overflow.as<int>(),
-                                         e->n_overflow.as<int>(), -1, nullptr, e->q_rows.as<float>(), nullptr),
+                                         e->n_overflow.as<int>(), -1, proj_s, e->q_rows.as<float>(), qproj_s),
                    "overflow search launch");
         stage_end(e, ST_EMIT);
         e->launches += 3;
@@ -1327,6 +1359,11 @@ int frnn_set_option(frnn_engine* e, int option, int64_t value) {
             if (value < FRNN_GRID_AXES_AUTO || value > FRNN_GRID_AXES_PRINCIPAL)
                 return fail(e, FRNN_ERR_INVALID_ARG, "grid axes must be AUTO, LEADING or PRINCIPAL");
             e->grid_axes_mode = (int)value;
+            return FRNN_OK;
+        case FRNN_OPT_LIST_SEARCH:
+            if (value < FRNN_LIST_SEARCH_AUTO || value > FRNN_LIST_SEARCH_NEVER)
+                return fail(e, FRNN_ERR_INVALID_ARG, "list search must be AUTO, ALWAYS or NEVER");
+            e->list_search = (int)value;
             return FRNN_OK;
         default:
             return fail(e, FRNN_ERR_INVALID_ARG, "unknown option");

@@ -59,6 +59,14 @@ cudaError_t launch_collect_d3(const float* rows, const int* starts, const GridPl
                               int cap, unsigned long long* lists, int* counts, int* overflow,
                               int* n_overflow, int q0, int q1, cudaStream_t s,
                               const float* qrows = nullptr);
+// collect for D != 3 (any grid the planner makes, K-independent): the same
+// lists as launch_collect_d3 from one thread per query over its 3^g shell;
+// qproj: the queries' projected coordinates on a principal-axis grid (the
+// points' own sorted projections for a self-search).
+cudaError_t launch_collect_nd(const float* rows, const int* ids, const int* starts, const GridPlan& P,
+                              float r2, int cap, unsigned long long* lists, int* counts, int* overflow,
+                              int* n_overflow, int q0, int q1, cudaStream_t s, const float* qrows = nullptr,
+                              const float* qproj = nullptr);
 // emit: for output rows q < n -- sorted position map[q] (map = inv: rows in
 // original order), or q0 + q without map -- whose count is at most cap, the K
 // smallest keys ascending to out[k*n + q], padded (-1, r2).

@@ -94,6 +94,94 @@ __global__ void __launch_bounds__(256)
     if (n > cap) overflow[atomicAdd(n_overflow, 1)] = sq;
 }
 
+// The same collect for D != 3: one thread per query over its 3^G shell
+// (axis 0 merged into spans, 3^(G-1) spans), the canonical chain distance
+// over NV float4 per row, the index from ids[] (loaded only for accepted
+// candidates).  Grid coordinates are the row's leading coordinates, or the
+// query's projected coordinates (qproj, kProjStride floats per point) on a
+// principal-axis grid.  prune: skip spans whose box lies beyond r (leading
+// coordinates only: their gaps bound the full distance from below; projected
+// gaps would need the projection's rounding slack, so principal grids visit
+// the whole shell, as the cooperative kernel does).
+template <int NV, int G>
+__global__ void __launch_bounds__(256)
+    collect_nd_kernel(const float4* __restrict__ rows, const int* __restrict__ ids,
+                      const int* __restrict__ starts, GridPlan P, float r2, int cap,
+                      unsigned long long* __restrict__ lists, int* __restrict__ counts,
+                      int* __restrict__ overflow, int* __restrict__ n_overflow, int q0, int q1,
+                      const float4* __restrict__ qrows, const float4* __restrict__ qproj, int prune) {
+    constexpr int W = NV == 1 ? 8 : (NV == 2 ? 4 : 2);  // rows in flight per pass
+    static_assert(W <= kCollectRowPad, "passes read at most kCollectRowPad rows past a span");
+    const int sq = q0 + blockIdx.x * blockDim.x + threadIdx.x;
+    if (sq >= q1) return;
+    float4 q[NV];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) q[v] = __ldg(&qrows[(long long)sq * NV + v]);
+    float y[G];
+    int gc[G];
+#pragma unroll
+    for (int a = 0; a < G; ++a) {
+        const float4 f = qproj ? __ldg(&qproj[(long long)sq * (kProjStride / 4) + (a >> 2)]) : q[a >> 2];
+        y[a] = (a & 3) == 0 ? f.x : (a & 3) == 1 ? f.y : (a & 3) == 2 ? f.z : f.w;
+        gc[a] = cell_coord(y[a], P.origin[a], P.inv_cell, P.res[a]);
+    }
+    unsigned long long* mine = lists + (long long)sq * cap;
+    int n = 0;
+    int spans = 1;
+#pragma unroll
+    for (int a = 1; a < G; ++a) spans *= 3;
+    for (int t = 0; t < spans; ++t) {
+        int u = t;
+        long long rb = 0;
+        float gap = 0.0f;
+        bool ok = true;
+#pragma unroll
+        for (int a = 1; a < G; ++a) {
+            const int c = gc[a] + (u % 3) - 1;
+            u /= 3;
+            ok &= (c >= 0) & (c < P.res[a]);
+            if (prune) gap += axis_gap(y[a], c, P.origin[a], P.cell, P.eps);
+            rb += (long long)c * P.stride[a];
+        }
+        if (!ok || gap * kPruneScale > r2) continue;
+        int xlo = max(gc[0] - 1, 0), xhi = min(gc[0] + 1, P.res[0] - 1);
+        if (prune) {
+            if (xlo < gc[0] && (gap + axis_gap(y[0], xlo, P.origin[0], P.cell, P.eps)) * kPruneScale > r2) xlo = gc[0];
+            if (xhi > gc[0] && (gap + axis_gap(y[0], xhi, P.origin[0], P.cell, P.eps)) * kPruneScale > r2) xhi = gc[0];
+        }
+        // clamped to [0, n): a corrupt start table never reads out of bounds
+        int j = min(max(__ldg(&starts[rb + xlo]), 0), P.n);
+        const int e = min(max(__ldg(&starts[rb + xhi + 1]), j), P.n);
+        for (; j < e; j += W) {
+            float4 p[W][NV];
+#pragma unroll
+            for (int w = 0; w < W; ++w)
+#pragma unroll
+                for (int v = 0; v < NV; ++v) p[w][v] = __ldg(&rows[(long long)(j + w) * NV + v]);
+#pragma unroll
+            for (int w = 0; w < W; ++w) {
+                float d = 0.0f;
+#pragma unroll
+                for (int v = 0; v < NV; ++v) {
+                    float df = q[v].x - p[w][v].x;
+                    d = __fmaf_rn(df, df, d);
+                    df = q[v].y - p[w][v].y;
+                    d = __fmaf_rn(df, df, d);
+                    df = q[v].z - p[w][v].z;
+                    d = __fmaf_rn(df, df, d);
+                    df = q[v].w - p[w][v].w;
+                    d = __fmaf_rn(df, df, d);
+                }
+                const bool acc = j + w < e && d < r2;
+                const int idx = acc ? __ldg(&ids[j + w]) : 0;
+                append_if(acc, mine, n, cap, d, idx);
+            }
+        }
+    }
+    counts[sq] = n;
+    if (n > cap) overflow[atomicAdd(n_overflow, 1)] = sq;
+}
+
 // Ascending bitonic merge of a bitonic register array.
 template <int N>
 __device__ __forceinline__ void bitonic_merge(unsigned long long (&a)[N]) {
@@ -238,6 +326,56 @@ cudaError_t launch_collect_d3(const float* rows, const int* starts, const GridPl
         reinterpret_cast<const float4*>(rows), starts, P, r2, cap, lists, counts, overflow, n_overflow,
         q0, q1, reinterpret_cast<const float4*>(qrows ? qrows : rows));
     return cudaGetLastError();
+}
+
+namespace {
+template <int NV, int G>
+cudaError_t launch_nd(const float* rows, const int* ids, const int* starts, const GridPlan& P, float r2,
+                      int cap, unsigned long long* lists, int* counts, int* overflow, int* n_overflow, int q0,
+                      int q1, cudaStream_t s, const float* qrows, const float* qproj, bool prune) {
+    collect_nd_kernel<NV, G><<<(q1 - q0 + 255) / 256, 256, 0, s>>>(
+        reinterpret_cast<const float4*>(rows), ids, starts, P, r2, cap, lists, counts, overflow, n_overflow,
+        q0, q1, reinterpret_cast<const float4*>(qrows ? qrows : rows), reinterpret_cast<const float4*>(qproj),
+        prune ? 1 : 0);
+    return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_collect_nd(const float* rows, const int* ids, const int* starts, const GridPlan& P,
+                              float r2, int cap, unsigned long long* lists, int* counts, int* overflow,
+                              int* n_overflow, int q0, int q1, cudaStream_t s, const float* qrows,
+                              const float* qproj) {
+    if (q1 <= q0) return cudaSuccess;
+    const bool prune = qproj == nullptr;
+    const int nv = P.row / 4;
+#define FRNN_ND(NV, G) return launch_nd<NV, G>(rows, ids, starts, P, r2, cap, lists, counts, overflow, \
+                                                n_overflow, q0, q1, s, qrows, qproj, prune)
+    if (nv == 1 && !qproj) {
+        if (P.g == 1) FRNN_ND(1, 1);
+        if (P.g == 2) FRNN_ND(1, 2);
+        if (P.g == 3) FRNN_ND(1, 3);
+        if (P.g == 4) FRNN_ND(1, 4);
+        return cudaErrorInvalidValue;
+    }
+#define FRNN_ND_G(NV)                      \
+    switch (P.g) {                         \
+        case 2: FRNN_ND(NV, 2);            \
+        case 3: FRNN_ND(NV, 3);            \
+        case 4: FRNN_ND(NV, 4);            \
+        case 5: FRNN_ND(NV, 5);            \
+        case 6: FRNN_ND(NV, 6);            \
+        default: return cudaErrorInvalidValue; \
+    }
+    if (!qproj && P.g != 4) return cudaErrorInvalidValue;
+    switch (nv) {
+        case 2: FRNN_ND_G(2)
+        case 3: FRNN_ND_G(3)
+        case 4: FRNN_ND_G(4)
+        case 8: FRNN_ND_G(8)
+        default: return cudaErrorInvalidValue;
+    }
+#undef FRNN_ND_G
+#undef FRNN_ND
 }
 
 cudaError_t launch_emit_lists(const unsigned long long* lists, const int* counts, const int* map,

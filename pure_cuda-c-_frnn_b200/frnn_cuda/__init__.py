@@ -271,7 +271,9 @@ class FRNNEngine:
 
     OPT_DIRECT_OUTPUT_MAX_BYTES = 1
     OPT_GRID_AXES = 2
+    OPT_LIST_SEARCH = 3
     GRID_AXES_AUTO, GRID_AXES_LEADING, GRID_AXES_PRINCIPAL = 0, 1, 2
+    LIST_SEARCH_AUTO, LIST_SEARCH_ALWAYS, LIST_SEARCH_NEVER = 0, 1, 2
 
     def set_option(self, option: int, value: int) -> None:
         self._check(self._lib.frnn_set_option(self._eng, int(option), int(value)), "set_option")

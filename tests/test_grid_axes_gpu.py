@@ -127,3 +127,33 @@ def test_option_rejects_unknown_mode(frnn):
     eng = frnn.FRNNEngine(max_points=10)
     with pytest.raises(ValueError):
         eng.set_option(eng.OPT_GRID_AXES, 3)
+
+
+def test_list_search_option_rejects_unknown_mode(frnn):
+    eng = frnn.FRNNEngine(max_points=10)
+    with pytest.raises(ValueError):
+        eng.set_option(eng.OPT_LIST_SEARCH, 3)
+
+
+@pytest.mark.parametrize("kind,D,K,axes", [("uniform", 1, 16, 0), ("uniform", 2, 32, 0), ("mixture", 4, 20, 0),
+                                           ("lowrank4", 8, 32, 2), ("lowrank4", 12, 8, 1), ("lowrank6", 16, 32, 2),
+                                           ("mixture", 5, 16, 1), ("lowrank6", 24, 32, 2)])
+@pytest.mark.parametrize("mode", ["AUTO", "ALWAYS", "NEVER"])
+def test_list_search_modes_agree(frnn, oracle_mod, kind, D, K, axes, mode):
+    # the list search (collect + emit) and the warp-cooperative search return
+    # the same bits on leading-coordinate and principal-axis grids; queries
+    # whose lists overflow go to the cooperative kernel in either mode
+    N = 12000
+    pts = datagen.generate(kind, N, D, seed=31 * D + K)
+    soa = datagen.soa(pts)
+    r = datagen.calibrate_radius(pts, 24, sample=512, seed=2)
+    eng = frnn.FRNNEngine(max_points=N)
+    eng.set_path("grid")
+    eng.set_option(eng.OPT_GRID_AXES, axes)
+    eng.set_option(eng.OPT_LIST_SEARCH, getattr(eng, "LIST_SEARCH_" + mode))
+    x = torch.from_numpy(soa).cuda()
+    eng.search_gpu(x.data_ptr(), N, D, K, r)
+    i, d = eng.get_results_arrays(N, K)
+    assert eng.last_plan()["path"] == "grid"
+    oi, od, _ = oracle_mod.search(soa, K, r)
+    assert_bit_exact(i, d, oi, od, f"{kind} D={D} K={K} axes={axes} {mode}")
