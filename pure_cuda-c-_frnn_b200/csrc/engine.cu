@@ -418,7 +418,7 @@ int plan_principal(frnn_engine* e, const float* d_pts, int N, int dim, float rad
     *principal = false;
     const int slots = pca_slots(dim);
     const int samples = std::min(N, 65536);
-    const int mblocks = std::max(1, std::min(64, samples / 256));
+    const int mblocks = std::max(1, std::min(256, samples / 256));
     FRNN_GROW(e, e->pca_partial, (size_t)mblocks * slots * 8);
     FRNN_GROW(e, e->pca_moments, (size_t)(slots + dim) * 8);
     FRNN_CHECK(e, launch_pca_moments(d_pts, N, dim, samples, mblocks, e->pca_partial.as<double>(),

@@ -76,13 +76,27 @@ __global__ void __launch_bounds__(kMomThreads)
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             if (sa[k] < 0) continue;
-            double a = acc[k];
+            // four chains over j mod 4, folded in a fixed order
+            double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+            int j = 0;
             if (sb[k] < 0) {
-                for (int j = 0; j < m; ++j) a += (double)tile[j][sa[k]];
+                for (; j + 3 < m; j += 4) {
+                    a0 += (double)tile[j][sa[k]];
+                    a1 += (double)tile[j + 1][sa[k]];
+                    a2 += (double)tile[j + 2][sa[k]];
+                    a3 += (double)tile[j + 3][sa[k]];
+                }
+                for (; j < m; ++j) a0 += (double)tile[j][sa[k]];
             } else {
-                for (int j = 0; j < m; ++j) a += (double)tile[j][sa[k]] * (double)tile[j][sb[k]];
+                for (; j + 3 < m; j += 4) {
+                    a0 += (double)tile[j][sa[k]] * (double)tile[j][sb[k]];
+                    a1 += (double)tile[j + 1][sa[k]] * (double)tile[j + 1][sb[k]];
+                    a2 += (double)tile[j + 2][sa[k]] * (double)tile[j + 2][sb[k]];
+                    a3 += (double)tile[j + 3][sa[k]] * (double)tile[j + 3][sb[k]];
+                }
+                for (; j < m; ++j) a0 += (double)tile[j][sa[k]] * (double)tile[j][sb[k]];
             }
-            acc[k] = a;
+            acc[k] += (a0 + a1) + (a2 + a3);
         }
     }
 #pragma unroll
@@ -209,9 +223,11 @@ __global__ void sample_kernel(const float* __restrict__ pts, int n, int dim, con
     for (int d = 0; d < 8; ++d) o[8 + d] = __ldg(&proj[i * kProjStride + d]);
 }
 
-// counts[q*16 + b*8 + g-1]: sample points within half-width h[b*8 + g-1] of
+// counts[q*16 + b*8 + g-1] += sample points within half-width h[b*8 + g-1] of
 // sample query q (query q = sample point q * m / nq) on each of the first g
-// axes of basis b (0 leading coordinates, 1 principal axes).
+// axes of basis b (0 leading coordinates, 1 principal axes); block (q, y)
+// scans the y-th of gridDim.y slices of the sample points (integer sums, so
+// the total does not depend on the order).
 __global__ void __launch_bounds__(256) estimate_kernel(const float* __restrict__ smp, int m, int nq,
                                                        const float* __restrict__ h, int* __restrict__ counts) {
     __shared__ float qv[16];
@@ -226,7 +242,9 @@ __global__ void __launch_bounds__(256) estimate_kernel(const float* __restrict__
     int c[16];
 #pragma unroll
     for (int t = 0; t < 16; ++t) c[t] = 0;
-    for (int j = threadIdx.x; j < m; j += blockDim.x) {
+    const int j0 = (int)((long long)m * blockIdx.y / gridDim.y), j1 = (int)((long long)m * (blockIdx.y + 1) / gridDim.y);
+#pragma unroll 2
+    for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) {
         const float* p = smp + (long long)j * 16;
 #pragma unroll
         for (int b = 0; b < 2; ++b) {
@@ -249,7 +267,7 @@ __global__ void __launch_bounds__(256) estimate_kernel(const float* __restrict__
     if (threadIdx.x < 16) {
         int a = 0;
         for (int w = 0; w < 8; ++w) a += red[threadIdx.x][w];
-        counts[(long long)blockIdx.x * 16 + threadIdx.x] = a;
+        atomicAdd(&counts[(long long)blockIdx.x * 16 + threadIdx.x], a);
     }
 }
 
@@ -283,7 +301,9 @@ cudaError_t launch_pca_estimate(const float* pts, int n, int dim, const float* p
     sample_kernel<<<(m + 255) / 256, 256, 0, s>>>(pts, n, dim, proj, m, smp);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    estimate_kernel<<<nq, 256, 0, s>>>(smp, m, nq, h, counts);
+    e = cudaMemsetAsync(counts, 0, (size_t)nq * 16 * sizeof(int), s);
+    if (e != cudaSuccess) return e;
+    estimate_kernel<<<dim3(nq, 8), 256, 0, s>>>(smp, m, nq, h, counts);
     return cudaGetLastError();
 }
 
