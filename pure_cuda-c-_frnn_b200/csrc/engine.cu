@@ -1581,7 +1581,7 @@ int frnn_search(frnn_engine* e, const float* h_points_aos, int64_t count, int K,
         cudaMemsetAsync(e->err_flag.p, 0, sizeof(int), s);
         cudaStreamSynchronize(s);
         e->last_N = -1;
-        return fail(e, FRNN_ERR_TIMEOUT, "prefix-scan look-back wait gave up");
+        return fail(e, FRNN_ERR_TIMEOUT, "a bounded device-side wait gave up");
     }
     return FRNN_OK;
 }
@@ -1607,7 +1607,7 @@ int frnn_search_host_soa(frnn_engine* e, const float* h_points_soa, int N, int d
         cudaMemsetAsync(e->err_flag.p, 0, sizeof(int), s);
         cudaStreamSynchronize(s);
         e->last_N = -1;
-        return fail(e, FRNN_ERR_TIMEOUT, "prefix-scan look-back wait gave up");
+        return fail(e, FRNN_ERR_TIMEOUT, "a bounded device-side wait gave up");
     }
     return FRNN_OK;
 }
