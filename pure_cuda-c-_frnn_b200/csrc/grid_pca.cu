@@ -106,19 +106,23 @@ __global__ void __launch_bounds__(kMomThreads)
     }
 }
 
-// out[s] = sum of the blocks' partials of slot s, in block order; then
-// out[slots + d] = x0_d (the shift the sums are taken about)
+// out[s] = sum of the blocks' partials of slot s, one warp per slot: lane l
+// sums blocks l, l + 32, ... and a fixed xor tree folds the lanes (the same
+// order on every run); then out[slots + d] = x0_d (the shift the sums are
+// taken about)
 __global__ void moments_reduce_kernel(const double* __restrict__ partial, int blocks, int slots,
                                       double* __restrict__ out, const float* __restrict__ pts, int n,
                                       int dim) {
-    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    const int s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (s >= slots) {
-        if (s < slots + dim) out[s] = (double)__ldg(&pts[(long long)(s - slots) * n]);
+        if (s < slots + dim && lane == 0) out[s] = (double)__ldg(&pts[(long long)(s - slots) * n]);
         return;
     }
     double a = 0.0;
-    for (int b = 0; b < blocks; ++b) a += partial[(long long)b * slots + s];
-    out[s] = a;
+    for (int b = lane; b < blocks; b += 32) a += __ldcg(&partial[(long long)b * slots + s]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+    if (lane == 0) out[s] = a;
 }
 
 __global__ void __launch_bounds__(kProjThreads)
@@ -209,18 +213,19 @@ __global__ void __launch_bounds__(kProjThreads)
     if (threadIdx.x == 0) *ticket = 0u;
 }
 
-// smp[j] = (leading coordinates 0..5, padded | projected coordinates 0..5,
-// padded) of sample point j (point j * n / m).
+// smp[c*m + j], column c = leading coordinate c (c < 8, zero past 6 or D)
+// or projected coordinate c - 8, of sample point j (point j * n / m):
+// column-major, so a warp's loads of one column are one 128-byte line.
 __global__ void sample_kernel(const float* __restrict__ pts, int n, int dim, const float* __restrict__ proj,
                               int m, float* __restrict__ smp) {
     const int j = blockIdx.x * blockDim.x + threadIdx.x;
     if (j >= m) return;
     const long long i = (long long)j * n / m;
-    float* o = smp + (long long)j * 16;
 #pragma unroll
-    for (int d = 0; d < 8; ++d) o[d] = d < dim && d < kMaxGridAxes ? __ldg(&pts[(long long)d * n + i]) : 0.0f;
+    for (int d = 0; d < 8; ++d)
+        smp[(long long)d * m + j] = d < dim && d < kMaxGridAxes ? __ldg(&pts[(long long)d * n + i]) : 0.0f;
 #pragma unroll
-    for (int d = 0; d < 8; ++d) o[8 + d] = __ldg(&proj[i * kProjStride + d]);
+    for (int d = 0; d < 8; ++d) smp[(long long)(8 + d) * m + j] = __ldg(&proj[i * kProjStride + d]);
 }
 
 // counts[q*16 + b*8 + g-1] += sample points within half-width h[b*8 + g-1] of
@@ -235,7 +240,7 @@ __global__ void __launch_bounds__(256) estimate_kernel(const float* __restrict__
     __shared__ int red[16][8];
     const int q = (int)((long long)blockIdx.x * m / nq);
     if (threadIdx.x < 16) {
-        qv[threadIdx.x] = smp[(long long)q * 16 + threadIdx.x];
+        qv[threadIdx.x] = smp[(long long)threadIdx.x * m + q];
         hh[threadIdx.x] = h[threadIdx.x];
     }
     __syncthreads();
@@ -245,13 +250,12 @@ __global__ void __launch_bounds__(256) estimate_kernel(const float* __restrict__
     const int j0 = (int)((long long)m * blockIdx.y / gridDim.y), j1 = (int)((long long)m * (blockIdx.y + 1) / gridDim.y);
 #pragma unroll 2
     for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) {
-        const float* p = smp + (long long)j * 16;
 #pragma unroll
         for (int b = 0; b < 2; ++b) {
             float run = 0.0f;
 #pragma unroll
             for (int g = 0; g < kMaxGridAxes; ++g) {
-                run = fmaxf(run, fabsf(p[8 * b + g] - qv[8 * b + g]));
+                run = fmaxf(run, fabsf(__ldg(&smp[(long long)(8 * b + g) * m + j]) - qv[8 * b + g]));
                 c[8 * b + g] += run < hh[8 * b + g] ? 1 : 0;
             }
         }
@@ -282,7 +286,7 @@ cudaError_t launch_pca_moments(const float* pts, int n, int dim, int samples, in
     moments_kernel<<<blocks, kMomThreads, 0, s>>>(pts, n, dim, samples, partial, slots);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    moments_reduce_kernel<<<(slots + dim + 127) / 128, 128, 0, s>>>(partial, blocks, slots, out, pts, n, dim);
+    moments_reduce_kernel<<<(slots + dim + 3) / 4, 128, 0, s>>>(partial, blocks, slots, out, pts, n, dim);
     return cudaGetLastError();
 }
 
