@@ -1,19 +1,24 @@
-// grid_collect.cu -- the D = 3 search as two kernels: collect, then emit.
+// grid_collect.cu -- the list search: a grid search as two kernels, collect
+// then emit (K <= 32).
 //
 // Replaces, for D = 3, the reference's FindNbrsAoS3Kernel (find_nbrs.cu:400-491)
-// followed by ScatterToOrigKernel (find_nbrs.cu:505-523).  Same candidates (the
-// 27-cell shell), same arithmetic, same acceptance rule (d2 < r2 strict, K
-// smallest, ties to the smaller index); the work is split where the GPU wants
-// it split:
+// and, for other dimensions, FindNbrsNDKernel (:116-214) and
+// FindNbrsGridDimKernel (:243-353), each followed by ScatterToOrigKernel
+// (:505-523).  Same candidates (the 3^g cell shell), same arithmetic, same
+// acceptance rule (d2 < r2 strict, K smallest, ties to the smaller index); the
+// work is split where the GPU wants it split:
 //
 //   collect  one thread per query in cell order (the lanes of a warp walk
 //            neighbouring cells, so candidate rows come from L1): every
 //            candidate with d2 < r2 is appended, as a 64-bit (d2, index) key,
 //            to the query's own list in global memory.  No selection and no
-//            sorting here, so the loop stays small and the kernel runs at full
+//            sorting here, so the loop stays small and the kernel runs at high
 //            occupancy.  The lists are in cell order (lists[sq*cap + j]): a
 //            list fills whole 32-byte sectors as it grows, and the lists of a
-//            warp's queries are neighbours in memory.
+//            warp's queries are neighbours in memory.  collect_d3_kernel is
+//            the D = 3 form (float4 rows carrying the index);
+//            collect_nd_kernel<NV, G> covers every other grid the planner
+//            makes (NV float4 per row, G axes, leading or principal).
 //   emit     one thread per query in ORIGINAL order (inv[] maps it to its cell
 //            order position), so the K result rows are written coalesced and no
 //            unpermute pass is needed.  Each thread keeps its K smallest keys in
