@@ -199,6 +199,35 @@ def test_engine_reuse_across_shapes(frnn, oracle_mod):
         assert_bit_exact(idx, dist, oi, od, f"reuse N={N} D={D}")
 
 
+@pytest.mark.parametrize("D,K", [(3, 16), (3, 48), (2, 8), (4, 32)])
+def test_points_changed_in_place_between_searches(frnn, oracle_mod, D, K):
+    # One engine searches the same device buffer while its contents change
+    # between calls (unchanged, moved, grown, shrunk, then a NaN): every call
+    # plans its grid from that call's points, so each must match the oracle or
+    # report the NaN, and a clean call after the NaN recovers.
+    N = 20000
+    base = datagen.generate("mixture", N, D, seed=D + K)
+    r = datagen.calibrate_radius(base, 16, sample=512, seed=5)
+    eng = frnn.FRNNEngine(max_points=N)
+    x = torch.empty((D, N), dtype=torch.float32, device="cuda")
+    for step, pts in enumerate([base, base, base + 0.3, base * 1.5, base * 0.7, base * 0.7]):
+        soa = datagen.soa(pts.astype(np.float32))
+        x.copy_(torch.from_numpy(soa))
+        eng.search_gpu(x.data_ptr(), N, D, K, r)
+        i, d = eng.get_results_arrays(N, K)
+        oi, od, _ = oracle_mod.search(soa, K, r)
+        assert_bit_exact(i, d, oi, od, f"step {step} D={D} K={K}")
+        assert eng.last_plan()["path"] == "grid"
+    x[0, 123] = float("nan")
+    with pytest.raises(ValueError):
+        eng.search_gpu(x.data_ptr(), N, D, K, r)
+    x[0, 123] = 0.5
+    eng.search_gpu(x.data_ptr(), N, D, K, r)
+    i, d = eng.get_results_arrays(N, K)
+    oi, od, _ = oracle_mod.search(x.cpu().numpy(), K, r)
+    assert_bit_exact(i, d, oi, od, "after the NaN")
+
+
 # ---- the reference's host-path and results surface ------------------------------
 
 
