@@ -4,7 +4,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl engine|reference]
                     [--config C]
 
-Workload (default ``--config 2``): D=3, N=1,000,000
+Workload (default ``--config 2``, the headline configuration): D=3, N=1,000,000
 points from a 64-component Gaussian mixture (sigma=0.02), K=32, radius
 calibrated for 24 mean in-radius neighbours, self-query.  One step = one full
 search (grid build + neighbour search + results in the reference layout) of
@@ -61,6 +61,11 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["engine", "reference"], default="engine")
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5])
+    ap.add_argument("--n", type=int, default=None,
+                    help="points (default: the configuration's own N; a smaller cloud gets a radius "
+                         "calibrated for the same mean neighbour count) -- for small profiling cases")
+    ap.add_argument("--no-per-config", action="store_true",
+                    help="skip the per_config sweep over all five configurations (N=1 only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--mode", choices=["weak", "strong"], default="weak",
@@ -148,6 +153,121 @@ def time_steps(torch, fn, steps, flush):
     return total / steps
 
 
+def step_times(torch, fn, steps, flush):
+    """Device time (ms) of each of ``steps`` calls of fn, L2 flushed before each."""
+    out = []
+    for _ in range(steps):
+        flush.zero_()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        out.append(a.elapsed_time(b))
+    return out
+
+
+def workload(cfg: int, n: int | None):
+    """(config, points (N, D), radius) of a configuration, at its own size or n.
+
+    The min-max normalised clouds (configurations 3 and 4) are clipped below
+    1.0: the reference's first-coordinate grid drops points at 1.0
+    (insert_points.cu:74-87) and its search then reads sorted slots that no
+    point filled (find_nbrs.cu:254-256), which is undefined.  Clipping moves at
+    most one point per coordinate by 1e-6 and leaves every measured time as it
+    is; both arms search the same clipped cloud."""
+    c = datagen.config(cfg)
+    if n is None or n == c.N:
+        pts, r = datagen.generate(c.kind, c.N, c.D, seed=datagen.SEED), c.radius
+    else:
+        pts, r = datagen.cloud(cfg, n)
+    if c.kind.startswith("lowrank"):
+        pts = np.minimum(pts, np.float32(0.999999))
+    return c, pts, r
+
+
+def config_dict(c, N: int, r: float) -> dict:
+    """The ``config`` block: identical in both arms for the same workload."""
+    return {"workload": c.name if N == c.N else f"{c.name}_n{N}", "describe": c.describe, "N": N,
+            "D": c.D, "K": c.K, "radius": r, "l2": "flushed before every timed step"}
+
+
+def search_roofline(N: int, D: int, K: int, cells: int, path: str, ms: float) -> dict:
+    """Whole-search roofline: the compulsory bytes B_alg = 4N(3D + 4 + 2K) + 12C
+    of a grid search against HBM, or the 2N^2 D flops of the tensor-core
+    filter against the sustained bf16 peak."""
+    hbm, _, bf16_sus, src = measured_peaks()
+    t = ms / 1e3
+    if path == "brute_tc":
+        f = 2.0 * N * N * D
+        return {"bound": "tensor", "alg_flops": f, "achieved": f / t / 1e12, "peak": bf16_sus,
+                "unit": "TFLOP/s", "frac": f / t / 1e12 / bf16_sus, "peak_source": src + " (bf16 sustained)"}
+    b = 4 * N * (3 * D + 4 + 2 * K) + 12 * cells
+    return {"bound": "hbm", "alg_bytes": int(b), "achieved": b / t / 1e9, "peak": hbm, "unit": "GB/s",
+            "frac": b / t / 1e9 / hbm, "peak_source": src}
+
+
+def per_config_engine(torch, dev, flush, steps: int = 5, warmup: int = 3) -> dict:
+    """Every configuration at full size on one GPU: median of ``steps`` timed
+    searches (L2 flushed before each), per-stage times and the roofline."""
+    import frnn_cuda
+    out = {}
+    for cfg in sorted(datagen.CONFIGS):
+        c, pts, r = workload(cfg, None)
+        soa = datagen.soa(pts)
+        del pts
+        x = torch.from_numpy(soa).to(dev)
+        eng = frnn_cuda.FRNNEngine(max_points=c.N, device=dev)
+        step = lambda: eng.search_gpu(x.data_ptr(), c.N, c.D, c.K, r)  # noqa: E731
+        for _ in range(warmup):
+            step()
+        n = steps if cfg != 5 else 3
+        ms = step_times(torch, step, n, flush)
+        eng.set_timing(True)
+        flush.zero_()
+        step()
+        stage_ms = eng.stage_times()
+        eng.set_timing(False)
+        plan = eng.last_plan()
+        med = statistics.median(ms)
+        out[f"cfg{cfg}"] = {"workload": c.name, "steps": n, "ms_median": med, "ms": ms,
+                            "queries_per_s": c.N / (med / 1e3), "stage_ms": stage_ms, "plan": plan,
+                            "roofline": search_roofline(c.N, c.D, c.K, plan["cells"], plan["path"], med)}
+        del eng, x
+        torch.cuda.empty_cache()
+    return out
+
+
+def per_config_reference(torch, dev, flush) -> dict:
+    """The reference engine on every configuration at full size (its own
+    dispatch): median of 5 timed searches, 2 for configuration 5, whose brute
+    force takes about 47 s per search on a B200."""
+    import oracle
+    out = {}
+    for cfg in sorted(datagen.CONFIGS):
+        c, pts, r = workload(cfg, None)
+        soa = datagen.soa(pts)
+        del pts
+        x = torch.from_numpy(soa).to(dev)
+        ref = oracle.RefEngine(c.N)
+        step = lambda: ref.search_gpu(x.data_ptr(), c.N, c.D, c.K, r)  # noqa: E731
+        warm, n = (1, 2) if cfg == 5 else (3, 5)
+        for _ in range(warm):
+            step()
+        ms = step_times(torch, step, n, flush)
+        ref.close()
+        plan = oracle.ref_plan(c.N, c.D, c.K, r)
+        med = statistics.median(ms)
+        path = "brute_tc" if plan["path"].startswith("bf") and c.D > 32 else "grid"
+        out[f"cfg{cfg}"] = {"workload": c.name, "steps": n, "ms_median": med, "ms": ms,
+                            "queries_per_s": c.N / (med / 1e3), "ref_path": plan["path"],
+                            "roofline": search_roofline(c.N, c.D, c.K, plan["cells"], path, med)}
+        del x
+        torch.cuda.empty_cache()
+    return out
+
+
 def cpu_baseline(soa: np.ndarray, K: int, r: float, budget_s: float = 12.0) -> dict:
     """The CPU oracle (exact grid search, OpenMP) on a bounded query sample,
     extrapolated to the whole self-query."""
@@ -176,11 +296,14 @@ def cpu_baseline(soa: np.ndarray, K: int, r: float, budget_s: float = 12.0) -> d
 
 def run_engine_arm(a, torch, dist, rank, world, dev):
     import frnn_cuda
-    c = datagen.config(a.config)
-    N, D, K, r = c.N, c.D, c.K, c.radius
     strong = a.mode == "strong" and world > 1
-    # weak: rank r searches replica r (its own sample of the same distribution)
-    pts = datagen.generate(c.kind, N, D, seed=datagen.SEED, replica=0 if strong else rank)
+    c, pts, r = workload(a.config, a.n)
+    N, D, K = pts.shape[0], c.D, c.K
+    if not strong and rank > 0:
+        # weak: rank r searches replica r (its own sample of the same distribution)
+        pts = datagen.generate(c.kind, N, D, seed=datagen.SEED, replica=rank)
+        if c.kind.startswith("lowrank"):
+            pts = np.minimum(pts, np.float32(0.999999))
     soa = datagen.soa(pts)
     x = torch.from_numpy(soa).to(dev)
     eng = frnn_cuda.FRNNEngine(max_points=N, device=dev)
@@ -316,12 +439,11 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_max,
         "higher_is_better": True, "scaling": "strong" if strong else "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic (seeded generator, seed 1234; rank r draws replica r of the same distribution)",
-        "config": {"workload": c.name, "describe": c.describe, "N": N, "D": D, "K": K,
-                   "radius": r, "queries_per_gpu": N // world if strong else N,
-                   "l2": "flushed before every timed step",
-                   "parallelism": (f"one cloud, queries sharded over {world} ranks (NCCL broadcast "
-                                   f"+ part search + gather to rank 0 in every step)") if strong
-                                  else f"independent clouds x{world}"},
+        "config": config_dict(c, N, r),
+        "parallelism": (f"one cloud, queries sharded over {world} ranks (NCCL broadcast "
+                        f"+ part search + gather to rank 0 in every step)") if strong
+                       else f"independent clouds x{world}",
+        "queries_per_gpu": N // world if strong else N,
         "latency_ms": ms_max,
         "pipeline": {"b_alg_bytes": int(b_alg), "b_alg_gbs": b_alg / (ms_max / 1e3) / 1e9,
                      "b_alg_frac": b_alg / (ms_max / 1e3) / 1e9 / hbm, "plan": plan,
@@ -333,16 +455,19 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
     }
     if world == 1 and not a.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(soa, K, r)
+    if world == 1 and not a.no_per_config:
+        del x
+        torch.cuda.empty_cache()
+        line["per_config"] = per_config_engine(torch, dev, flush)
     return line
 
 
 def run_reference_arm(a, torch, dev):
     import oracle
-    c = datagen.config(a.config)
-    N, D, K, r = c.N, c.D, c.K, c.radius
     if not os.path.exists(oracle.REF_SO):
         return {"impl": "reference", "unavailable": "oracle/_ref/libfrnn_ref.so was not built"}
-    pts = datagen.generate(c.kind, N, D, seed=datagen.SEED)
+    c, pts, r = workload(a.config, a.n)
+    N, D, K = pts.shape[0], c.D, c.K
     soa = datagen.soa(pts)
     x = torch.from_numpy(soa).to(dev)
     ref = oracle.RefEngine(N)
@@ -365,8 +490,7 @@ def run_reference_arm(a, torch, dev):
         "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded generator, seed 1234)",
         "impl": "reference",
-        "config": {"workload": c.name, "describe": c.describe, "N": N, "D": D, "K": K,
-                   "radius": r, "l2": "flushed before every timed step"},
+        "config": config_dict(c, N, r),
         "latency_ms": ms,
         "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -389,6 +513,9 @@ def main():
         if rank != 0:
             return 0
         line = run_reference_arm(a, torch, local)
+        if world == 1 and not a.no_per_config and "unavailable" not in line:
+            flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=local)
+            line["per_config"] = per_config_reference(torch, local, flush)
         print(json.dumps(line), flush=True)
         return 0
     dist = None

@@ -20,7 +20,7 @@
  *   - returned device pointers are engine-owned and stay valid until the next
  *     search call on the same engine (frnn_engine.cu:248-249).
  *
- * Differences (all documented in DESIGN.md of this repository):
+ * Differences from the reference:
  *   - the K slots of a query are returned in ascending (d2, index) order and
  *     ties at equal d2 are broken by the smaller index, so results are a
  *     deterministic function of the input (the reference returns heap order
@@ -145,8 +145,8 @@ int frnn_query_grid(frnn_engine* e, const float* d_queries_soa, int M, int K, in
 
 /* Part of a search, for sharding the queries of one cloud over several
  * engines (one per GPU).  No counterpart in the reference, whose engine only
- * searches whole clouds; SURVEY-style query sharding splits the reference's
- * search_gpu (python_interface/frnn_engine.cu:195-250) this way.  Every part
+ * searches whole clouds (python_interface/frnn_engine.cu:195-250); queries
+ * are independent, so its search splits over GPUs by query.  Every part
  * sees all N points; part `part` of `nparts` searches one contiguous slice of
  * the engine's query order (cell order on the grid path, input order on brute
  * force, whole 128-query tiles on the tensor-core path), and the slices of
@@ -186,7 +186,23 @@ enum frnn_option {
      * list, then a register sort emits the K smallest in original order, as
      * for D = 3) or the warp-cooperative search.  Default AUTO: the list
      * search for D <= 12.  No reference counterpart. */
-    FRNN_OPT_LIST_SEARCH = 3
+    FRNN_OPT_LIST_SEARCH = 3,
+    /* Tests of the timeout path only (FRNN_TEST_STALL_*): make one bounded
+     * device wait run out on purpose, so a test can check that the search
+     * returns FRNN_ERR_TIMEOUT and that the engine's next search succeeds.
+     * SCAN: one tile of the grid's prefix scan (the cell-count scan that
+     * replaces the reference's thrust::exclusive_scan, frnn_engine.cu:91-94)
+     * never publishes its status, so the next tile's look-back gives up
+     * after its poll limit.  TC_FILTER: the tensor-core filter's producer
+     * never copies one point tile, so the MMA thread's wait for it gives up
+     * after 2 s.  Results of a stalled search are undefined; nothing is
+     * written outside the engine's buffers.  Default OFF. */
+    FRNN_OPT_TEST_STALL = 4
+};
+enum frnn_test_stall {
+    FRNN_TEST_STALL_OFF = 0,
+    FRNN_TEST_STALL_SCAN = 1,      /* needs a grid of more than 8,192 cells   */
+    FRNN_TEST_STALL_TC_FILTER = 2  /* needs more than 128 points              */
 };
 enum frnn_list_search {
     FRNN_LIST_SEARCH_AUTO = 0,     /* list search for D <= 12               */
@@ -210,7 +226,7 @@ int frnn_last_grid_axes(const frnn_engine* e, int* axes);
  * histogram, 2 prefix scan, 3 scatter, 4 neighbour search, 5 unpermute,
  * 6 brute force, 7 candidate collection and 8 list emit -- stages 7 and 8
  * replace 4 and 5 for D = 3 with K <= 32 -- and, on FRNN_PATH_BRUTE_TC,
- * 9 prep, 10 tensor-core filter, 11 exact re-rank, with 6 timing the
+ * 0 the per-dimension box, 9 prep, 10 tensor-core filter, 11 exact re-rank, with 6 timing the
  * brute-force pass over queries whose candidate list overflowed), -1 for
  * stages that did not run. */
 int frnn_set_timing(frnn_engine* e, int enable);
@@ -218,6 +234,17 @@ int frnn_last_stage_times(frnn_engine* e, float* ms, int n);
 
 /* Number of kernels this engine has launched since it was created. */
 int frnn_launch_count(const frnn_engine* e, int64_t* n);
+
+/* Queries of the last whole search (frnn_search_gpu, _async once finished,
+ * _queries, frnn_query_grid, frnn_search, frnn_search_host_soa) whose
+ * candidate list overflowed its capacity and which a fallback pass searched
+ * again (the grid list search keeps up to 64 or 128 in-radius keys per query;
+ * the tensor-core filter up to max(4K, 256) candidates).  *count receives
+ * their number; the first min(*count, max_ids) original query indices go to
+ * h_query_ids (any order).  Searches without candidate lists report 0.
+ * FRNN_ERR_STATE when no whole search has finished.  No reference
+ * counterpart (its heaps never overflow: they keep K entries). */
+int frnn_last_overflow(frnn_engine* e, int* count, int* h_query_ids, int max_ids);
 
 /* Allocation-free search.  No counterpart in the reference: it is for callers
  * that cannot allocate device memory while they search (a framework whose own

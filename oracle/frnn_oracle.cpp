@@ -46,6 +46,7 @@
 #include <cstring>
 #include <limits>
 #include <vector>
+#include <immintrin.h>
 #include <omp.h>
 
 namespace {
@@ -232,6 +233,92 @@ void grid_visit(const CpuGrid& G, const float* q, F&& f) {
     }
 }
 
+// Mean candidates per query that grid_visit would enumerate, over up to 64
+// evenly spaced queries (an estimate used only to choose the accelerator).
+double grid_candidates(const CpuGrid& G, const float* qsoa, long long qstride, const int* qids, int nq,
+                       int D) {
+    const int m = std::min(nq, 64);
+    std::vector<float> q(D);
+    double sum = 0.0;
+    for (int t = 0; t < m; ++t) {
+        const int qi = qids ? qids[(long long)t * nq / m] : (int)((long long)t * nq / m);
+        for (int d = 0; d < D; ++d) q[d] = qsoa[(long long)d * qstride + qi];
+        grid_visit(G, q.data(), [&](int) { sum += 1.0; });
+    }
+    return m ? sum / m : 0.0;
+}
+
+// Exhaustive chain-order search (d2 = fma(diff, diff, d2), d = 0..D-1) with
+// AVX2: 4 queries x 16 points per step, each lane its own chain, so every d2
+// is bit-identical to dist2_chain.  Points are visited in tiles of kTile so a
+// tile stays in cache while all of a thread's queries pass over it.  Used
+// for D > 3 when the leading-coordinate grid would enumerate most points.
+void brute_chain_search(const float* soa, int N, int D, int K, float r2, const float* qsoa,
+                        long long qstride, const int* qids, int nq, int threads, int* idx_out,
+                        float* dist_out, int out_stride) {
+    constexpr int kTile = 2048, kQB = 4, kChunk = 64;
+    const int nchunks = (nq + kChunk - 1) / kChunk;
+#pragma omp parallel for num_threads(threads) schedule(dynamic, 1)
+    for (int ch = 0; ch < nchunks; ++ch) {
+        const int t0 = ch * kChunk, t1 = std::min(nq, t0 + kChunk), nt = t1 - t0;
+        std::vector<float> q((size_t)kChunk * D);
+        for (int t = 0; t < nt; ++t) {
+            const int qi = qids ? qids[t0 + t] : t0 + t;
+            for (int d = 0; d < D; ++d) q[(size_t)t * D + d] = qsoa[(long long)d * qstride + qi];
+        }
+        std::vector<std::vector<Cand>> cand(nt);
+        const __m256 vr2 = _mm256_set1_ps(r2);
+        for (int j0 = 0; j0 < N; j0 += kTile) {
+            const int j1 = std::min(N, j0 + kTile);
+            const int jv = j0 + (j1 - j0) / 16 * 16;  // vector part [j0, jv)
+            for (int b = 0; b < nt; b += kQB) {
+                const int nb = std::min(kQB, nt - b);
+                const float* qb[kQB];
+                for (int u = 0; u < kQB; ++u) qb[u] = &q[(size_t)(b + std::min(u, nb - 1)) * D];
+                for (int j = j0; j < jv; j += 16) {
+                    __m256 a00 = _mm256_setzero_ps(), a01 = a00, a10 = a00, a11 = a00, a20 = a00, a21 = a00,
+                           a30 = a00, a31 = a00;
+                    const float* pj = soa + j;
+                    for (int d = 0; d < D; ++d) {
+                        const __m256 p0 = _mm256_loadu_ps(pj + (long long)d * N);
+                        const __m256 p1 = _mm256_loadu_ps(pj + (long long)d * N + 8);
+                        __m256 x = _mm256_set1_ps(qb[0][d]), t;
+                        t = _mm256_sub_ps(x, p0); a00 = _mm256_fmadd_ps(t, t, a00);
+                        t = _mm256_sub_ps(x, p1); a01 = _mm256_fmadd_ps(t, t, a01);
+                        x = _mm256_set1_ps(qb[1][d]);
+                        t = _mm256_sub_ps(x, p0); a10 = _mm256_fmadd_ps(t, t, a10);
+                        t = _mm256_sub_ps(x, p1); a11 = _mm256_fmadd_ps(t, t, a11);
+                        x = _mm256_set1_ps(qb[2][d]);
+                        t = _mm256_sub_ps(x, p0); a20 = _mm256_fmadd_ps(t, t, a20);
+                        t = _mm256_sub_ps(x, p1); a21 = _mm256_fmadd_ps(t, t, a21);
+                        x = _mm256_set1_ps(qb[3][d]);
+                        t = _mm256_sub_ps(x, p0); a30 = _mm256_fmadd_ps(t, t, a30);
+                        t = _mm256_sub_ps(x, p1); a31 = _mm256_fmadd_ps(t, t, a31);
+                    }
+                    const __m256 acc[kQB][2] = {{a00, a01}, {a10, a11}, {a20, a21}, {a30, a31}};
+                    for (int u = 0; u < nb; ++u)
+                        for (int h = 0; h < 2; ++h) {
+                            int m = _mm256_movemask_ps(_mm256_cmp_ps(acc[u][h], vr2, _CMP_LT_OQ));
+                            if (!m) continue;
+                            alignas(32) float v[8];
+                            _mm256_store_ps(v, acc[u][h]);
+                            for (; m; m &= m - 1) {
+                                const int l = __builtin_ctz(m);
+                                cand[b + u].push_back({v[l], j + 8 * h + l});
+                            }
+                        }
+                }
+                for (int u = 0; u < nb; ++u)
+                    for (int j = jv; j < j1; ++j) {
+                        const float d2 = dist2_chain(qb[u], soa + j, N, D);
+                        if (d2 < r2) cand[b + u].push_back({d2, j});
+                    }
+            }
+        }
+        for (int t = 0; t < nt; ++t) emit(cand[t], K, r2, out_stride, t0 + t, idx_out, dist_out);
+    }
+}
+
 // Core exact search over a query subset.  `include` (may be null) restricts the
 // candidate set; `order` selects the distance arithmetic.
 // Queries are read from qsoa (SoA, stride qstride): the points themselves
@@ -249,6 +336,18 @@ int search_core(const float* soa, int N, int D, int K, float r, int order,
     bool have_grid = build_grid(soa, N, D, r, include, G);
     long long total = 0;
     if (threads <= 0) threads = omp_get_max_threads();
+    // D > 3 in the chain order over every point: the exhaustive SIMD search
+    // when the grid (on at most 3 leading coordinates) would enumerate more
+    // than 1/16 of the points per query (the SIMD loop is at least that much
+    // faster per candidate).  Same candidates, same d2 bits, same ranking.
+    const bool chain = order == ORDER_CHAIN || (order == ORDER_ENGINE && D != 3);
+    if (chain && D > 3 && !include &&
+        (!have_grid || grid_candidates(G, qsoa, qstride, qids, nq, D) * 16.0 > (double)N)) {
+        brute_chain_search(soa, N, D, K, r2, qsoa, qstride, qids, nq, threads, idx_out, dist_out,
+                           out_stride);
+        if (n_cand) *n_cand = (long long)nq * N;
+        return 0;
+    }
 #pragma omp parallel num_threads(threads) reduction(+ : total)
     {
         std::vector<float> q(D);

@@ -336,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     filter_kernel(const uint8_t* __restrict__ tiles, const float* __restrict__ qa, const float* __restrict__ pb,
                   int n, int ntiles, int cap, int* __restrict__ lists, int* __restrict__ counts,
                   int* __restrict__ overflow, int* __restrict__ n_overflow, int* __restrict__ err,
-                  int qb_begin, int qb_end, const uint8_t* __restrict__ qtiles) {
+                  int qb_begin, int qb_end, const uint8_t* __restrict__ qtiles, int skip_tile) {
     // qtiles: the query blocks' tiles (the points' own tiles for a self-query)
     using C = Cfg<KC>;
     constexpr int S = C::kStages;
@@ -410,14 +410,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     give_up();
                     break;
                 }
-                mbar_expect_tx(full(s), TB);
-                bulk_g2s(sB + (uint32_t)s * TB, tiles + (size_t)t * TB, TB, full(s));
+                // skip_tile (tests of the timeout path only): this stage is
+                // never filled, so the MMA thread's wait for it gives up
+                if (t != skip_tile) {
+                    mbar_expect_tx(full(s), TB);
+                    bulk_g2s(sB + (uint32_t)s * TB, tiles + (size_t)t * TB, TB, full(s));
+                }
                 issued = t + 1;
             }
             // copies still in flight land before the CTA may exit
             drain_wait(afull, 0);
             for (int t = issued - S < 0 ? 0 : issued - S; t < issued; ++t)
-                drain_wait(full(t % S), (uint32_t)(t / S) & 1u);
+                if (t != skip_tile) drain_wait(full(t % S), (uint32_t)(t / S) & 1u);
         }
     } else if (warp == kMmaWarp) {
         if (lane == 0) {
@@ -607,14 +611,15 @@ cudaError_t launch_rerank(const float* rows32, int dim, int dp, const int* lists
 template <int KC>
 cudaError_t launch_filter_kc(const uint8_t* tiles, const float* qa, const float* pb, int n, int ntiles,
                              int cap, int* lists, int* counts, int* overflow, int* n_overflow, int* err,
-                             int qb_begin, int qb_end, cudaStream_t s, const uint8_t* qtiles) {
+                             int qb_begin, int qb_end, cudaStream_t s, const uint8_t* qtiles, int skip_tile) {
     const size_t smem = Cfg<KC>::kSmem;
     cudaError_t e =
         cudaFuncSetAttribute(filter_kernel<KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     if (qb_end <= qb_begin) return cudaSuccess;
     filter_kernel<KC><<<(qb_end - qb_begin + 1) / 2, kThreads, smem, s>>>(
-        tiles, qa, pb, n, ntiles, cap, lists, counts, overflow, n_overflow, err, qb_begin, qb_end, qtiles);
+        tiles, qa, pb, n, ntiles, cap, lists, counts, overflow, n_overflow, err, qb_begin, qb_end, qtiles,
+        skip_tile);
     return cudaGetLastError();
 }
 
@@ -642,7 +647,8 @@ cudaError_t launch_tc_prep(const float* pts, int n, int dim, const float* center
 
 cudaError_t launch_tc_filter(const uint8_t* tiles, const float* qa, const float* pb, int n, int dim,
                              int cap, int* lists, int* counts, int* overflow, int* n_overflow, int* err,
-                             int qb_begin, int qb_end, cudaStream_t s, const uint8_t* qtiles, int m) {
+                             int qb_begin, int qb_end, cudaStream_t s, const uint8_t* qtiles, int m,
+                             int skip_tile) {
     const int ntiles = (n + tc::kRows - 1) / tc::kRows;
     const int qtiles_n = qtiles ? (m + tc::kRows - 1) / tc::kRows : ntiles;
     if (qb_begin < 0 || qb_end > qtiles_n) return cudaErrorInvalidValue;
@@ -652,9 +658,9 @@ cudaError_t launch_tc_filter(const uint8_t* tiles, const float* qa, const float*
     }
     if (tc_kc(dim) == 1)
         return tc::launch_filter_kc<1>(tiles, qa, pb, m, ntiles, cap, lists, counts, overflow, n_overflow, err,
-                                       qb_begin, qb_end, s, qtiles);
+                                       qb_begin, qb_end, s, qtiles, skip_tile);
     return tc::launch_filter_kc<2>(tiles, qa, pb, m, ntiles, cap, lists, counts, overflow, n_overflow, err,
-                                   qb_begin, qb_end, s, qtiles);
+                                   qb_begin, qb_end, s, qtiles, skip_tile);
 }
 
 cudaError_t launch_tc_rerank(const float* rows32, int dim, const int* lists, const int* counts, int cap,

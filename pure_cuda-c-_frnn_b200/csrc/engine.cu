@@ -19,22 +19,13 @@
 #include "frnn_b200.h"
 #include "frnn_device.cuh"
 #include "frnn_internal.h"
+#include "grid_plan.cuh"
+#include "engine_state.h"
 
 using namespace frnn;
 
-namespace {
-
-struct DevBuf {
-    void* p = nullptr;
-    size_t bytes = 0;
-    template <class T>
-    T* as() const { return static_cast<T*>(p); }
-};
-
-constexpr int kBoxMaxBlocks = 1024;
-// bbox, hash, scan, scatter, search, unpermute, brute force, collect, emit,
-// tensor-core prep, tensor-core filter, exact re-rank
-#define FRNN_STAGES 12
+namespace frnn {
+namespace eng {
 
 // Brute force is taken when the all-pairs work is small enough that the grid
 // build would dominate (the reference's own small-input rule is
@@ -47,78 +38,7 @@ constexpr double kBruteSmallWork = 4.0e8;   // N*N*D below this -> brute force
 // host round trips are most of its time).
 constexpr int kTcMinPoints = 1024;
 
-}  // namespace
 
-struct frnn_engine {
-    int device = 0;
-    int max_points = 0;
-    int sms = 148;
-    cudaStream_t stream = 0;
-    int forced_path = FRNN_PATH_AUTO;
-    unsigned epoch = 0;
-    long long direct_output_max_bytes = 48LL << 20;
-
-    DevBuf box_partial, box_ticket, box_out;
-    DevBuf counts, starts, scan_status, scan_ticket, err_flag;
-    DevBuf cellrank, rows, ids, inv;
-    DevBuf lists, list_counts, overflow, n_overflow;
-    DevBuf tmp_idx, tmp_dist, out_idx, out_dist;
-    DevBuf in_stage, in_soa, out_rm_idx, out_rm_dist;
-    DevBuf tc_box, tc_center, tc_tiles, tc_rows, tc_qa, tc_pb;
-    DevBuf part_ids;          // original query index of each row of a part search
-    // principal-axis grid: moments, axes, projected coordinates, estimate
-    DevBuf pca_partial, pca_moments, pca_mu, pca_pm, proj_box_partial, proj_ticket, proj_out;
-    DevBuf proj_u, proj_s, pca_smp, pca_h, pca_counts;
-    // a separate query set: its grid (same plan as the points), projected
-    // coordinates and tensor-core tiles
-    DevBuf q_counts, q_starts, q_cellrank, q_rows, q_ids, q_inv, q_proj_u, q_proj_s, q_proj_partial,
-        q_proj_out, q_box_out;
-    DevBuf q_tiles, q_rows32, q_qa, q_pb;
-    void* h_pca = nullptr;    // pinned, 32 KiB
-    int grid_axes_mode = 0;   // FRNN_OPT_GRID_AXES
-    int list_search = 0;      // FRNN_OPT_LIST_SEARCH
-    // a point set kept for frnn_query_grid: on the grid path its sorted rows,
-    // ids, cell starts (and projected coordinates) stay in the point buffers
-    struct {
-        bool valid = false;
-        const float* pts = nullptr;
-        int N = 0, dim = 0, path = 0;
-        float radius = 0.0f;
-        bool principal = false;
-        GridPlan P{};
-    } built;
-    int last_principal = 0;   // the last grid was on principal axes
-    int last_part_rows = -1;  // rows of the last part search (-1: last search was whole)
-    float* h_box = nullptr;   // pinned, 9 floats
-    float* h_tc = nullptr;    // pinned, 512 floats: per-dimension box + flag, then the centre
-    int* h_err = nullptr;     // pinned
-
-    int last_N = -1, last_K = -1;
-    int last_path = 0, last_g = 0;
-    long long last_cells = 0;
-    std::string last_error;
-
-    // per-stage device timing (frnn_set_timing); stage s spans events
-    // ev[2s] .. ev[2s+1] on the engine stream
-    bool timing = false;
-    cudaEvent_t ev[2 * FRNN_STAGES] = {};
-    bool stage_used[FRNN_STAGES] = {};
-    long long launches = 0;
-};
-
-namespace {
-
-struct DeviceGuard {
-    int prev = -1;
-    explicit DeviceGuard(int dev) {
-        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
-        if (prev != dev) cudaSetDevice(dev);
-    }
-    ~DeviceGuard() {
-        int cur = -1;
-        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
-    }
-};
 
 int fail(frnn_engine* e, int status, const std::string& msg) {
     if (e) e->last_error = msg;
@@ -130,12 +50,6 @@ int cuda_fail(frnn_engine* e, cudaError_t err, const char* what) {
     cudaGetLastError();  // clear a sticky launch error so the engine stays usable
     return fail(e, err == cudaErrorMemoryAllocation ? FRNN_ERR_OOM : FRNN_ERR_CUDA, m);
 }
-
-#define FRNN_CHECK(e, call, what)                          \
-    do {                                                   \
-        cudaError_t err__ = (call);                        \
-        if (err__ != cudaSuccess) return cuda_fail(e, err__, what); \
-    } while (0)
 
 int grow(frnn_engine* e, DevBuf& b, size_t bytes, const char* what) {
     if (bytes == 0) bytes = 16;
@@ -157,16 +71,17 @@ int grow(frnn_engine* e, DevBuf& b, size_t bytes, const char* what) {
     return FRNN_OK;
 }
 
-#define FRNN_GROW(e, buf, bytes)                                   \
-    do {                                                           \
-        int st__ = grow(e, buf, bytes, #buf);                      \
-        if (st__ != FRNN_OK) return st__;                          \
-    } while (0)
-
-enum Stage {
-    ST_BBOX = 0, ST_HASH, ST_SCAN, ST_SCATTER, ST_SEARCH, ST_UNPERMUTE, ST_BRUTE, ST_COLLECT, ST_EMIT,
-    ST_TC_PREP, ST_TC_FILTER, ST_TC_RERANK
-};
+// The scan's look-back status words carry the epoch of the search that wrote
+// them, and every engine counts epochs from 1: a status buffer that reuses
+// memory another engine (or anything else) wrote could hold words that look
+// current.  So a newly allocated buffer is cleared before its first scan.
+int grow_scan_status(frnn_engine* e, size_t bytes) {
+    const size_t before = e->scan_status.bytes;
+    FRNN_GROW(e, e->scan_status, bytes);
+    if (e->scan_status.bytes != before)  // reallocated (grow never shrinks)
+        FRNN_CHECK(e, cudaMemsetAsync(e->scan_status.p, 0, e->scan_status.bytes, e->stream), "memset status");
+    return FRNN_OK;
+}
 
 void stage_begin(frnn_engine* e, int st) {
     if (e->timing) cudaEventRecord(e->ev[2 * st], e->stream);
@@ -261,6 +176,14 @@ __global__ void iota_kernel(int* __restrict__ out, int base, int n) {
     if (i < n) out[i] = base + i;
 }
 
+// out[j] = original query index of overflow entry j < min(*n, max_out)
+__global__ void overflow_ids_kernel(const int* __restrict__ ovf, const int* __restrict__ n,
+                                    const int* __restrict__ map, int max_out, int* __restrict__ out) {
+    const int cnt = min(*n, max_out);
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < cnt; j += gridDim.x * blockDim.x)
+        out[j] = map ? map[ovf[j]] : ovf[j];
+}
+
 cudaError_t launch_iota(int* out, int base, int n, cudaStream_t s) {
     iota_kernel<<<(n + 255) / 256, 256, 0, s>>>(out, base, n);
     return cudaGetLastError();
@@ -278,83 +201,16 @@ cudaError_t launch_transpose(const void* in, void* out, int rows, int cols, cuda
 
 int grid_axes_for(int dim) { return dim <= 4 ? dim : 4; }
 
-int row_floats(int dim) {
-    if (dim == 3) return 4;
-    int r = (dim + 3) / 4 * 4;
-    if (r > 16 && r <= 32) r = 32;
-    return r;
-}
-
-// Build the grid plan from the box.  Returns false when a grid is useless
-// (every query would scan nearly everything) or cannot be formed.
-// Plan a grid on g axes whose bounding box is box[2d], box[2d+1]; `extra` is
-// an absolute allowance added to the cell edge (the rounding bound of
-// projected coordinates; 0 for the data's own coordinates).
+// Build the grid plan from the box of the grid axes (plan_grid): false when a
+// grid is useless or cannot be formed.  The dense cell table may hold
+// `cells_per_point` cells per point (at least 2^22): 12 bytes of build traffic
+// per cell, and sparse clouds such as Gaussian mixtures leave most cells
+// empty, while coarser cells would multiply the candidates of every query.
 bool make_plan_axes(const float* box, int g, int N, int dim, float radius, double extra, GridPlan& P,
                     long long cells_per_point = 32) {
-    double ext_max = 0.0, mag = 0.0;
-    for (int d = 0; d < g; ++d) {
-        double lo = box[2 * d], hi = box[2 * d + 1];
-        ext_max = std::max(ext_max, hi - lo);
-        mag = std::max(mag, std::max(std::fabs(lo), std::fabs(hi)));
-    }
-    // Cell edge slightly above r: a point within r of the query then lies in
-    // the query's 3^g shell despite float rounding of the cell assignment
-    // (|error| of (x-origin)*inv_cell is a few ulps of the cell index).
-    const double u = 1.0 / 16777216.0;
-    double cell = (double)radius * (1.0 + 1e-5 + 8.0 * u * (ext_max / radius + 2.0)) + extra;
-    // Dense cell table budget: 32 cells per point by default (12 bytes of
-    // build traffic per cell); sparse clouds such as Gaussian mixtures leave
-    // most cells empty, and coarser cells would multiply the candidates of
-    // every query.
     const long long budget = std::min<long long>(std::max<long long>(1LL << 22, cells_per_point * N),
                                                  (1LL << 31) - 2);
-    long long res[kMaxGridAxes];
-    long long cells = 1;
-    for (int iter = 0; iter < 64; ++iter) {
-        cells = 1;
-        bool over = false;
-        for (int d = 0; d < g; ++d) {
-            double ext = (double)box[2 * d + 1] - (double)box[2 * d];
-            res[d] = (long long)std::floor(ext / cell) + 1;
-            if (res[d] > (1LL << 30)) { over = true; break; }
-            cells *= res[d];
-            if (cells > budget) { over = true; break; }
-        }
-        if (!over) break;
-        cell *= 1.25;  // coarser cells keep cr = 1 valid, only the work grows
-    }
-    if (cells > budget) return false;
-    bool useful = false;
-    for (int d = 0; d < g; ++d) useful |= res[d] > 3;
-    if (!useful) return false;
-    P.g = g;
-    P.n = N;
-    P.dim = dim;
-    P.row = row_floats(dim);
-    P.cell = (float)cell;
-    P.inv_cell = 1.0f / P.cell;
-    // Recompute resolutions with the float cell actually used by the kernels:
-    // the largest coordinate must map inside the grid.
-    long long s = 1;
-    for (int d = 0; d < kMaxGridAxes; ++d) {
-        if (d < g) {
-            P.origin[d] = box[2 * d];
-            int c = (int)std::floor((box[2 * d + 1] - P.origin[d]) * P.inv_cell);
-            res[d] = std::max<long long>(res[d], (long long)c + 1);
-            P.res[d] = (int)res[d];
-            P.stride[d] = s;
-            s *= res[d];
-        } else {
-            P.origin[d] = 0.0f;
-            P.res[d] = 1;
-            P.stride[d] = s;
-        }
-    }
-    P.cells = s;
-    if (P.cells > (1LL << 31) - 2) return false;
-    P.eps = (float)(std::ldexp(1.0, -20) * (mag + ext_max)) + 1e-30f;
-    return true;
+    return plan_grid(box, g, N, dim, radius, extra, budget, P);
 }
 
 bool make_plan(const float* box, int N, int dim, float radius, GridPlan& P) {
@@ -552,14 +408,25 @@ bool list_search_nd(const frnn_engine* e, const GridPlan& P) {
     return P.row <= 12;
 }
 
-int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2,
-             const GridPlan& P, int* out_idx, float* out_dist, bool part, int& s0, int& s1,
-             const float* proj) {
+// Whether a grid search over plan P with K neighbours takes the list search
+// (collect + emit): D = 3 on its own coordinates always, other D as
+// list_search_nd decides; K <= 32 only.
+bool uses_lists(const frnn_engine* e, const GridPlan& P, int K, bool principal) {
+    const bool d3 = P.dim == 3 && P.g == 3 && !principal;
+    return K <= 32 && (d3 || list_search_nd(e, P));
+}
+
+int build_points(frnn_engine* e, const float* d_pts, const GridPlan& P, const float* proj, bool with_inv,
+                 unsigned long long* tile_work) {
     cudaStream_t s = e->stream;
+    const int N = P.n;
     FRNN_GROW(e, e->counts, (size_t)P.cells * 4);
     FRNN_GROW(e, e->starts, ((size_t)P.cells + 1) * 4);
     const long long tiles = scan_tiles(P.cells);
-    FRNN_GROW(e, e->scan_status, (size_t)tiles * 8);
+    {
+        const int st = grow_scan_status(e, (size_t)tiles * 8);
+        if (st != FRNN_OK) return st;
+    }
     FRNN_GROW(e, e->cellrank, (size_t)N * 8);
     // padded: the D = 3 collect kernel reads whole 8-row passes
     FRNN_GROW(e, e->rows, ((size_t)N + kCollectRowPad) * P.row * 4);
@@ -581,51 +448,42 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
     stage_begin(e, ST_SCAN);
     FRNN_CHECK(e, launch_scan(e->counts.as<int>(), e->starts.as<int>(), P.cells,
                               e->scan_status.as<unsigned long long>(), e->scan_ticket.as<int>(),
-                              e->epoch, e->err_flag.as<int>(), s),
+                              e->epoch, e->err_flag.as<int>(), s,
+                              e->test_stall == FRNN_TEST_STALL_SCAN ? 1 : -1, tile_work),
                "scan launch");
     stage_end(e, ST_SCAN);
-    if (part) {
-        // part boundaries move to cell boundaries, so that parts searched by
-        // separate builds cover every query exactly once
-        int* h = reinterpret_cast<int*>(e->h_tc);
-        FRNN_CHECK(e, launch_cell_floor(e->starts.as<int>(), P.cells, s0, s1, e->scan_ticket.as<int>() + 1, s),
-                   "cell floor launch");
-        FRNN_CHECK(e, cudaMemcpyAsync(h, e->scan_ticket.as<int>() + 1, 2 * sizeof(int), cudaMemcpyDeviceToHost, s),
-                   "part bounds readback");
-        FRNN_CHECK(e, cudaStreamSynchronize(s), "part bounds sync");
-        s0 = s0 >= N ? N : h[0];
-        s1 = s1 >= N ? N : h[1];
-    }
-    // K <= 32: collect every in-radius key per query into a list, then sort and
-    // emit in original order (D = 3 always; other dimensions as
-    // list_search_nd decides)
-    const bool d3 = P.dim == 3 && P.g == 3 && !proj;
-    const bool two_kernel = K <= 32 && (d3 || list_search_nd(e, P));
-    if (two_kernel) FRNN_GROW(e, e->inv, (size_t)N * 4);
-    const float* proj_s = nullptr;
-    if (proj) {
-        FRNN_GROW(e, e->proj_s, (size_t)N * kProjStride * 4);
-        proj_s = e->proj_s.as<float>();
-    }
+    if (with_inv) FRNN_GROW(e, e->inv, (size_t)N * 4);
+    if (proj) FRNN_GROW(e, e->proj_s, (size_t)N * kProjStride * 4);
     stage_begin(e, ST_SCATTER);
     FRNN_CHECK(e, launch_scatter(d_pts, P, e->cellrank.as<int2>(), e->starts.as<int>(),
                                  e->rows.as<float>(), e->ids.as<int>(), s,
-                                 two_kernel ? e->inv.as<int>() : nullptr, proj,
+                                 with_inv ? e->inv.as<int>() : nullptr, proj,
                                  proj ? e->proj_s.as<float>() : nullptr),
                "scatter launch");
     stage_end(e, ST_SCATTER);
     e->launches += 2;
-    if (two_kernel) {
-        // D = 3: collect every in-radius key per query, then sort and emit in
-        // original query order (no unpermute); queries whose list overflows
-        // are searched again by the cooperative kernel.
+    return FRNN_OK;
+}
+
+int search_built(frnn_engine* e, const GridPlan& P, bool principal, int K, float r2, int q0, int q1,
+                 bool whole, int* out_idx, float* out_dist) {
+    cudaStream_t s = e->stream;
+    const int N = P.n;
+    const float* proj_s = principal ? e->proj_s.as<float>() : nullptr;
+    const bool d3 = P.dim == 3 && P.g == 3 && !principal;
+    const int rows = q1 - q0;
+    if (uses_lists(e, P, K, principal)) {
+        // collect every in-radius key per query, then sort and emit (whole:
+        // original query order through inv, no unpermute; slice: sorted
+        // order); queries whose list overflows are searched again by the
+        // cooperative kernel.
         const int cap = K <= 16 ? 64 : 128;
         FRNN_GROW(e, e->lists, (size_t)N * cap * 8);
         FRNN_GROW(e, e->list_counts, (size_t)N * 4);
         FRNN_GROW(e, e->overflow, (size_t)N * 4);
         FRNN_GROW(e, e->n_overflow, 16);
         FRNN_CHECK(e, cudaMemsetAsync(e->n_overflow.p, 0, 4, s), "memset overflow count");
-        const int q0 = part ? s0 : 0, q1 = part ? s1 : N, rows = q1 - q0;
+        e->last_overflow_map = whole ? 1 : 0;
         stage_begin(e, ST_COLLECT);
         if (d3)
             FRNN_CHECK(e, launch_collect_d3(e->rows.as<float>(), e->starts.as<int>(), P, r2, cap,
@@ -640,14 +498,13 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
                        "collect launch");
         stage_end(e, ST_COLLECT);
         stage_begin(e, ST_EMIT);
-        // whole: rows in original order through inv; part: rows in sorted order
         FRNN_CHECK(e, launch_emit_lists(e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
-                                        part ? nullptr : e->inv.as<int>(), q0, rows, K, cap, r2,
+                                        whole ? e->inv.as<int>() : nullptr, q0, rows, K, cap, r2,
                                         out_idx, out_dist, s),
                    "emit launch");
         FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(),
                                          P, K, r2, 0, N, out_idx, out_dist, rows,
-                                         part ? nullptr : e->ids.as<int>(), s, e->overflow.as<int>(),
+                                         whole ? e->ids.as<int>() : nullptr, s, e->overflow.as<int>(),
                                          e->n_overflow.as<int>(), q0, proj_s),
                    "overflow search launch");
         stage_end(e, ST_EMIT);
@@ -658,10 +515,10 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
     // scattered stores stay in L2).  Large ones: write in cell order, then
     // unpermute one output row at a time.
     const long long out_bytes = (long long)N * K * 8;
-    if (part) {
+    if (!whole) {
         stage_begin(e, ST_SEARCH);
         FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(), P, K,
-                                         r2, s0, s1, out_idx, out_dist, s1 - s0, nullptr, s, nullptr,
+                                         r2, q0, q1, out_idx, out_dist, rows, nullptr, s, nullptr,
                                          nullptr, -1, proj_s),
                    "grid search launch");
         stage_end(e, ST_SEARCH);
@@ -695,25 +552,50 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
     return FRNN_OK;
 }
 
-// Brute force with the tcgen05 distance filter (bf_tc.cu).  Sets *done = false
-// (and launches nothing that writes results) when the data do not suit the
-// filter -- non-finite coordinates, or a radius whose scaled square is not a
-// finite fp32 -- and the caller runs the SIMT brute force instead.
-// Queries [qb_begin*128, min(N, qb_end*128)) (all of them for a whole search),
-// results to rows q - qb_begin*128 of out[k*rows + row].
-int run_brute_tc(frnn_engine* e, const float* d_pts, int N, int dim, int K, float radius,
-                 int* out_idx, float* out_dist, int qb_begin, int qb_end, bool* done,
-                 const float* d_q = nullptr, int M = 0) {
-    // d_q: a separate query set of M points (tiles [qb_begin, qb_end) of its
-    // own); the points themselves otherwise
+// Whole search (part == false): results for every query in original order,
+// out[k*N + q].  Part search: the queries at sorted positions [s0, s1) only,
+// rounded to cell starts, row j = sorted position s0 + j of
+// out[k*(s1-s0) + j].  proj: the points' projected coordinates when P is a
+// principal-axis grid.
+int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2,
+             const GridPlan& P, int* out_idx, float* out_dist, bool part, int& s0, int& s1,
+             const float* proj) {
     cudaStream_t s = e->stream;
-    *done = false;
+    const bool principal = proj != nullptr;
+    int st = build_points(e, d_pts, P, proj, !part && uses_lists(e, P, K, principal), nullptr);
+    if (st != FRNN_OK) return st;
+    if (part) {
+        // part boundaries move to cell boundaries, so that parts searched by
+        // separate builds cover every query exactly once
+        int* h = reinterpret_cast<int*>(e->h_tc);
+        FRNN_CHECK(e, launch_cell_floor(e->starts.as<int>(), P.cells, s0, s1, e->scan_ticket.as<int>() + 1, s),
+                   "cell floor launch");
+        FRNN_CHECK(e, cudaMemcpyAsync(h, e->scan_ticket.as<int>() + 1, 2 * sizeof(int), cudaMemcpyDeviceToHost, s),
+                   "part bounds readback");
+        FRNN_CHECK(e, cudaStreamSynchronize(s), "part bounds sync");
+        s0 = s0 >= N ? N : h[0];
+        s1 = s1 >= N ? N : h[1];
+    }
+    return search_built(e, P, principal, K, r2, part ? s0 : 0, part ? s1 : N, !part, out_idx, out_dist);
+}
+
+// Brute force with the tcgen05 distance filter (bf_tc.cu), in two halves.
+//
+// tc_plan: the per-dimension box of the points (and of a separate query set
+// d_q of M points), read back to the host, gives the centre and power-of-two
+// scale of the fp16 tiles and the filter's threshold constants.  tp->ok is
+// false (nothing else launched) when the data do not suit the filter --
+// non-finite coordinates, or a radius whose scaled square is not a finite
+// fp32 -- and the caller runs the SIMT brute force instead.
+int tc_plan(frnn_engine* e, const float* d_pts, int N, int dim, float radius, TcPlan* tp,
+            const float* d_q, int M) {
+    cudaStream_t s = e->stream;
+    tp->ok = false;
     const bool sep = d_q != nullptr;
-    const int Q = sep ? M : N;
     const float r2 = radius * radius;
     FRNN_GROW(e, e->tc_box, 1024 * sizeof(float) + 16);
     int* nonfinite = reinterpret_cast<int*>(e->tc_box.as<float>() + 1024);
-    stage_begin(e, ST_TC_PREP);
+    stage_begin(e, ST_BBOX);
     FRNN_CHECK(e, cudaMemsetAsync(nonfinite, 0, sizeof(int), s), "memset non-finite flag");
     FRNN_CHECK(e, launch_tc_box(d_pts, N, dim, e->tc_box.as<float>(), nonfinite, s), "box launch");
     e->launches++;
@@ -721,6 +603,7 @@ int run_brute_tc(frnn_engine* e, const float* d_pts, int N, int dim, int K, floa
         FRNN_CHECK(e, launch_tc_box(d_q, M, dim, e->tc_box.as<float>() + 512, nonfinite, s), "box launch");
         e->launches++;
     }
+    stage_end(e, ST_BBOX);
     float* hq = static_cast<float*>(e->h_pca) + 6144;  // the query set's box
     FRNN_CHECK(e, cudaMemcpyAsync(e->h_tc, e->tc_box.p, 2 * dim * sizeof(float), cudaMemcpyDeviceToHost, s),
                "box readback");
@@ -738,7 +621,6 @@ int run_brute_tc(frnn_engine* e, const float* d_pts, int N, int dim, int K, floa
     // centre = per-dimension midpoint of the box of points (and queries);
     // scale = 2^(14 - e) with max|x - c| < 2^e, so every scaled coordinate
     // stays below 2^14 in magnitude (fp16 max 65504)
-    float* center = e->h_tc + 2 * kMaxK + 4;
     double hmax = 0.0;
     for (int d = 0; d < dim; ++d) {
         double lo = e->h_tc[2 * d], hi = e->h_tc[2 * d + 1];
@@ -746,8 +628,8 @@ int run_brute_tc(frnn_engine* e, const float* d_pts, int N, int dim, int K, floa
             lo = std::min(lo, (double)hq[2 * d]);
             hi = std::max(hi, (double)hq[2 * d + 1]);
         }
-        center[d] = (float)(0.5 * (lo + hi));
-        hmax = std::max(hmax, std::max(hi - (double)center[d], (double)center[d] - lo));
+        tp->center[d] = (float)(0.5 * (lo + hi));
+        hmax = std::max(hmax, std::max(hi - (double)tp->center[d], (double)tp->center[d] - lo));
     }
     int ex = 0;
     if (hmax > 0.0) std::frexp(hmax * (1.0 + 1e-6), &ex);
@@ -758,9 +640,25 @@ int run_brute_tc(frnn_engine* e, const float* d_pts, int N, int dim, int K, floa
     float rc = (float)rcd;
     if ((double)rc < rcd) rc = std::nextafter(rc, INFINITY);
     if (!std::isfinite(rc)) return FRNN_OK;
-    const float one_minus_alpha = 1.0f - std::ldexp(1.0f, -8);
-    const float eta_c = (float)(4.0 * eta * std::sqrt((double)dim));
+    tp->scale = (float)scale;
+    tp->rc = rc;
+    tp->one_minus_alpha = 1.0f - std::ldexp(1.0f, -8);
+    tp->eta_c = (float)(4.0 * eta * std::sqrt((double)dim));
+    tp->ok = true;
+    return FRNN_OK;
+}
 
+// tc_search: fp16 tiles, fp32 rows and threshold terms of the points (and of
+// the separate query set), the tensor-core filter over query tiles
+// [qb_begin, qb_end), the exact fp32 re-rank, and the SIMT brute force for
+// queries whose candidate list overflowed.  Queries [qb_begin*128,
+// min(Q, qb_end*128)), results to rows q - qb_begin*128 of out[k*rows + row].
+int tc_search(frnn_engine* e, const float* d_pts, int N, int dim, int K, float radius, const TcPlan& tp,
+              int* out_idx, float* out_dist, int qb_begin, int qb_end, const float* d_q, int M) {
+    cudaStream_t s = e->stream;
+    const bool sep = d_q != nullptr;
+    const int Q = sep ? M : N;
+    const float r2 = radius * radius;
     const int ntiles = (N + 127) / 128, qtiles = (Q + 127) / 128;
     const int dp = tc_row_floats(dim);
     const int cap = tc_list_cap(K);
@@ -773,10 +671,14 @@ int run_brute_tc(frnn_engine* e, const float* d_pts, int N, int dim, int K, floa
     FRNN_GROW(e, e->list_counts, (size_t)Q * 4);
     FRNN_GROW(e, e->overflow, (size_t)Q * 4);
     FRNN_GROW(e, e->n_overflow, 16);
-    FRNN_CHECK(e, cudaMemcpyAsync(e->tc_center.p, center, (size_t)dim * 4, cudaMemcpyHostToDevice, s),
+    // the centre goes through pinned staging (the caller's plan may be on the stack)
+    float* hcenter = e->h_tc + 2 * kMaxK + 4;
+    std::memcpy(hcenter, tp.center, (size_t)dim * 4);
+    stage_begin(e, ST_TC_PREP);
+    FRNN_CHECK(e, cudaMemcpyAsync(e->tc_center.p, hcenter, (size_t)dim * 4, cudaMemcpyHostToDevice, s),
                "centre upload");
-    FRNN_CHECK(e, launch_tc_prep(d_pts, N, dim, e->tc_center.as<float>(), (float)scale, one_minus_alpha,
-                                 eta_c, rc, e->tc_tiles.as<uint8_t>(), e->tc_rows.as<float>(),
+    FRNN_CHECK(e, launch_tc_prep(d_pts, N, dim, e->tc_center.as<float>(), tp.scale, tp.one_minus_alpha,
+                                 tp.eta_c, tp.rc, e->tc_tiles.as<uint8_t>(), e->tc_rows.as<float>(),
                                  e->tc_qa.as<float>(), e->tc_pb.as<float>(), s),
                "prep launch");
     e->launches++;
@@ -787,8 +689,8 @@ int run_brute_tc(frnn_engine* e, const float* d_pts, int N, int dim, int K, floa
         FRNN_GROW(e, e->q_rows32, (size_t)M * dp * 4);
         FRNN_GROW(e, e->q_qa, (size_t)qtiles * 128 * 4);
         FRNN_GROW(e, e->q_pb, (size_t)qtiles * 128 * 4);
-        FRNN_CHECK(e, launch_tc_prep(d_q, M, dim, e->tc_center.as<float>(), (float)scale, one_minus_alpha,
-                                     eta_c, rc, e->q_tiles.as<uint8_t>(), e->q_rows32.as<float>(),
+        FRNN_CHECK(e, launch_tc_prep(d_q, M, dim, e->tc_center.as<float>(), tp.scale, tp.one_minus_alpha,
+                                     tp.eta_c, tp.rc, e->q_tiles.as<uint8_t>(), e->q_rows32.as<float>(),
                                      e->q_qa.as<float>(), e->q_pb.as<float>(), s),
                    "query prep launch");
         e->launches++;
@@ -797,11 +699,13 @@ int run_brute_tc(frnn_engine* e, const float* d_pts, int N, int dim, int K, floa
     stage_end(e, ST_TC_PREP);
     const int q0 = qb_begin * 128, q1 = std::min(Q, qb_end * 128), rows = q1 - q0;
     FRNN_CHECK(e, cudaMemsetAsync(e->n_overflow.p, 0, 4, s), "memset overflow count");
+    e->last_overflow_map = 2;
     stage_begin(e, ST_TC_FILTER);
     FRNN_CHECK(e, launch_tc_filter(e->tc_tiles.as<uint8_t>(), qa, e->tc_pb.as<float>(), N, dim, cap,
                                    e->lists.as<int>(), e->list_counts.as<int>(), e->overflow.as<int>(),
                                    e->n_overflow.as<int>(), e->err_flag.as<int>(), qb_begin, qb_end, s,
-                                   sep ? e->q_tiles.as<uint8_t>() : nullptr, Q),
+                                   sep ? e->q_tiles.as<uint8_t>() : nullptr, Q,
+                                   e->test_stall == FRNN_TEST_STALL_TC_FILTER ? 1 : -1),
                "filter launch");
     stage_end(e, ST_TC_FILTER);
     stage_begin(e, ST_TC_RERANK);
@@ -824,6 +728,20 @@ int run_brute_tc(frnn_engine* e, const float* d_pts, int N, int dim, int K, floa
         stage_end(e, ST_BRUTE);
         e->launches++;
     }
+    return FRNN_OK;
+}
+
+// Both halves; *done = false when the filter does not suit the data (the
+// caller then runs the SIMT brute force).
+int run_brute_tc(frnn_engine* e, const float* d_pts, int N, int dim, int K, float radius,
+                 int* out_idx, float* out_dist, int qb_begin, int qb_end, bool* done,
+                 const float* d_q = nullptr, int M = 0) {
+    *done = false;
+    TcPlan tp;
+    int st = tc_plan(e, d_pts, N, dim, radius, &tp, d_q, M);
+    if (st != FRNN_OK || !tp.ok) return st;
+    st = tc_search(e, d_pts, N, dim, K, radius, tp, out_idx, out_dist, qb_begin, qb_end, d_q, M);
+    if (st != FRNN_OK) return st;
     *done = true;
     return FRNN_OK;
 }
@@ -837,9 +755,13 @@ int sort_into_cells(frnn_engine* e, const float* pts, const GridPlan& P, const f
     const int n = P.n;
     FRNN_GROW(e, counts, (size_t)P.cells * 4);
     FRNN_GROW(e, starts, ((size_t)P.cells + 1) * 4);
-    FRNN_GROW(e, e->scan_status, (size_t)scan_tiles(P.cells) * 8);
+    {
+        const int st = grow_scan_status(e, (size_t)scan_tiles(P.cells) * 8);
+        if (st != FRNN_OK) return st;
+    }
     FRNN_GROW(e, cellrank, (size_t)n * 8);
-    FRNN_GROW(e, rows, (size_t)n * P.row * 4);
+    // padded: the D = 3 collect kernel reads whole 8-row passes
+    FRNN_GROW(e, rows, ((size_t)n + kCollectRowPad) * P.row * 4);
     FRNN_GROW(e, ids, (size_t)n * 4);
     if (inv) FRNN_GROW(e, *inv, (size_t)n * 4);
     if (proj) FRNN_GROW(e, *proj_s, (size_t)n * kProjStride * 4);
@@ -852,7 +774,8 @@ int sort_into_cells(frnn_engine* e, const float* pts, const GridPlan& P, const f
         e->epoch = 1;
     }
     FRNN_CHECK(e, launch_scan(counts.as<int>(), starts.as<int>(), P.cells, e->scan_status.as<unsigned long long>(),
-                              e->scan_ticket.as<int>(), e->epoch, e->err_flag.as<int>(), s),
+                              e->scan_ticket.as<int>(), e->epoch, e->err_flag.as<int>(), s,
+                              e->test_stall == FRNN_TEST_STALL_SCAN ? 1 : -1),
                "scan launch");
     FRNN_CHECK(e, launch_scatter(pts, P, cellrank.as<int2>(), starts.as<int>(), rows.as<float>(), ids.as<int>(), s,
                                  inv ? inv->as<int>() : nullptr, proj, proj ? proj_s->as<float>() : nullptr),
@@ -886,6 +809,7 @@ int search_sorted_queries(frnn_engine* e, const float* d_q, int M, int K, float 
         FRNN_GROW(e, e->overflow, (size_t)M * 4);
         FRNN_GROW(e, e->n_overflow, 16);
         FRNN_CHECK(e, cudaMemsetAsync(e->n_overflow.p, 0, 4, s), "memset overflow count");
+        e->last_overflow_map = 3;
         stage_begin(e, ST_COLLECT);
         if (d3)
             FRNN_CHECK(e, launch_collect_d3(e->rows.as<float>(), e->starts.as<int>(), P, r2, cap,
@@ -1012,6 +936,7 @@ int search_queries_core(frnn_engine* e, const float* d_pts, int N, const float* 
     e->last_N = -1;
     e->last_part_rows = -1;
     e->built.valid = false;  // the point buffers are about to be overwritten
+    e->last_overflow_map = 0;
     for (int i = 0; i < FRNN_STAGES; ++i) e->stage_used[i] = false;
     int path = e->forced_path;
     if (path == FRNN_PATH_AUTO) {
@@ -1113,6 +1038,44 @@ int search_queries_core(frnn_engine* e, const float* d_pts, int N, const float* 
     return FRNN_OK;
 }
 
+int self_search_path(const frnn_engine* e, int N, int dim) {
+    int path = e->forced_path;
+    if (path == FRNN_PATH_AUTO) {
+        const double work = (double)N * (double)N * dim;
+        if (dim > 32) path = N >= kTcMinPoints ? FRNN_PATH_BRUTE_TC : FRNN_PATH_BRUTE;
+        else if (work <= kBruteSmallWork) path = FRNN_PATH_BRUTE;
+        else path = FRNN_PATH_GRID;
+    }
+    if (path == FRNN_PATH_GRID && dim > 32) path = FRNN_PATH_BRUTE;
+    return path;
+}
+
+int plan_grid_search(frnn_engine* e, const float* d_pts, int N, int dim, float radius, int* path, GridPlan& P,
+                     bool* principal) {
+    cudaStream_t s = e->stream;
+    *principal = false;
+    const int g = grid_axes_for(dim);
+    const int blocks = std::min(bbox_blocks(N, e->sms), kBoxMaxBlocks);
+    stage_begin(e, ST_BBOX);
+    FRNN_CHECK(e, launch_bbox(d_pts, N, g, e->box_partial.as<float>(), e->box_ticket.as<unsigned>(),
+                              e->box_out.as<float>(), blocks, s),
+               "bbox launch");
+    stage_end(e, ST_BBOX);
+    e->launches++;
+    FRNN_CHECK(e, cudaMemcpyAsync(e->h_box, e->box_out.p, 9 * sizeof(float), cudaMemcpyDeviceToHost, s),
+               "bbox readback");
+    FRNN_CHECK(e, cudaStreamSynchronize(s), "bbox sync");
+    if (e->h_box[8] != 0.0f) return fail(e, FRNN_ERR_INVALID_ARG, "points contain NaN or Inf coordinates");
+    bool grid_ok = make_plan(e->h_box, N, dim, radius, P);
+    if (dim > 4 && dim <= kMaxPcaDim && e->grid_axes_mode != FRNN_GRID_AXES_LEADING) {
+        int st = plan_principal(e, d_pts, N, dim, radius, grid_ok, P, principal);
+        if (st != FRNN_OK) return st;
+        grid_ok |= *principal;
+    }
+    if (!grid_ok) *path = FRNN_PATH_BRUTE;
+    return FRNN_OK;
+}
+
 // Whole search (nparts == 0): every query, results out[k*N + q].  Part search
 // (0 <= part < nparts): the part-th of nparts contiguous slices of the path's
 // query order -- cell order on the grid path, input order on brute force,
@@ -1131,16 +1094,10 @@ int search_core(frnn_engine* e, const float* d_pts, int N, int dim, int K, float
     e->last_N = -1;
     e->last_part_rows = -1;
     e->built.valid = false;  // the point buffers are about to be overwritten
+    e->last_overflow_map = 0;
 
     for (int i = 0; i < FRNN_STAGES; ++i) e->stage_used[i] = false;
-    int path = e->forced_path;
-    if (path == FRNN_PATH_AUTO) {
-        const double work = (double)N * (double)N * dim;
-        if (dim > 32) path = N >= kTcMinPoints ? FRNN_PATH_BRUTE_TC : FRNN_PATH_BRUTE;
-        else if (work <= kBruteSmallWork) path = FRNN_PATH_BRUTE;
-        else path = FRNN_PATH_GRID;
-    }
-    if (path == FRNN_PATH_GRID && dim > 32) path = FRNN_PATH_BRUTE;
+    int path = self_search_path(e, N, dim);
 
     // this call's slice: [s0, s1) of the query order (tiles [qb0, qb1) on the
     // tensor-core path)
@@ -1158,28 +1115,10 @@ int search_core(frnn_engine* e, const float* d_pts, int N, int dim, int K, float
     int rows = s1 - s0;
 
     GridPlan P{};
-    bool grid_ok = false, principal = false;
+    bool principal = false;
     if (path == FRNN_PATH_GRID) {
-        const int g = grid_axes_for(dim);
-        const int blocks = std::min(bbox_blocks(N, e->sms), kBoxMaxBlocks);
-        stage_begin(e, ST_BBOX);
-        FRNN_CHECK(e, launch_bbox(d_pts, N, g, e->box_partial.as<float>(), e->box_ticket.as<unsigned>(),
-                                  e->box_out.as<float>(), blocks, s),
-                   "bbox launch");
-        stage_end(e, ST_BBOX);
-        e->launches++;
-        FRNN_CHECK(e, cudaMemcpyAsync(e->h_box, e->box_out.p, 9 * sizeof(float), cudaMemcpyDeviceToHost, s),
-                   "bbox readback");
-        FRNN_CHECK(e, cudaStreamSynchronize(s), "bbox sync");
-        if (e->h_box[8] != 0.0f)
-            return fail(e, FRNN_ERR_INVALID_ARG, "points contain NaN or Inf coordinates");
-        grid_ok = make_plan(e->h_box, N, dim, radius, P);
-        if (dim > 4 && dim <= kMaxPcaDim && e->grid_axes_mode != FRNN_GRID_AXES_LEADING) {
-            int st = plan_principal(e, d_pts, N, dim, radius, grid_ok, P, &principal);
-            if (st != FRNN_OK) return st;
-            grid_ok |= principal;
-        }
-        if (!grid_ok) path = FRNN_PATH_BRUTE;
+        int st = plan_grid_search(e, d_pts, N, dim, radius, &path, P, &principal);
+        if (st != FRNN_OK) return st;
     }
 
     if (path == FRNN_PATH_BRUTE_TC) {
@@ -1238,7 +1177,10 @@ int search_core(frnn_engine* e, const float* d_pts, int N, int dim, int K, float
     return FRNN_OK;
 }
 
-}  // namespace
+}  // namespace eng
+}  // namespace frnn
+
+using namespace frnn::eng;
 
 // ---- C ABI ------------------------------------------------------------------------
 
@@ -1315,7 +1257,7 @@ int frnn_destroy(frnn_engine* e) {
                           &e->proj_u, &e->proj_s, &e->pca_smp, &e->pca_h, &e->pca_counts,
                           &e->q_counts, &e->q_starts, &e->q_cellrank, &e->q_rows, &e->q_ids, &e->q_inv,
                           &e->q_proj_u, &e->q_proj_s, &e->q_proj_partial, &e->q_proj_out, &e->q_box_out,
-                          &e->q_tiles, &e->q_rows32, &e->q_qa, &e->q_pb};
+                          &e->q_tiles, &e->q_rows32, &e->q_qa, &e->q_pb, &e->ovf_ids};
         for (DevBuf* b : bufs) free_buf(*b);
         for (cudaEvent_t& ev : e->ev)
             if (ev) cudaEventDestroy(ev);
@@ -1364,6 +1306,11 @@ int frnn_set_option(frnn_engine* e, int option, int64_t value) {
             if (value < FRNN_LIST_SEARCH_AUTO || value > FRNN_LIST_SEARCH_NEVER)
                 return fail(e, FRNN_ERR_INVALID_ARG, "list search must be AUTO, ALWAYS or NEVER");
             e->list_search = (int)value;
+            return FRNN_OK;
+        case FRNN_OPT_TEST_STALL:
+            if (value < FRNN_TEST_STALL_OFF || value > FRNN_TEST_STALL_TC_FILTER)
+                return fail(e, FRNN_ERR_INVALID_ARG, "test stall must be OFF, SCAN or TC_FILTER");
+            e->test_stall = (int)value;
             return FRNN_OK;
         default:
             return fail(e, FRNN_ERR_INVALID_ARG, "unknown option");
@@ -1431,6 +1378,7 @@ int frnn_build_grid(frnn_engine* e, const float* d_points_soa, int N, int dim, f
     e->built.valid = false;
     e->last_N = -1;
     e->last_part_rows = -1;
+    e->last_overflow_map = 0;
     for (int i = 0; i < FRNN_STAGES; ++i) e->stage_used[i] = false;
     int path = e->forced_path;
     if (path == FRNN_PATH_AUTO)
@@ -1503,6 +1451,7 @@ int frnn_query_grid(frnn_engine* e, const float* d_queries_soa, int M, int K, in
         FRNN_GROW(e, e->out_dist, (size_t)M * K * 4);
         e->last_N = -1;
         e->last_part_rows = -1;
+        e->last_overflow_map = 0;
         for (int i = 0; i < FRNN_STAGES; ++i) e->stage_used[i] = false;
         st = prepare_queries(e, d_queries_soa, M, b.dim, b.principal);
         if (st != FRNN_OK) return st;
@@ -1639,6 +1588,34 @@ int frnn_last_stage_times(frnn_engine* e, float* ms, int n) {
 int frnn_launch_count(const frnn_engine* e, int64_t* n) {
     if (!e || !n) return FRNN_ERR_INVALID_ARG;
     *n = e->launches;
+    return FRNN_OK;
+}
+
+int frnn_last_overflow(frnn_engine* e, int* count, int* h_query_ids, int max_ids) {
+    if (!e || !count) return FRNN_ERR_INVALID_ARG;
+    if (max_ids < 0 || (max_ids > 0 && !h_query_ids))
+        return fail(e, FRNN_ERR_INVALID_ARG, "max_ids must be >= 0 with a buffer for them");
+    if (e->last_N < 0) return fail(e, FRNN_ERR_STATE, "no finished whole search to report on");
+    *count = 0;
+    if (e->last_overflow_map == 0) return FRNN_OK;
+    DeviceGuard g(e->device);
+    cudaStream_t s = e->stream;
+    FRNN_CHECK(e, cudaMemcpyAsync(e->h_err + 1, e->n_overflow.p, sizeof(int), cudaMemcpyDeviceToHost, s),
+               "overflow count readback");
+    FRNN_CHECK(e, cudaStreamSynchronize(s), "overflow count sync");
+    *count = e->h_err[1];
+    const int n = std::min(*count, max_ids);
+    if (n > 0) {
+        const int* map = e->last_overflow_map == 1 ? e->ids.as<int>()
+                         : e->last_overflow_map == 3 ? e->q_ids.as<int>() : nullptr;
+        FRNN_GROW(e, e->ovf_ids, (size_t)n * 4);
+        overflow_ids_kernel<<<std::min((n + 255) / 256, 4 * e->sms), 256, 0, s>>>(
+            e->overflow.as<int>(), e->n_overflow.as<int>(), map, n, e->ovf_ids.as<int>());
+        FRNN_CHECK(e, cudaGetLastError(), "overflow ids launch");
+        FRNN_CHECK(e, cudaMemcpyAsync(h_query_ids, e->ovf_ids.p, (size_t)n * 4, cudaMemcpyDeviceToHost, s),
+                   "overflow ids readback");
+        FRNN_CHECK(e, cudaStreamSynchronize(s), "overflow ids sync");
+    }
     return FRNN_OK;
 }
 

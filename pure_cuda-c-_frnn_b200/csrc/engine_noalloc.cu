@@ -29,6 +29,7 @@
 #include "frnn_b200.h"
 #include "frnn_device.cuh"
 #include "frnn_internal.h"
+#include "grid_plan.cuh"
 
 using namespace frnn;
 
@@ -101,61 +102,10 @@ bool device_buffer(const void* p, int dev) {
     return a.type == cudaMemoryTypeDevice && a.device == dev;
 }
 
-// Grid on the leading min(dim, 4) axes over the bounding box, cell edge just
-// above r, at most kMaxCells cells (coarser cells keep the 3^g shell exact).
+// Grid on the leading min(dim, 4) axes over the bounding box: the engine's own
+// planner (grid_plan.cuh) with the table capped at kMaxCells cells.
 bool plan(const float* box, int N, int dim, float radius, GridPlan& P) {
-    const int g = dim <= 4 ? dim : 4;
-    double ext_max = 0.0, mag = 0.0;
-    for (int d = 0; d < g; ++d) {
-        const double lo = box[2 * d], hi = box[2 * d + 1];
-        ext_max = std::fmax(ext_max, hi - lo);
-        mag = std::fmax(mag, std::fmax(std::fabs(lo), std::fabs(hi)));
-    }
-    const double u = 1.0 / 16777216.0;
-    double cell = (double)radius * (1.0 + 1e-5 + 8.0 * u * (ext_max / radius + 2.0));
-    long long res[kMaxGridAxes];
-    long long cells = 1;
-    for (int iter = 0; iter < 200; ++iter) {
-        cells = 1;
-        bool over = false;
-        for (int d = 0; d < g; ++d) {
-            const double ext = (double)box[2 * d + 1] - (double)box[2 * d];
-            res[d] = (long long)std::floor(ext / cell) + 1;
-            cells *= res[d];
-            if (res[d] > (1LL << 30) || cells > kMaxCells) { over = true; break; }
-        }
-        if (!over) break;
-        cell *= 1.25;
-    }
-    if (cells > kMaxCells) return false;
-    bool useful = false;
-    for (int d = 0; d < g; ++d) useful |= res[d] > 3;
-    if (!useful) return false;
-    P.g = g;
-    P.n = N;
-    P.dim = dim;
-    P.row = dim == 3 ? 4 : (dim + 3) / 4 * 4;
-    P.cell = (float)cell;
-    P.inv_cell = 1.0f / P.cell;
-    long long s = 1;
-    for (int d = 0; d < kMaxGridAxes; ++d) {
-        if (d < g) {
-            P.origin[d] = box[2 * d];
-            const int c = (int)std::floor((box[2 * d + 1] - P.origin[d]) * P.inv_cell);
-            res[d] = res[d] > (long long)c + 1 ? res[d] : (long long)c + 1;
-            P.res[d] = (int)res[d];
-            P.stride[d] = s;
-            s *= res[d];
-        } else {
-            P.origin[d] = 0.0f;
-            P.res[d] = 1;
-            P.stride[d] = s;
-        }
-    }
-    P.cells = s;
-    if (P.cells > kMaxCells) return false;
-    P.eps = (float)(std::ldexp(1.0, -20) * (mag + ext_max)) + 1e-30f;
-    return true;
+    return plan_grid(box, dim <= 4 ? dim : 4, N, dim, radius, 0.0, kMaxCells, P);
 }
 
 #define NA_CHECK(call)                                  \

@@ -18,9 +18,14 @@ cudaError_t launch_bbox(const float* pts, int n, int g, float* partial, unsigned
 cudaError_t launch_hash_count(const float* pts, const GridPlan& P, int* counts, int2* cellrank,
                               cudaStream_t s, const float* proj = nullptr);
 long long scan_tiles(long long cells);
+// withhold >= 0 makes that tile keep its status to itself, so the bounded
+// look-back of the next tile gives up (tests of the timeout path only).
+// tile_work (optional, scan_tiles(cells) entries): per 4,096-cell tile, the
+// sum of count * (count + 2) over its cells (work weights for sharding).
+constexpr int kScanTileCells = 4096;
 cudaError_t launch_scan(const int* counts, int* starts, long long cells,
                         unsigned long long* status, int* ticket, unsigned epoch, int* err,
-                        cudaStream_t s);
+                        cudaStream_t s, int withhold = -1, unsigned long long* tile_work = nullptr);
 // inv (optional): inv[original index] = sorted position; proj (optional, D > 3):
 // projected coordinates copied to proj_sorted in cell order
 cudaError_t launch_scatter(const float* pts, const GridPlan& P, const int2* cellrank,
@@ -124,10 +129,12 @@ cudaError_t launch_tc_prep(const float* pts, int n, int dim, const float* center
 // lists[q*cap ..]; queries with more go to overflow[0..*n_overflow)
 // qtiles (optional): a separate query set of m points (its own tiles; qa then
 // holds its terms), searched against the n points of tiles / pb
+// skip_tile >= 0: the producer never copies that point tile, so the MMA
+// thread's bounded wait for it gives up (tests of the timeout path only)
 cudaError_t launch_tc_filter(const uint8_t* tiles, const float* qa, const float* pb, int n, int dim,
                              int cap, int* lists, int* counts, int* overflow, int* n_overflow, int* err,
                              int qb_begin, int qb_end, cudaStream_t s, const uint8_t* qtiles = nullptr,
-                             int m = 0);
+                             int m = 0, int skip_tile = -1);
 // exact results for the queries q in [q0, q1) with counts[q] <= cap, to row
 // q - q0 of out[k*(q1-q0) + row]
 // qrows32 (optional): the separate query set's fp32 rows (n = its size)

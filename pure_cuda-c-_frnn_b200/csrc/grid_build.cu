@@ -159,6 +159,7 @@ __global__ void __launch_bounds__(256) hash_count_kernel(const float* __restrict
 constexpr int kScanThreads = 256;
 constexpr int kScanItems = 16;
 constexpr int kScanTile = kScanThreads * kScanItems;
+static_assert(kScanTile == kScanTileCells, "the tile size the sharded search assumes");
 
 constexpr unsigned kFlagAgg = 1u, kFlagPrefix = 2u;
 
@@ -172,11 +173,20 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const int* __restric
                                                             long long cells,
                                                             unsigned long long* __restrict__ status,
                                                             int* __restrict__ ticket, unsigned epoch,
-                                                            int* __restrict__ err) {
+                                                            int* __restrict__ err, int withhold,
+                                                            unsigned long long* __restrict__ tile_work) {
+    // tile_work (optional): the tile's sum over cells of count * (count + 2),
+    // the weights a query-sharded search splits its work by
+    // withhold >= 0 (a test of the bounded wait only): that tile never
+    // publishes its status, so the tile after it must give up waiting
     __shared__ int s_tile;
     __shared__ int s_warp[kScanThreads / 32];
     __shared__ unsigned s_excl;
-    if (threadIdx.x == 0) s_tile = atomicAdd(ticket, 1);
+    __shared__ unsigned long long s_work;
+    if (threadIdx.x == 0) {
+        s_tile = atomicAdd(ticket, 1);
+        s_work = 0;
+    }
     __syncthreads();
     const int tile = s_tile;
     const long long base = (long long)tile * kScanTile;
@@ -199,6 +209,14 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const int* __restric
     int tsum = 0;
 #pragma unroll
     for (int j = 0; j < kScanItems; ++j) tsum += v[j];
+    if (tile_work) {
+        unsigned long long w = 0;
+#pragma unroll
+        for (int j = 0; j < kScanItems; ++j) w += (unsigned long long)v[j] * (unsigned long long)(v[j] + 2);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
+        if (lane == 0) atomicAdd(&s_work, w);
+    }
     // exclusive scan of thread sums inside the block
     int incl = tsum;
 #pragma unroll
@@ -220,10 +238,11 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const int* __restric
         unsigned agg = (unsigned)__shfl_sync(0xffffffffu, wi, kScanThreads / 32 - 1);
         // publish this tile's aggregate, then look back for its prefix
         unsigned excl = 0;
+        const bool publish = tile != withhold;
         if (tile == 0) {
-            if (lane == 0) atomicExch(&status[0], pack_status(epoch, kFlagPrefix, agg));
+            if (lane == 0 && publish) atomicExch(&status[0], pack_status(epoch, kFlagPrefix, agg));
         } else {
-            if (lane == 0) atomicExch(&status[tile], pack_status(epoch, kFlagAgg, agg));
+            if (lane == 0 && publish) atomicExch(&status[tile], pack_status(epoch, kFlagAgg, agg));
             long long look = tile - 1;
             int spins = 0;
             while (true) {
@@ -237,7 +256,8 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const int* __restric
                 int firstp = pmask ? __ffs(pmask) - 1 : 32;
                 unsigned need = firstp >= 31 ? 0xffffffffu : ((2u << firstp) - 1u);
                 if (bad & need) {
-                    if (++spins > (1 << 22)) {
+                    // a test that withholds a tile's status waits briefly
+                    if (++spins > (withhold >= 0 ? 4096 : (1 << 22))) {
                         if (lane == 0) atomicExch(err, 1);
                         break;
                     }
@@ -251,12 +271,13 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const int* __restric
                 if (firstp < 32) break;
                 look -= 32;
             }
-            if (lane == 0) atomicExch(&status[tile], pack_status(epoch, kFlagPrefix, excl + agg));
+            if (lane == 0 && publish) atomicExch(&status[tile], pack_status(epoch, kFlagPrefix, excl + agg));
         }
         if (lane == 0) s_excl = excl;
         if (lane == 0 && base + kScanTile >= cells) starts[cells] = (int)(excl + agg);
     }
     __syncthreads();
+    if (tile_work && threadIdx.x == 0) tile_work[tile] = s_work;
     int run = (int)s_excl + s_warp[warp] + (incl - tsum);
     if (first + kScanItems <= cells) {
         int4* dst = reinterpret_cast<int4*>(starts + first);
@@ -354,10 +375,10 @@ long long scan_tiles(long long cells) { return (cells + kScanTile - 1) / kScanTi
 
 cudaError_t launch_scan(const int* counts, int* starts, long long cells,
                         unsigned long long* status, int* ticket, unsigned epoch, int* err,
-                        cudaStream_t s) {
+                        cudaStream_t s, int withhold, unsigned long long* tile_work) {
     long long tiles = scan_tiles(cells);
     scan_kernel<<<(unsigned)tiles, kScanThreads, 0, s>>>(counts, starts, cells, status, ticket,
-                                                         epoch & 0x3fffffffu, err);
+                                                         epoch & 0x3fffffffu, err, withhold, tile_work);
     return cudaGetLastError();
 }
 

@@ -291,7 +291,8 @@ __global__ void __launch_bounds__(128, 5)
     int cls = 0, cnt_own = 0, sq_own = 0;
     if (q_own < n) {
         sq_own = map ? __ldg(&map[q_own]) : q0 + q_own;
-        cnt_own = __ldg(&counts[sq_own]);
+        // a map entry outside [0, n) only exists after a scan gave up
+        cnt_own = (unsigned)sq_own < (unsigned)(map ? n : q0 + n) ? __ldg(&counts[sq_own]) : 0;
         cls = cnt_own > cap ? 0 : min((cnt_own + 15) >> 4, kEmitClasses - 1);
     }
     if (t <= kEmitClasses) hist[t] = 0;
@@ -307,6 +308,7 @@ __global__ void __launch_bounds__(128, 5)
     const int q = blockIdx.x * 128 + src;
     if (q >= n) return;
     const int sq = map ? __ldg(&map[q]) : q0 + q;
+    if (map && (unsigned)sq >= (unsigned)n) return;  // only after a scan gave up
     const int cnt = __ldg(&counts[sq]);
     if (cnt > cap) return;  // searched by the overflow pass
     unsigned long long a[KN];

@@ -398,6 +398,9 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
                 const long long orow =
                     scatter_ids ? (long long)__ldg(&scatter_ids[sq]) : (long long)sq - row_base;
                 const unsigned long long* list = lists + (size_t)g * cap;
+                // an output row outside [0, ostride) only comes from a
+                // permutation left incomplete by a scan that gave up
+                if ((unsigned long long)orow >= (unsigned long long)ostride) continue;
                 if (n <= 32 && K <= 32) {
                     emit_rank32(list, n, K, lane, r2, oidx + orow, odist + orow, ostride);
                 } else {

@@ -30,6 +30,9 @@ __global__ void __launch_bounds__(256) unpermute_kernel(const int* __restrict__ 
     const int sq = blockIdx.x * blockDim.x + threadIdx.x;
     if (sq >= n) return;
     const int o = __ldg(&ids[sq]);
+    // a permutation entry outside [0, n) only exists after a scan gave up
+    // (the search then reports FRNN_ERR_TIMEOUT); never write through it
+    if ((unsigned)o >= (unsigned)n) return;
     const int k0 = blockIdx.y * kUnpermRows;
     int vi[kUnpermRows];
     float vd[kUnpermRows];

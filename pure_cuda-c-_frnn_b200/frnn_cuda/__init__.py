@@ -79,6 +79,7 @@ def load_library() -> ctypes.CDLL:
         "frnn_launch_count": (I, [P, ctypes.POINTER(L)]),
         "frnn_set_option": (I, [P, I, L]),
         "frnn_last_grid_axes": (I, [P, ctypes.POINTER(I)]),
+        "frnn_last_overflow": (I, [P, ctypes.POINTER(I), P, I]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -272,6 +273,8 @@ class FRNNEngine:
     OPT_DIRECT_OUTPUT_MAX_BYTES = 1
     OPT_GRID_AXES = 2
     OPT_LIST_SEARCH = 3
+    OPT_TEST_STALL = 4
+    TEST_STALL_OFF, TEST_STALL_SCAN, TEST_STALL_TC_FILTER = 0, 1, 2
     GRID_AXES_AUTO, GRID_AXES_LEADING, GRID_AXES_PRINCIPAL = 0, 1, 2
     LIST_SEARCH_AUTO, LIST_SEARCH_ALWAYS, LIST_SEARCH_NEVER = 0, 1, 2
 
@@ -290,6 +293,19 @@ class FRNNEngine:
         buf = (ctypes.c_float * n)()
         self._check(self._lib.frnn_last_stage_times(self._eng, buf, n), "stage_times")
         return {k: float(v) for k, v in zip(self.STAGES, buf) if v >= 0}
+
+    def last_overflow(self, max_ids: int = 1 << 24) -> np.ndarray:
+        """Original indices of the queries of the last whole search whose
+        candidate list overflowed and were searched again by the fallback
+        pass (sorted ascending)."""
+        n = ctypes.c_int()
+        self._check(self._lib.frnn_last_overflow(self._eng, ctypes.byref(n), None, 0), "last_overflow")
+        m = min(int(n.value), int(max_ids))
+        out = np.empty(m, dtype=np.int32)
+        if m:
+            self._check(self._lib.frnn_last_overflow(self._eng, ctypes.byref(n), out.ctypes.data, m),
+                        "last_overflow")
+        return np.sort(out)
 
     def launch_count(self) -> int:
         n = ctypes.c_int64()

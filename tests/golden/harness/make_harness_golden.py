@@ -33,7 +33,10 @@ def reference_functions(ref_root):
 
 
 def main():
-    ns = reference_functions(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FRNN_REF_ROOT")
+    if not ref_root:
+        sys.exit("usage: make_harness_golden.py REF_ROOT (or set FRNN_REF_ROOT): the reference checkout")
+    ns = reference_functions(ref_root)
     out = {}
     cases = [("uniform", 3, 0.02, 2000, 3), ("lowrank", 3, 0.02, 3000, 12), ("lowrank", 3, 0.02, 2500, 16),
              ("lowrank", 5, 0.05, 1500, 8)]

@@ -1,6 +1,6 @@
 """Record the reference engine's outputs on tests/golden/cases.py (run on a B200).
 
-    python tests/golden/make_golden.py [OUT_DIR]
+    python tests/golden/make_golden.py OUT_DIR
 
 Runs FRNNEngine.search_gpu of the reference (oracle/_ref/libfrnn_ref.so,
 compiled from the reference's own sources by oracle/Makefile) on each case and
@@ -44,4 +44,6 @@ def main(out_dir):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.path.join(ROOT, "gpurun_out", "golden"))
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py OUT_DIR (the .npz files are then reviewed and copied here)")
+    main(sys.argv[1])

@@ -28,9 +28,12 @@ def assert_bit_exact(idx_a, dist_a, idx_b, dist_b, what=""):
     bad = np.argwhere((idx_a != idx_b) | (dist_a.view(np.int32) != dist_b.view(np.int32)))
     if len(bad):
         k, q = bad[0]
+        qs = np.unique(bad[:, 1])
+        rows = "; ".join(f"q={int(x)} k={[int(y) for y in bad[bad[:, 1] == x, 0][:4]]} "
+                         f"a={idx_a[:4, x].tolist()} b={idx_b[:4, x].tolist()}" for x in qs[:4])
         raise AssertionError(
-            f"{what}: {len(bad)} mismatching slots; first at k={k} q={q}: "
-            f"a=({idx_a[k, q]}, {dist_a[k, q]!r}) b=({idx_b[k, q]}, {dist_b[k, q]!r})")
+            f"{what}: {len(bad)} mismatching slots in {len(qs)} queries; first at k={k} q={q}: "
+            f"a=({idx_a[k, q]}, {dist_a[k, q]!r}) b=({idx_b[k, q]}, {dist_b[k, q]!r}); {rows}")
 
 
 def sort_rows(idx: np.ndarray, dist: np.ndarray):

@@ -353,3 +353,26 @@ def test_d3_cooperative_unpermute_and_direct(frnn, oracle_mod, limit):
     assert ("unpermute" in eng.stage_times()) == (limit == 0)
     oi, od, _ = oracle_mod.search(soa, 48, r)
     assert_bit_exact(idx, dist, oi, od, f"K=48 limit={limit}")
+
+
+def test_fresh_engines_on_reused_memory(frnn, oracle_mod):
+    """Engines created one after another get device memory that earlier
+    engines freed.  The prefix scan tags its look-back status words with a
+    per-engine epoch that starts at 1 in every engine, so a status buffer that
+    reuses an earlier engine's memory must be cleared first, or the new
+    engine's first scan reads that engine's sums as its own.  Two clouds with
+    the same grid size but different cell counts, searched alternately by
+    fresh engines, must each stay exact."""
+    N, K = 150_000, 16
+    clouds = []
+    for seed in (11, 12):
+        pts = np.random.default_rng(seed).random((N, 3), dtype=np.float64).astype(np.float32)
+        soa = datagen.soa(pts)
+        r = datagen.uniform_radius(N, 3, K)
+        oi, od, _ = oracle_mod.search(soa, K, r)
+        clouds.append((soa, r, oi, od))
+    for it in range(6):
+        soa, r, oi, od = clouds[it % 2]
+        idx, dist, plan = run_engine(frnn, soa, K, r)
+        assert plan["path"] == "grid"
+        assert_bit_exact(idx, dist, oi, od, f"fresh engine {it}")

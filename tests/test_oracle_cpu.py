@@ -204,3 +204,32 @@ def test_oracle_query_set(oracle_mod, D):
             assert set(inside) <= set(got) <= set(inside) | set(np.where(near)[0])
         else:
             assert len(got) == K
+
+
+@pytest.mark.parametrize("D,N,K", [(5, 3001, 16), (8, 2500, 32), (16, 4099, 64), (33, 1500, 8),
+                                   (128, 1037, 128)])
+def test_oracle_exhaustive_simd_equals_scalar_chain(oracle_mod, D, N, K):
+    """The oracle's exhaustive AVX2 search (taken for D > 3 when the grid would
+    enumerate most points) gives the same bits as the scalar chain distance
+    of every pair, ranked by (d2, index)."""
+    rng = np.random.default_rng(D * 1000 + N)
+    soa = rng.random((D, N), dtype=np.float64).astype(np.float32)
+    # a radius holding ~K/2 points on average, so some rows fill and some pad
+    P = soa.T.astype(np.float64)
+    q = rng.choice(N, 40, replace=False).astype(np.int32)
+    d2q = ((P[q][:, None, :] - P[None, :, :]) ** 2).sum(-1)
+    r = float(np.sqrt(np.quantile(np.sort(d2q, axis=1)[:, K // 2], 0.5)))
+    r2 = np.float32(np.float32(r) * np.float32(r))
+    idx, dist, nc = oracle_mod.search_subset(soa, q, K, r)
+    assert nc == len(q) * N  # the exhaustive loop ran
+    for t, qi in enumerate(q):
+        pj = np.arange(N, dtype=np.int32)
+        d2 = oracle_mod.pair_d2_f32(soa, np.full(N, qi, np.int32), pj, oracle_mod.ORDER_CHAIN)
+        keep = np.nonzero(d2 < r2)[0]
+        o = keep[np.lexsort((keep, d2[keep]))][:K]
+        want_i = np.full(K, -1, np.int32)
+        want_d = np.full(K, r2, np.float32)
+        want_i[:len(o)] = o
+        want_d[:len(o)] = d2[o]
+        assert np.array_equal(idx[:, t], want_i), (t, qi)
+        assert np.array_equal(dist[:, t].view(np.int32), want_d.view(np.int32)), (t, qi)
