@@ -10,14 +10,16 @@ calibrated for 24 mean in-radius neighbours, self-query.  One step = one full
 search (grid build + neighbour search + results in the reference layout) of
 one cloud.
 
-Multi-GPU (one process per GPU under torchrun), ``--mode weak`` (default):
-every rank searches its own cloud -- replica ``rank`` of the configuration's
-distribution (same mixture centres or basis, its own sample of N points, same
-radius) -- with no data-path collective, so scaling is weak.  ``value`` = all
-ranks' queries / max-over-ranks step time.  ``--mode strong``: one cloud,
-queries sharded over the ranks (frnn_cuda.sharded: NCCL broadcast of the
-cloud, one part search per rank, gather to rank 0, all inside every step);
-``value`` = N / max-over-ranks step time.
+Multi-GPU (one process per GPU under torchrun), ``--mode strong`` (default):
+one cloud, its queries sharded over the ranks by the engine's own NCCL path
+(frnn_search_sharded: rank 0 plans and builds the grid once, broadcasts the
+built structure, every rank searches a work-balanced slice of the cell-sorted
+queries, the slices are gathered to rank 0 and scattered into [K, N] -- all
+inside every step); ``value`` = N / max-over-ranks step time, ``shard``
+reports every rank's stage times and bytes.  ``--mode weak``: every rank
+searches its own cloud -- replica ``rank`` of the configuration's
+distribution -- with no data-path collective; ``value`` = all ranks'
+queries / max-over-ranks step time.
 
 Timing: W untimed warm-up steps, then exactly K timed steps, bracketed by a
 barrier and torch.cuda.synchronize; each step is timed with CUDA events on the
@@ -68,10 +70,11 @@ def parse():
                     help="skip the per_config sweep over all five configurations (N=1 only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--mode", choices=["weak", "strong"], default="weak",
-                    help="weak: every rank searches its own cloud (no data-path collective); "
-                         "strong: one cloud, queries sharded over the ranks (broadcast, part "
-                         "search, gather to rank 0 inside every step)")
+    ap.add_argument("--mode", choices=["weak", "strong"], default="strong",
+                    help="strong (default): one cloud, queries sharded over the ranks by the "
+                         "engine's NCCL path (root builds once, broadcast, slice search, gather "
+                         "to rank 0, all inside every step); weak: every rank searches its own "
+                         "cloud with no data-path collective")
     return ap.parse_args()
 
 
@@ -308,10 +311,13 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
     x = torch.from_numpy(soa).to(dev)
     eng = frnn_cuda.FRNNEngine(max_points=N, device=dev)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    shard = None
     if strong:
-        from frnn_cuda.sharded import engine_part_search, search_sharded
-        part = engine_part_search(eng)
-        step = lambda: search_sharded(x if rank == 0 else None, N, D, K, r, part)  # noqa: E731
+        from frnn_cuda.sharded import _DeviceArray, nccl_shard
+        shard = nccl_shard(eng)
+        shard.set_timeout(120.0)
+        xp = x.data_ptr() if rank == 0 else 0
+        step = lambda: shard.search(0, xp, N, D, K, r)  # noqa: E731
     else:
         step = lambda: eng.search_gpu(x.data_ptr(), N, D, K, r)  # noqa: E731
 
@@ -337,15 +343,24 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
 
     # per-stage device times, from separate instrumented steps
     eng.set_timing(True)
-    stages = {}
+    stages, sh_stages = {}, {}
     for _ in range(5):
         flush.zero_()
         step()
         for k, v in eng.stage_times().items():
             stages.setdefault(k, []).append(v)
+        if shard is not None:
+            for k, v in shard.last_stats()["stage_ms"].items():
+                sh_stages.setdefault(k, []).append(v)
     eng.set_timing(False)
     stage_ms = {k: statistics.median(v) for k, v in stages.items()}
     plan = eng.last_plan()
+    shard_ranks = None
+    if shard is not None:
+        mine = dict(shard.last_stats(), stage_ms={k: statistics.median(v) for k, v in sh_stages.items()},
+                    engine_stage_ms=stage_ms, rank=rank)
+        shard_ranks = [None] * world
+        dist.all_gather_object(shard_ranks, mine)
 
     ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if world > 1:
@@ -365,10 +380,10 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
                 # rank 0: pinned host cloud in, sharded search, results out
                 if rank == 0:
                     x.copy_(h_in, non_blocking=True)
-                out = step()
+                pi, pd = step()
                 if rank == 0:
-                    h_idx.copy_(out[0])
-                    h_dst.copy_(out[1])
+                    h_idx.copy_(torch.as_tensor(_DeviceArray(pi, (K, N), "<i4"), device=dev))
+                    h_dst.copy_(torch.as_tensor(_DeviceArray(pd, (K, N), "<f4"), device=dev))
         else:
             e2e_step = lambda: eng.search_soa_host(hi, K, r, hx, hd)  # noqa: E731
         for _ in range(2):
@@ -383,6 +398,8 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
                "h2d_bytes_per_step": int(N * D * 4), "d2h_bytes_per_step": int(N * K * 8),
                "ms_per_step": float(et.item())}
 
+    if shard is not None:
+        shard.close()  # before the process group goes: NCCL resources of this rank
     if rank != 0:
         return None
 
@@ -390,6 +407,8 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
     # dominant kernel: the stage with the largest device time
     dom = max(stage_ms, key=stage_ms.get) if stage_ms else None
     roofline = None
+    # the share of the queries rank 0 searched (per-query kernels scale with it)
+    qf = shard_ranks[0]["rows"] / N if shard_ranks else 1.0
     if dom is not None:
         cells = plan["cells"]
         row = 16 if D == 3 else ((D + 3) // 4 * 4 if D <= 16 else 32) * 4
@@ -414,6 +433,8 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
             # the filter is a dense contraction: 2*N*N*D flops (below)
             "tc_filter": 2.0 * N * N * D,
         }[dom]
+        if dom in ("search", "collect", "emit", "tc_rerank", "tc_filter", "brute", "unpermute"):
+            alg *= qf
         t = stage_ms[dom] / 1e3
         traffic = None
         tpath = os.path.join(ROOT, "profiles", "traffic.json")
@@ -438,10 +459,13 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
         "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_max,
         "higher_is_better": True, "scaling": "strong" if strong else "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic (seeded generator, seed 1234; rank r draws replica r of the same distribution)",
+        "dtype": "f32",
+        "data": ("synthetic (seeded generator, seed 1234; rank 0's cloud, sharded)" if strong else
+                 "synthetic (seeded generator, seed 1234; rank r draws replica r of the same distribution)"),
         "config": config_dict(c, N, r),
-        "parallelism": (f"one cloud, queries sharded over {world} ranks (NCCL broadcast "
-                        f"+ part search + gather to rank 0 in every step)") if strong
+        "parallelism": (f"one cloud, queries sharded over {world} ranks by the engine's NCCL path: "
+                        f"rank 0 builds once, broadcasts the built structure, every rank searches a "
+                        f"work-balanced slice, slices gathered to rank 0 -- all in every step") if strong
                        else f"independent clouds x{world}",
         "queries_per_gpu": N // world if strong else N,
         "latency_ms": ms_max,
@@ -453,6 +477,15 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
         "gpu_launches": int(launches),
         "clocks": clocks,
     }
+    if shard_ranks:
+        # per rank: device ms of each protocol stage and the bytes it moved;
+        # the limiting collective is the slower of the broadcast and the gather
+        root = shard_ranks[0]["stage_ms"]
+        coll = {k: root.get(k, 0.0) for k in ("broadcast", "gather")}
+        line["shard"] = {"ranks": shard_ranks, "limiting_collective": max(coll, key=coll.get),
+                         "collective_ms": coll,
+                         "search_ms_max": max(r["stage_ms"].get("search", 0.0) for r in shard_ranks),
+                         "search_ms_min": min(r["stage_ms"].get("search", 0.0) for r in shard_ranks)}
     if world == 1 and not a.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(soa, K, r)
     if world == 1 and not a.no_per_config:

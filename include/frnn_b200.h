@@ -50,7 +50,8 @@ enum frnn_status {
     FRNN_ERR_CUDA = 3,         /* a CUDA runtime call or kernel launch failed    */
     FRNN_ERR_TIMEOUT = 4,      /* a bounded device wait gave up (scan lookback)  */
     FRNN_ERR_NO_DEVICE = 5,    /* no usable sm_100 device                        */
-    FRNN_ERR_STATE = 6         /* call order violated (e.g. results before search) */
+    FRNN_ERR_STATE = 6,        /* call order violated (e.g. results before search) */
+    FRNN_ERR_COMM = 7          /* a collective of the sharded search failed       */
 };
 
 /* Search paths (frnn_engine.cu:215-246 chooses among the reference's three). */
@@ -245,6 +246,66 @@ int frnn_launch_count(const frnn_engine* e, int64_t* n);
  * FRNN_ERR_STATE when no whole search has finished.  No reference
  * counterpart (its heaps never overflow: they keep K entries). */
 int frnn_last_overflow(frnn_engine* e, int* count, int* h_query_ids, int max_ids);
+
+/* ---- query-sharded search over the GPUs of a node ----------------------
+ *
+ * One cloud, searched by several engines (one process per GPU), each taking
+ * a slice of the queries; results gathered on one rank.  No counterpart in the
+ * reference, whose engine searches a cloud on one GPU
+ * (python_interface/frnn_engine.cu:195-250): queries are independent and the
+ * point set is read-only, so that search splits by query.  The ranks are
+ * joined by an NCCL communicator (NVLink / NVSwitch); NCCL is loaded at the
+ * first call of frnn_shard_unique_id or frnn_shard_create (the process's own
+ * libnccl.so.2 when one is already loaded).
+ *
+ * Per call of frnn_search_sharded (every rank calls it, with the same root,
+ * N, dim, K and radius): the root plans and builds the search structure once
+ * (on the grid path the cell-sorted rows, their ids and the cell starts), cuts
+ * the query order into one slice per rank of equal estimated work, and
+ * broadcasts the plan and the structure (the cloud itself on the brute-force
+ * paths); every rank searches its slice; the slices are gathered to the root,
+ * whose results -- [k*N + q], the same values as frnn_search_gpu on the whole
+ * cloud -- are returned in shard-owned device buffers valid until the next
+ * call.  Host waits are bounded by the shard's timeout (default 120 s):
+ * FRNN_ERR_TIMEOUT when a rank does not take part, FRNN_ERR_COMM when NCCL
+ * reports an error; after either the shard is unusable (FRNN_ERR_STATE).  An
+ * error on one rank before the data exchange (bad arguments, allocation) is
+ * returned by every rank.  Blocking. */
+typedef struct frnn_shard frnn_shard;
+#define FRNN_SHARD_ID_BYTES 128
+
+/* A new id for one shard group (an NCCL unique id): call on one rank and pass
+ * the FRNN_SHARD_ID_BYTES bytes to every rank over any host channel. */
+int frnn_shard_unique_id(unsigned char* id_out);
+
+/* Join rank `rank` of `nranks` (collective: every rank calls it with the same
+ * id).  The engine (on this process's GPU) does the rank's work; it stays
+ * usable for ordinary searches, which discard nothing the shard needs. */
+int frnn_shard_create(frnn_engine* e, int nranks, int rank, const unsigned char* id, frnn_shard** out);
+int frnn_shard_destroy(frnn_shard* sh);
+int frnn_shard_set_timeout(frnn_shard* sh, double seconds);
+
+/* The sharded search.  d_points_soa: the root's cloud (SoA [d*N + i], device
+ * memory on the root's GPU); ignored on the other ranks.  On the root
+ * *d_idxs / *d_dists receive the [K, N] results; elsewhere NULL. */
+int frnn_search_sharded(frnn_shard* sh, int root, const float* d_points_soa, int N, int dim, int K,
+                        float radius, int** d_idxs, float** d_dists);
+
+/* The last sharded call on this rank: device milliseconds of its stages
+ * (0 root plan and build, 1 header and status exchange, 2 data broadcast,
+ * 3 slice search, 4 gather, 5 root scatter; -1 when not run or timing is off,
+ * see frnn_set_timing on the engine), the bytes this rank broadcast or
+ * received and sent or gathered, and its slice's rows. */
+int frnn_shard_last_stats(frnn_shard* sh, float* stage_ms, int n, int64_t* bcast_bytes, int64_t* gather_bytes,
+                          int* rows);
+
+/* The partition the root applies (host code, no GPU): tile t of the query
+ * order starts at position tile_start[t] (ascending) and carries tile_work[t]
+ * units of estimated work; bounds[0..nparts] receive the cut points, each a
+ * tile start (or N) nearest to the r/nparts quantile of the cumulative work;
+ * slice r is [bounds[r], bounds[r+1]), possibly empty. */
+int frnn_shard_partition(const uint64_t* tile_work, const int* tile_start, int64_t tiles, int N, int nparts,
+                         int* bounds);
 
 /* Allocation-free search.  No counterpart in the reference: it is for callers
  * that cannot allocate device memory while they search (a framework whose own

@@ -93,7 +93,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
             sys.stderr.write(" ".join(cmd) + "\n" + p.stdout + p.stderr + "\n")
         raise RuntimeError(f"nvcc failed for {len(failed)} file(s)")
     if force or jobs or _stale(lib, objs):
-        cmd = [cc, "-shared", "-o", lib] + objs + ARCH + ["-lcudart"]
+        cmd = [cc, "-shared", "-o", lib] + objs + ARCH + ["-lcudart", "-ldl"]
         if verbose:
             print(" ".join(cmd), flush=True)
         p = subprocess.run(cmd, capture_output=True, text=True)

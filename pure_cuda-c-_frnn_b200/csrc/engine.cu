@@ -417,7 +417,7 @@ bool uses_lists(const frnn_engine* e, const GridPlan& P, int K, bool principal) 
 }
 
 int build_points(frnn_engine* e, const float* d_pts, const GridPlan& P, const float* proj, bool with_inv,
-                 unsigned long long* tile_work) {
+                 unsigned long long* tile_work, int* tile_start) {
     cudaStream_t s = e->stream;
     const int N = P.n;
     FRNN_GROW(e, e->counts, (size_t)P.cells * 4);
@@ -449,7 +449,7 @@ int build_points(frnn_engine* e, const float* d_pts, const GridPlan& P, const fl
     FRNN_CHECK(e, launch_scan(e->counts.as<int>(), e->starts.as<int>(), P.cells,
                               e->scan_status.as<unsigned long long>(), e->scan_ticket.as<int>(),
                               e->epoch, e->err_flag.as<int>(), s,
-                              e->test_stall == FRNN_TEST_STALL_SCAN ? 1 : -1, tile_work),
+                              e->test_stall == FRNN_TEST_STALL_SCAN ? 1 : -1, tile_work, tile_start),
                "scan launch");
     stage_end(e, ST_SCAN);
     if (with_inv) FRNN_GROW(e, e->inv, (size_t)N * 4);
@@ -562,7 +562,7 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
              const float* proj) {
     cudaStream_t s = e->stream;
     const bool principal = proj != nullptr;
-    int st = build_points(e, d_pts, P, proj, !part && uses_lists(e, P, K, principal), nullptr);
+    int st = build_points(e, d_pts, P, proj, !part && uses_lists(e, P, K, principal), nullptr, nullptr);
     if (st != FRNN_OK) return st;
     if (part) {
         // part boundaries move to cell boundaries, so that parts searched by
@@ -1195,6 +1195,7 @@ const char* frnn_status_string(int status) {
         case FRNN_ERR_TIMEOUT: return "device wait timed out";
         case FRNN_ERR_NO_DEVICE: return "no usable CUDA device";
         case FRNN_ERR_STATE: return "invalid call order";
+        case FRNN_ERR_COMM: return "collective communication failed";
         default: return "unknown status";
     }
 }

@@ -148,9 +148,10 @@ int plan_grid_search(frnn_engine* e, const float* d_pts, int N, int dim, float r
 bool uses_lists(const frnn_engine* e, const frnn::GridPlan& P, int K, bool principal);
 // Cell histogram, prefix scan and counting-sort scatter of the P.n points into
 // e->counts / starts / rows / ids (inv when with_inv, proj_s when proj).
-// tile_work (optional): per-scan-tile work weights (launch_scan).
+// tile_work / tile_start (optional): per-scan-tile work weights and cut
+// points (launch_scan).
 int build_points(frnn_engine* e, const float* d_pts, const frnn::GridPlan& P, const float* proj,
-                 bool with_inv, unsigned long long* tile_work);
+                 bool with_inv, unsigned long long* tile_work, int* tile_start);
 // Search the built points' sorted positions [q0, q1).  whole: every query,
 // out[k*N + q] in original order (needs inv when lists are used); otherwise
 // row j = sorted position q0 + j of out[k*(q1-q0) + j].

@@ -174,9 +174,11 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const int* __restric
                                                             unsigned long long* __restrict__ status,
                                                             int* __restrict__ ticket, unsigned epoch,
                                                             int* __restrict__ err, int withhold,
-                                                            unsigned long long* __restrict__ tile_work) {
-    // tile_work (optional): the tile's sum over cells of count * (count + 2),
-    // the weights a query-sharded search splits its work by
+                                                            unsigned long long* __restrict__ tile_work,
+                                                            int* __restrict__ tile_start) {
+    // tile_work / tile_start (optional): the tile's sum over cells of
+    // count * (count + 2) and the start of its first cell -- the weights and
+    // the cut points a query-sharded search splits its work by
     // withhold >= 0 (a test of the bounded wait only): that tile never
     // publishes its status, so the tile after it must give up waiting
     __shared__ int s_tile;
@@ -277,7 +279,10 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const int* __restric
         if (lane == 0 && base + kScanTile >= cells) starts[cells] = (int)(excl + agg);
     }
     __syncthreads();
-    if (tile_work && threadIdx.x == 0) tile_work[tile] = s_work;
+    if (tile_work && threadIdx.x == 0) {
+        tile_work[tile] = s_work;
+        tile_start[tile] = (int)s_excl;
+    }
     int run = (int)s_excl + s_warp[warp] + (incl - tsum);
     if (first + kScanItems <= cells) {
         int4* dst = reinterpret_cast<int4*>(starts + first);
@@ -375,10 +380,12 @@ long long scan_tiles(long long cells) { return (cells + kScanTile - 1) / kScanTi
 
 cudaError_t launch_scan(const int* counts, int* starts, long long cells,
                         unsigned long long* status, int* ticket, unsigned epoch, int* err,
-                        cudaStream_t s, int withhold, unsigned long long* tile_work) {
+                        cudaStream_t s, int withhold, unsigned long long* tile_work, int* tile_start) {
+    if (!tile_work != !tile_start) return cudaErrorInvalidValue;
     long long tiles = scan_tiles(cells);
     scan_kernel<<<(unsigned)tiles, kScanThreads, 0, s>>>(counts, starts, cells, status, ticket,
-                                                         epoch & 0x3fffffffu, err, withhold, tile_work);
+                                                         epoch & 0x3fffffffu, err, withhold, tile_work,
+                                                         tile_start);
     return cudaGetLastError();
 }
 

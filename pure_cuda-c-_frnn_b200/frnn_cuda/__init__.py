@@ -22,13 +22,13 @@ from typing import Sequence
 
 import numpy as np
 
-__all__ = ["FRNNEngine", "FRNNError", "PATH_AUTO", "PATH_GRID", "PATH_BRUTE", "PATH_BRUTE_TC",
+__all__ = ["FRNNEngine", "FRNNError", "FRNNShard", "shard_partition", "PATH_AUTO", "PATH_GRID", "PATH_BRUTE", "PATH_BRUTE_TC",
            "library_path", "load_library"]
 
 PATH_AUTO, PATH_GRID, PATH_BRUTE, PATH_BRUTE_TC = 0, 1, 2, 3
 PATH_NAMES = {PATH_AUTO: "auto", PATH_GRID: "grid", PATH_BRUTE: "brute", PATH_BRUTE_TC: "brute_tc"}
 
-_OK, _ERR_INVALID, _ERR_OOM, _ERR_CUDA, _ERR_TIMEOUT, _ERR_NODEV, _ERR_STATE = range(7)
+_OK, _ERR_INVALID, _ERR_OOM, _ERR_CUDA, _ERR_TIMEOUT, _ERR_NODEV, _ERR_STATE, _ERR_COMM = range(8)
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 _lib = None
@@ -80,6 +80,14 @@ def load_library() -> ctypes.CDLL:
         "frnn_set_option": (I, [P, I, L]),
         "frnn_last_grid_axes": (I, [P, ctypes.POINTER(I)]),
         "frnn_last_overflow": (I, [P, ctypes.POINTER(I), P, I]),
+        "frnn_shard_unique_id": (I, [P]),
+        "frnn_shard_create": (I, [P, I, I, P, ctypes.POINTER(P)]),
+        "frnn_shard_destroy": (I, [P]),
+        "frnn_shard_set_timeout": (I, [P, ctypes.c_double]),
+        "frnn_search_sharded": (I, [P, I, P, I, I, I, F, ctypes.POINTER(P), ctypes.POINTER(P)]),
+        "frnn_shard_last_stats": (I, [P, ctypes.POINTER(F), I, ctypes.POINTER(L), ctypes.POINTER(L),
+                                      ctypes.POINTER(I)]),
+        "frnn_shard_partition": (I, [P, P, L, I, I, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -320,3 +328,90 @@ class FRNNEngine:
         self._check(self._lib.frnn_last_grid_axes(self._eng, ctypes.byref(ax)), "last_plan")
         return {"path": PATH_NAMES.get(p.value, str(p.value)), "grid_dims": g.value, "cells": c.value,
                 "axes": "principal" if ax.value == self.GRID_AXES_PRINCIPAL else "leading"}
+
+
+def shard_partition(tile_work, tile_start, N: int, nparts: int) -> np.ndarray:
+    """The cut points a sharded search applies (frnn_shard_partition, host
+    code): query-order tiles starting at ``tile_start`` with estimated work
+    ``tile_work``; returns ``bounds[0..nparts]``, slice r = [bounds[r], bounds[r+1])."""
+    lib = load_library()
+    w = np.ascontiguousarray(tile_work, dtype=np.uint64)
+    t = np.ascontiguousarray(tile_start, dtype=np.int32)
+    if w.shape != t.shape or w.ndim != 1:
+        raise ValueError("tile_work and tile_start must be 1-D of the same length")
+    out = np.empty(int(nparts) + 1, dtype=np.int32)
+    st = lib.frnn_shard_partition(w.ctypes.data, t.ctypes.data, len(w), int(N), int(nparts), out.ctypes.data)
+    if st != _OK:
+        _raise(lib, None, st, "shard_partition")
+    return out
+
+
+class FRNNShard:
+    """One rank of a query-sharded search (frnn_shard_*): ``engine`` (on this
+    process's GPU) joined to the other ranks' engines by an NCCL communicator.
+
+    Every rank constructs it with the same ``uid`` (``FRNNShard.unique_id()``
+    on one rank, shared over any host channel) and then calls ``search`` with
+    the same arguments; the root passes its cloud and receives device pointers
+    to the [K, N] results, valid until the next call."""
+
+    ID_BYTES = 128
+    STAGES = ("build", "header", "broadcast", "search", "gather", "scatter")
+
+    @staticmethod
+    def unique_id() -> bytes:
+        lib = load_library()
+        buf = (ctypes.c_ubyte * FRNNShard.ID_BYTES)()
+        st = lib.frnn_shard_unique_id(buf)
+        if st != _OK:
+            _raise(lib, None, st, "shard unique_id")
+        return bytes(buf)
+
+    def __init__(self, engine: "FRNNEngine", nranks: int, rank: int, uid: bytes):
+        if len(uid) != self.ID_BYTES:
+            raise ValueError(f"uid must be {self.ID_BYTES} bytes")
+        self._engine = engine
+        self._lib = engine._lib
+        self._sh = ctypes.c_void_p()
+        buf = (ctypes.c_ubyte * self.ID_BYTES).from_buffer_copy(uid)
+        st = self._lib.frnn_shard_create(engine._eng, int(nranks), int(rank), buf, ctypes.byref(self._sh))
+        if st != _OK:
+            _raise(self._lib, engine._eng, st, "shard create")
+        self.nranks, self.rank = int(nranks), int(rank)
+
+    def close(self) -> None:
+        if getattr(self, "_sh", None):
+            self._lib.frnn_shard_destroy(self._sh)
+            self._sh = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_timeout(self, seconds: float) -> None:
+        st = self._lib.frnn_shard_set_timeout(self._sh, float(seconds))
+        if st != _OK:
+            _raise(self._lib, self._engine._eng, st, "shard set_timeout")
+
+    def search(self, root: int, dev_ptr: int, N: int, dim: int, K: int, radius: float):
+        """frnn_search_sharded: (idx_ptr, dist_ptr) of the [K, N] results on
+        the root, (0, 0) on the other ranks."""
+        pi, pd = ctypes.c_void_p(), ctypes.c_void_p()
+        st = self._lib.frnn_search_sharded(self._sh, int(root), ctypes.c_void_p(int(dev_ptr or 0)), int(N),
+                                           int(dim), int(K), float(radius), ctypes.byref(pi), ctypes.byref(pd))
+        if st != _OK:
+            _raise(self._lib, self._engine._eng, st, "search_sharded")
+        return pi.value or 0, pd.value or 0
+
+    def last_stats(self) -> dict:
+        n = len(self.STAGES)
+        ms = (ctypes.c_float * n)()
+        bb, gb, rows = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int()
+        st = self._lib.frnn_shard_last_stats(self._sh, ms, n, ctypes.byref(bb), ctypes.byref(gb),
+                                             ctypes.byref(rows))
+        if st != _OK:
+            _raise(self._lib, self._engine._eng, st, "shard last_stats")
+        return {"stage_ms": {k: float(v) for k, v in zip(self.STAGES, ms) if v >= 0},
+                "broadcast_bytes": int(bb.value), "gather_bytes": int(gb.value), "rows": int(rows.value)}

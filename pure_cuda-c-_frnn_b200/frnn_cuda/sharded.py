@@ -1,5 +1,18 @@
 """Query-sharded search of one cloud over the ranks of a torch.distributed group.
 
+Two forms of the same protocol:
+
+* ``nccl_shard(engine)`` -- the engine's own NCCL path (frnn_search_sharded in
+  the C ABI, csrc/shard.cu): the root builds the search structure once and
+  broadcasts it, every rank searches a slice of the cell-sorted queries of
+  equal estimated work, and one kernel on the root scatters the gathered
+  slices.  torch.distributed only carries the 128-byte NCCL id at set-up;
+  no tensor of the search passes through torch.
+* ``search_sharded(points, ..., part_search)`` -- the same steps written with
+  torch.distributed collectives around a ``part_search`` callable, so that the
+  protocol (including its failure handling) runs on CPU ranks over gloo with
+  the oracle as the part search.
+
 The reference searches a cloud on one GPU (``FRNNEngine.search_gpu``,
 python_interface/frnn_engine.cu:195-250).  Queries are independent and the
 point set is read-only, so a cloud splits over ranks (one process per GPU) by
@@ -28,7 +41,7 @@ from typing import Callable, Optional
 import torch
 import torch.distributed as dist
 
-__all__ = ["ShardError", "engine_part_search", "search_sharded"]
+__all__ = ["ShardError", "engine_part_search", "nccl_shard", "search_sharded"]
 
 
 class ShardError(RuntimeError):
@@ -41,6 +54,19 @@ class _DeviceArray:
     def __init__(self, ptr: int, shape: tuple, typestr: str):
         self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (int(ptr), False),
                                          "version": 3, "strides": None}
+
+
+def nccl_shard(engine, group=None, src: int = 0):
+    """This rank's ``FRNNShard`` for ``engine``: rank ``src`` of ``group``
+    makes the NCCL id and every rank receives it (a host-side broadcast over
+    the group); collective."""
+    from frnn_cuda import FRNNShard
+    rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
+    src_global = dist.get_global_rank(group, src) if group is not None else src
+    box = [FRNNShard.unique_id() if rank == src else None]
+    dist.broadcast_object_list(box, src=src_global, group=group)
+    return FRNNShard(engine, world, rank, box[0])
 
 
 def engine_part_search(engine) -> Callable:
