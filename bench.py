@@ -66,6 +66,13 @@ def parse():
     ap.add_argument("--n", type=int, default=None,
                     help="points (default: the configuration's own N; a smaller cloud gets a radius "
                          "calibrated for the same mean neighbour count) -- for small profiling cases")
+    ap.add_argument("--k", type=int, default=None,
+                    help="neighbours per query (default: the configuration's K) -- for small profiling "
+                         "cases of other kernels")
+    ap.add_argument("--shard-chunks", type=int, default=1,
+                    help="strong mode: chunks per rank's slice, each sent while the next is searched")
+    ap.add_argument("--shard-comm-priority", type=int, default=0, choices=[0, 1],
+                    help="strong mode: 1 gives the gather's stream the highest priority")
     ap.add_argument("--no-per-config", action="store_true",
                     help="skip the per_config sweep over all five configurations (N=1 only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -190,10 +197,12 @@ def workload(cfg: int, n: int | None):
     return c, pts, r
 
 
-def config_dict(c, N: int, r: float) -> dict:
+def config_dict(c, N: int, r: float, K: int | None = None) -> dict:
     """The ``config`` block: identical in both arms for the same workload."""
-    return {"workload": c.name if N == c.N else f"{c.name}_n{N}", "describe": c.describe, "N": N,
-            "D": c.D, "K": c.K, "radius": r, "l2": "flushed before every timed step"}
+    K = K or c.K
+    name = c.name + ("" if N == c.N else f"_n{N}") + ("" if K == c.K else f"_k{K}")
+    return {"workload": name, "describe": c.describe, "N": N, "D": c.D, "K": K, "radius": r,
+            "l2": "flushed before every timed step"}
 
 
 def search_roofline(N: int, D: int, K: int, cells: int, path: str, ms: float) -> dict:
@@ -301,7 +310,7 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
     import frnn_cuda
     strong = a.mode == "strong" and world > 1
     c, pts, r = workload(a.config, a.n)
-    N, D, K = pts.shape[0], c.D, c.K
+    N, D, K = pts.shape[0], c.D, a.k or c.K
     if not strong and rank > 0:
         # weak: rank r searches replica r (its own sample of the same distribution)
         pts = datagen.generate(c.kind, N, D, seed=datagen.SEED, replica=rank)
@@ -316,6 +325,8 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
         from frnn_cuda.sharded import _DeviceArray, nccl_shard
         shard = nccl_shard(eng)
         shard.set_timeout(120.0)
+        shard.set_option(shard.OPT_CHUNKS, a.shard_chunks)
+        shard.set_option(shard.OPT_COMM_PRIORITY, a.shard_comm_priority)
         xp = x.data_ptr() if rank == 0 else 0
         step = lambda: shard.search(0, xp, N, D, K, r)  # noqa: E731
     else:
@@ -462,12 +473,13 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
         "dtype": "f32",
         "data": ("synthetic (seeded generator, seed 1234; rank 0's cloud, sharded)" if strong else
                  "synthetic (seeded generator, seed 1234; rank r draws replica r of the same distribution)"),
-        "config": config_dict(c, N, r),
+        "config": config_dict(c, N, r, K),
         "parallelism": (f"one cloud, queries sharded over {world} ranks by the engine's NCCL path: "
                         f"rank 0 builds once, broadcasts the built structure, every rank searches a "
                         f"work-balanced slice, slices gathered to rank 0 -- all in every step") if strong
                        else f"independent clouds x{world}",
         "queries_per_gpu": N // world if strong else N,
+        "shard_options": {"chunks": a.shard_chunks, "comm_priority": a.shard_comm_priority} if strong else None,
         "latency_ms": ms_max,
         "pipeline": {"b_alg_bytes": int(b_alg), "b_alg_gbs": b_alg / (ms_max / 1e3) / 1e9,
                      "b_alg_frac": b_alg / (ms_max / 1e3) / 1e9 / hbm, "plan": plan,
@@ -480,6 +492,8 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
     if shard_ranks:
         # per rank: device ms of each protocol stage and the bytes it moved;
         # the limiting collective is the slower of the broadcast and the gather
+        # (the gather overlaps the search: its time is from the first receive
+        # to the last scatter on rank 0's communication stream)
         root = shard_ranks[0]["stage_ms"]
         coll = {k: root.get(k, 0.0) for k in ("broadcast", "gather")}
         line["shard"] = {"ranks": shard_ranks, "limiting_collective": max(coll, key=coll.get),
@@ -500,7 +514,7 @@ def run_reference_arm(a, torch, dev):
     if not os.path.exists(oracle.REF_SO):
         return {"impl": "reference", "unavailable": "oracle/_ref/libfrnn_ref.so was not built"}
     c, pts, r = workload(a.config, a.n)
-    N, D, K = pts.shape[0], c.D, c.K
+    N, D, K = pts.shape[0], c.D, a.k or c.K
     soa = datagen.soa(pts)
     x = torch.from_numpy(soa).to(dev)
     ref = oracle.RefEngine(N)
@@ -523,7 +537,7 @@ def run_reference_arm(a, torch, dev):
         "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded generator, seed 1234)",
         "impl": "reference",
-        "config": config_dict(c, N, r),
+        "config": config_dict(c, N, r, K),
         "latency_ms": ms,
         "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},

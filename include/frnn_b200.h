@@ -285,6 +285,18 @@ int frnn_shard_create(frnn_engine* e, int nranks, int rank, const unsigned char*
 int frnn_shard_destroy(frnn_shard* sh);
 int frnn_shard_set_timeout(frnn_shard* sh, double seconds);
 
+/* Tuning of the gather (frnn_shard_set_option). */
+enum frnn_shard_option {
+    /* Chunks a rank's slice is searched in (1..8, default 1): each finished
+     * chunk is sent to the root while the next one is searched, and the root
+     * scatters each chunk as it arrives.  Chunks are at least 65,536 queries. */
+    FRNN_SHARD_OPT_CHUNKS = 1,
+    /* 1: the gather's stream gets the device's highest priority; 0 (default)
+     * normal priority. */
+    FRNN_SHARD_OPT_COMM_PRIORITY = 2
+};
+int frnn_shard_set_option(frnn_shard* sh, int option, int64_t value);
+
 /* The sharded search.  d_points_soa: the root's cloud (SoA [d*N + i], device
  * memory on the root's GPU); ignored on the other ranks.  On the root
  * *d_idxs / *d_dists receive the [K, N] results; elsewhere NULL. */
@@ -293,9 +305,10 @@ int frnn_search_sharded(frnn_shard* sh, int root, const float* d_points_soa, int
 
 /* The last sharded call on this rank: device milliseconds of its stages
  * (0 root plan and build, 1 header and status exchange, 2 data broadcast,
- * 3 slice search, 4 gather, 5 root scatter; -1 when not run or timing is off,
- * see frnn_set_timing on the engine), the bytes this rank broadcast or
- * received and sent or gathered, and its slice's rows. */
+ * 3 slice search -- chunk by chunk, each chunk sent as soon as it is done --,
+ * 4 on the root its receives and scatters, which overlap stage 3; -1 when not
+ * run or timing is off, see frnn_set_timing on the engine), the bytes this
+ * rank broadcast or received and sent or gathered, and its slice's rows. */
 int frnn_shard_last_stats(frnn_shard* sh, float* stage_ms, int n, int64_t* bcast_bytes, int64_t* gather_bytes,
                           int* rows);
 

@@ -219,6 +219,30 @@ bool make_plan(const float* box, int N, int dim, float radius, GridPlan& P) {
 
 constexpr long long kPrincipalCellsPerPoint = 128;
 
+// Per-coordinate rounding bound of projected coordinates computed in fp32:
+// (D + 2) 2^-24 |x - mu| (one fixed summation order over D terms), for the
+// largest |x - mu| of a point set (max_sq = its square).
+double projection_delta(int dim, double max_sq) {
+    return (dim + 2) * std::ldexp(std::sqrt(std::max(0.0, max_sq)) * 1.001, -24);
+}
+
+// Screening bound of projected squared distances on a principal-axis grid.
+// A pair the fp32 chain accepts (d2 < fl(r*r)) is within r (1 + 2^-16) in the
+// full dimension -- the chain's relative rounding is below (D + 3) 2^-25 --
+// and so in projection (orthonormal axes never lengthen a distance; the fp32
+// axes are orthonormal to about 2^-20).  Computed projections differ from
+// exact ones by at most delta_q + delta_p per coordinate, so the computed
+// projected distance stays below r (1 + 2^-16) + (delta_q + delta_p) sqrt(g);
+// the factor (1 + 2^-16)^2 covers the fp32 evaluation of the screened
+// distance itself.
+float screen_r2(float radius, int g, double delta_sum) {
+    const double e = std::ldexp(1.0, -16);
+    const double rr = ((double)radius * (1.0 + e) + delta_sum * std::sqrt((double)g)) * (1.0 + e);
+    float f = (float)(rr * rr);
+    if ((double)f < rr * rr) f = std::nextafter(f, INFINITY);
+    return f;
+}
+
 // Eigen-decomposition of a symmetric n x n matrix (row-major, destroyed) by
 // cyclic Jacobi rotations in double: w[i] eigenvalues, column i of V (row-major
 // n x n) the eigenvector of w[i].
@@ -386,6 +410,8 @@ int plan_principal(frnn_engine* e, const float* d_pts, int N, int dim, float rad
     if (e->grid_axes_mode != FRNN_GRID_AXES_PRINCIPAL && first_ok && !(1.25 * best < cost(P.g - 1, P.g)))
         return FRNN_OK;
     P = cand[best_g];
+    e->proj_delta = projection_delta(dim, (double)hbox[pslots - 2]);
+    P.pre_r2 = screen_r2(radius, P.g, 2.0 * e->proj_delta);
     *principal = true;
     return FRNN_OK;
 }
@@ -416,8 +442,7 @@ bool uses_lists(const frnn_engine* e, const GridPlan& P, int K, bool principal) 
     return K <= 32 && (d3 || list_search_nd(e, P));
 }
 
-int build_points(frnn_engine* e, const float* d_pts, const GridPlan& P, const float* proj, bool with_inv,
-                 unsigned long long* tile_work, int* tile_start) {
+int build_points(frnn_engine* e, const float* d_pts, const GridPlan& P, const float* proj, bool with_inv) {
     cudaStream_t s = e->stream;
     const int N = P.n;
     FRNN_GROW(e, e->counts, (size_t)P.cells * 4);
@@ -449,7 +474,7 @@ int build_points(frnn_engine* e, const float* d_pts, const GridPlan& P, const fl
     FRNN_CHECK(e, launch_scan(e->counts.as<int>(), e->starts.as<int>(), P.cells,
                               e->scan_status.as<unsigned long long>(), e->scan_ticket.as<int>(),
                               e->epoch, e->err_flag.as<int>(), s,
-                              e->test_stall == FRNN_TEST_STALL_SCAN ? 1 : -1, tile_work, tile_start),
+                              e->test_stall == FRNN_TEST_STALL_SCAN ? 1 : -1),
                "scan launch");
     stage_end(e, ST_SCAN);
     if (with_inv) FRNN_GROW(e, e->inv, (size_t)N * 4);
@@ -562,7 +587,7 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
              const float* proj) {
     cudaStream_t s = e->stream;
     const bool principal = proj != nullptr;
-    int st = build_points(e, d_pts, P, proj, !part && uses_lists(e, P, K, principal), nullptr, nullptr);
+    int st = build_points(e, d_pts, P, proj, !part && uses_lists(e, P, K, principal));
     if (st != FRNN_OK) return st;
     if (part) {
         // part boundaries move to cell boundaries, so that parts searched by
@@ -648,29 +673,18 @@ int tc_plan(frnn_engine* e, const float* d_pts, int N, int dim, float radius, Tc
     return FRNN_OK;
 }
 
-// tc_search: fp16 tiles, fp32 rows and threshold terms of the points (and of
-// the separate query set), the tensor-core filter over query tiles
-// [qb_begin, qb_end), the exact fp32 re-rank, and the SIMT brute force for
-// queries whose candidate list overflowed.  Queries [qb_begin*128,
-// min(Q, qb_end*128)), results to rows q - qb_begin*128 of out[k*rows + row].
-int tc_search(frnn_engine* e, const float* d_pts, int N, int dim, int K, float radius, const TcPlan& tp,
-              int* out_idx, float* out_dist, int qb_begin, int qb_end, const float* d_q, int M) {
+// tc_prepare: fp16 tiles, fp32 rows and threshold terms of the points (and of
+// the separate query set) with the plan's centre and scale.
+int tc_prepare(frnn_engine* e, const float* d_pts, int N, int dim, const TcPlan& tp, const float* d_q, int M) {
     cudaStream_t s = e->stream;
     const bool sep = d_q != nullptr;
-    const int Q = sep ? M : N;
-    const float r2 = radius * radius;
-    const int ntiles = (N + 127) / 128, qtiles = (Q + 127) / 128;
+    const int ntiles = (N + 127) / 128, qtiles = (M + 127) / 128;
     const int dp = tc_row_floats(dim);
-    const int cap = tc_list_cap(K);
     FRNN_GROW(e, e->tc_center, (size_t)dim * 4);
     FRNN_GROW(e, e->tc_tiles, (size_t)ntiles * tc_tile_bytes(dim));
     FRNN_GROW(e, e->tc_rows, (size_t)N * dp * 4);
     FRNN_GROW(e, e->tc_qa, (size_t)ntiles * 128 * 4);
     FRNN_GROW(e, e->tc_pb, (size_t)ntiles * 128 * 4);
-    FRNN_GROW(e, e->lists, (size_t)Q * cap * 4);
-    FRNN_GROW(e, e->list_counts, (size_t)Q * 4);
-    FRNN_GROW(e, e->overflow, (size_t)Q * 4);
-    FRNN_GROW(e, e->n_overflow, 16);
     // the centre goes through pinned staging (the caller's plan may be on the stack)
     float* hcenter = e->h_tc + 2 * kMaxK + 4;
     std::memcpy(hcenter, tp.center, (size_t)dim * 4);
@@ -682,7 +696,6 @@ int tc_search(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r
                                  e->tc_qa.as<float>(), e->tc_pb.as<float>(), s),
                "prep launch");
     e->launches++;
-    const float* qa = e->tc_qa.as<float>();
     if (sep) {
         // the queries' tiles, rows and query-side terms (point-side terms unused)
         FRNN_GROW(e, e->q_tiles, (size_t)qtiles * tc_tile_bytes(dim));
@@ -694,9 +707,27 @@ int tc_search(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r
                                      e->q_qa.as<float>(), e->q_pb.as<float>(), s),
                    "query prep launch");
         e->launches++;
-        qa = e->q_qa.as<float>();
     }
     stage_end(e, ST_TC_PREP);
+    return FRNN_OK;
+}
+
+// tc_query_tiles: after tc_prepare, the tensor-core filter over query tiles
+// [qb_begin, qb_end), the exact fp32 re-rank, and the SIMT brute force for
+// queries whose candidate list overflowed.  Queries [qb_begin*128,
+// min(Q, qb_end*128)), results to rows q - qb_begin*128 of out[k*rows + row].
+int tc_query_tiles(frnn_engine* e, const float* d_pts, int N, int dim, int K, float radius, int* out_idx,
+                   float* out_dist, int qb_begin, int qb_end, const float* d_q, int M) {
+    cudaStream_t s = e->stream;
+    const bool sep = d_q != nullptr;
+    const int Q = sep ? M : N;
+    const float r2 = radius * radius;
+    const int cap = tc_list_cap(K);
+    FRNN_GROW(e, e->lists, (size_t)Q * cap * 4);
+    FRNN_GROW(e, e->list_counts, (size_t)Q * 4);
+    FRNN_GROW(e, e->overflow, (size_t)Q * 4);
+    FRNN_GROW(e, e->n_overflow, 16);
+    const float* qa = sep ? e->q_qa.as<float>() : e->tc_qa.as<float>();
     const int q0 = qb_begin * 128, q1 = std::min(Q, qb_end * 128), rows = q1 - q0;
     FRNN_CHECK(e, cudaMemsetAsync(e->n_overflow.p, 0, 4, s), "memset overflow count");
     e->last_overflow_map = 2;
@@ -729,6 +760,13 @@ int tc_search(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r
         e->launches++;
     }
     return FRNN_OK;
+}
+
+int tc_search(frnn_engine* e, const float* d_pts, int N, int dim, int K, float radius, const TcPlan& tp,
+              int* out_idx, float* out_dist, int qb_begin, int qb_end, const float* d_q, int M) {
+    int st = tc_prepare(e, d_pts, N, dim, tp, d_q, M);
+    if (st != FRNN_OK) return st;
+    return tc_query_tiles(e, d_pts, N, dim, K, radius, out_idx, out_dist, qb_begin, qb_end, d_q, M);
 }
 
 // Both halves; *done = false when the filter does not suit the data (the
@@ -906,6 +944,7 @@ int prepare_queries(frnn_engine* e, const float* d_q, int M, int dim, bool princ
                "query projection readback");
     FRNN_CHECK(e, cudaStreamSynchronize(s), "query projection sync");
     if (hqp[pslots - 1] != 0.0f) return fail(e, FRNN_ERR_INVALID_ARG, "queries contain NaN or Inf coordinates");
+    e->q_proj_delta = projection_delta(dim, (double)hqp[pslots - 2]);
     return FRNN_OK;
 }
 
@@ -999,6 +1038,8 @@ int search_queries_core(frnn_engine* e, const float* d_pts, int N, const float* 
         FRNN_CHECK(e, cudaStreamSynchronize(s), "query projection sync");
         if (hqp[pslots - 1] != 0.0f)
             return fail(e, FRNN_ERR_INVALID_ARG, "points or queries contain NaN or Inf coordinates");
+        // the queries' own projection rounding widens the screening bound
+        P.pre_r2 = screen_r2(radius, P.g, e->proj_delta + projection_delta(dim, (double)hqp[pslots - 2]));
     }
     if (path == FRNN_PATH_BRUTE_TC) {
         bool done = false;
@@ -1424,6 +1465,7 @@ int frnn_build_grid(frnn_engine* e, const float* d_points_soa, int N, int dim, f
     e->built.path = path;
     e->built.principal = principal;
     e->built.P = P;
+    e->built.proj_delta = principal ? e->proj_delta : 0.0;
     e->built.valid = true;
     return FRNN_OK;
 }
@@ -1456,7 +1498,9 @@ int frnn_query_grid(frnn_engine* e, const float* d_queries_soa, int M, int K, in
         for (int i = 0; i < FRNN_STAGES; ++i) e->stage_used[i] = false;
         st = prepare_queries(e, d_queries_soa, M, b.dim, b.principal);
         if (st != FRNN_OK) return st;
-        st = search_sorted_queries(e, d_queries_soa, M, K, b.radius * b.radius, b.P, b.principal,
+        GridPlan Pq = b.P;
+        if (b.principal) Pq.pre_r2 = screen_r2(b.radius, Pq.g, b.proj_delta + e->q_proj_delta);
+        st = search_sorted_queries(e, d_queries_soa, M, K, b.radius * b.radius, Pq, b.principal,
                                    b.principal ? e->q_proj_u.as<float>() : nullptr, e->out_idx.as<int>(),
                                    e->out_dist.as<float>());
         if (st != FRNN_OK) return st;

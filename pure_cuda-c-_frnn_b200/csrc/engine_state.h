@@ -64,9 +64,12 @@ struct frnn_engine {
         int N = 0, dim = 0, path = 0;
         float radius = 0.0f;
         bool principal = false;
+        double proj_delta = 0.0;
         frnn::GridPlan P{};
     } built;
     int last_principal = 0;   // the last grid was on principal axes
+    // rounding bounds of the points' / last query set's projected coordinates
+    double proj_delta = 0.0, q_proj_delta = 0.0;
     int last_part_rows = -1;  // rows of the last part search (-1: last search was whole)
     // what the overflow list of the last search holds: 0 nothing (no list
     // search ran), 1 the points' sorted positions (original index = ids[]),
@@ -148,10 +151,8 @@ int plan_grid_search(frnn_engine* e, const float* d_pts, int N, int dim, float r
 bool uses_lists(const frnn_engine* e, const frnn::GridPlan& P, int K, bool principal);
 // Cell histogram, prefix scan and counting-sort scatter of the P.n points into
 // e->counts / starts / rows / ids (inv when with_inv, proj_s when proj).
-// tile_work / tile_start (optional): per-scan-tile work weights and cut
-// points (launch_scan).
 int build_points(frnn_engine* e, const float* d_pts, const frnn::GridPlan& P, const float* proj,
-                 bool with_inv, unsigned long long* tile_work, int* tile_start);
+                 bool with_inv);
 // Search the built points' sorted positions [q0, q1).  whole: every query,
 // out[k*N + q] in original order (needs inv when lists are used); otherwise
 // row j = sorted position q0 + j of out[k*(q1-q0) + j].
@@ -169,6 +170,12 @@ int tc_plan(frnn_engine* e, const float* d_pts, int N, int dim, float radius, Tc
             const float* d_q = nullptr, int M = 0);
 int tc_search(frnn_engine* e, const float* d_pts, int N, int dim, int K, float radius, const TcPlan& tp,
               int* out_idx, float* out_dist, int qb_begin, int qb_end, const float* d_q = nullptr, int M = 0);
+// tc_search in two steps: the tiles and rows of every point (and query) once,
+// then any number of query-tile ranges.
+int tc_prepare(frnn_engine* e, const float* d_pts, int N, int dim, const TcPlan& tp, const float* d_q = nullptr,
+               int M = 0);
+int tc_query_tiles(frnn_engine* e, const float* d_pts, int N, int dim, int K, float radius, int* out_idx,
+                   float* out_dist, int qb_begin, int qb_end, const float* d_q = nullptr, int M = 0);
 
 }  // namespace eng
 }  // namespace frnn

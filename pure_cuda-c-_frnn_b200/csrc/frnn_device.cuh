@@ -32,6 +32,10 @@ struct GridPlan {
     int res[kMaxGridAxes];       // cells per axis
     long long stride[kMaxGridAxes];
     long long cells;             // product of res
+    // principal-axis grids: a candidate whose computed projected squared
+    // distance to the query exceeds pre_r2 is not within r (0 on grids of the
+    // data's own coordinates)
+    float pre_r2;
 };
 
 // 64-bit ranking key: non-negative float bits are order-preserving as an

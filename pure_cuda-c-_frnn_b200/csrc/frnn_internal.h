@@ -20,14 +20,9 @@ cudaError_t launch_hash_count(const float* pts, const GridPlan& P, int* counts, 
 long long scan_tiles(long long cells);
 // withhold >= 0 makes that tile keep its status to itself, so the bounded
 // look-back of the next tile gives up (tests of the timeout path only).
-// tile_work / tile_start (optional, both or neither, scan_tiles(cells)
-// entries): per 4,096-cell tile, the sum of count * (count + 2) over its cells
-// and the start of its first cell (work weights and cut points for sharding).
-constexpr int kScanTileCells = 4096;
 cudaError_t launch_scan(const int* counts, int* starts, long long cells,
                         unsigned long long* status, int* ticket, unsigned epoch, int* err,
-                        cudaStream_t s, int withhold = -1, unsigned long long* tile_work = nullptr,
-                        int* tile_start = nullptr);
+                        cudaStream_t s, int withhold = -1);
 // inv (optional): inv[original index] = sorted position; proj (optional, D > 3):
 // projected coordinates copied to proj_sorted in cell order
 cudaError_t launch_scatter(const float* pts, const GridPlan& P, const int2* cellrank,

@@ -159,7 +159,6 @@ __global__ void __launch_bounds__(256) hash_count_kernel(const float* __restrict
 constexpr int kScanThreads = 256;
 constexpr int kScanItems = 16;
 constexpr int kScanTile = kScanThreads * kScanItems;
-static_assert(kScanTile == kScanTileCells, "the tile size the sharded search assumes");
 
 constexpr unsigned kFlagAgg = 1u, kFlagPrefix = 2u;
 
@@ -173,22 +172,13 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const int* __restric
                                                             long long cells,
                                                             unsigned long long* __restrict__ status,
                                                             int* __restrict__ ticket, unsigned epoch,
-                                                            int* __restrict__ err, int withhold,
-                                                            unsigned long long* __restrict__ tile_work,
-                                                            int* __restrict__ tile_start) {
-    // tile_work / tile_start (optional): the tile's sum over cells of
-    // count * (count + 2) and the start of its first cell -- the weights and
-    // the cut points a query-sharded search splits its work by
+                                                            int* __restrict__ err, int withhold) {
     // withhold >= 0 (a test of the bounded wait only): that tile never
     // publishes its status, so the tile after it must give up waiting
     __shared__ int s_tile;
     __shared__ int s_warp[kScanThreads / 32];
     __shared__ unsigned s_excl;
-    __shared__ unsigned long long s_work;
-    if (threadIdx.x == 0) {
-        s_tile = atomicAdd(ticket, 1);
-        s_work = 0;
-    }
+    if (threadIdx.x == 0) s_tile = atomicAdd(ticket, 1);
     __syncthreads();
     const int tile = s_tile;
     const long long base = (long long)tile * kScanTile;
@@ -211,14 +201,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const int* __restric
     int tsum = 0;
 #pragma unroll
     for (int j = 0; j < kScanItems; ++j) tsum += v[j];
-    if (tile_work) {
-        unsigned long long w = 0;
-#pragma unroll
-        for (int j = 0; j < kScanItems; ++j) w += (unsigned long long)v[j] * (unsigned long long)(v[j] + 2);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
-        if (lane == 0) atomicAdd(&s_work, w);
-    }
+
     // exclusive scan of thread sums inside the block
     int incl = tsum;
 #pragma unroll
@@ -279,10 +262,6 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const int* __restric
         if (lane == 0 && base + kScanTile >= cells) starts[cells] = (int)(excl + agg);
     }
     __syncthreads();
-    if (tile_work && threadIdx.x == 0) {
-        tile_work[tile] = s_work;
-        tile_start[tile] = (int)s_excl;
-    }
     int run = (int)s_excl + s_warp[warp] + (incl - tsum);
     if (first + kScanItems <= cells) {
         int4* dst = reinterpret_cast<int4*>(starts + first);
@@ -380,12 +359,10 @@ long long scan_tiles(long long cells) { return (cells + kScanTile - 1) / kScanTi
 
 cudaError_t launch_scan(const int* counts, int* starts, long long cells,
                         unsigned long long* status, int* ticket, unsigned epoch, int* err,
-                        cudaStream_t s, int withhold, unsigned long long* tile_work, int* tile_start) {
-    if (!tile_work != !tile_start) return cudaErrorInvalidValue;
+                        cudaStream_t s, int withhold) {
     long long tiles = scan_tiles(cells);
     scan_kernel<<<(unsigned)tiles, kScanThreads, 0, s>>>(counts, starts, cells, status, ticket,
-                                                         epoch & 0x3fffffffu, err, withhold, tile_work,
-                                                         tile_start);
+                                                         epoch & 0x3fffffffu, err, withhold);
     return cudaGetLastError();
 }
 

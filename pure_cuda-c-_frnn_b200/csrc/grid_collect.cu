@@ -104,17 +104,19 @@ __global__ void __launch_bounds__(256)
 // over NV float4 per row, the index from ids[] (loaded only for accepted
 // candidates).  Grid coordinates are the row's leading coordinates, or the
 // query's projected coordinates (qproj, kProjStride floats per point) on a
-// principal-axis grid.  prune: skip spans whose box lies beyond r (leading
-// coordinates only: their gaps bound the full distance from below; projected
-// gaps would need the projection's rounding slack, so principal grids visit
-// the whole shell, as the cooperative kernel does).
+// principal-axis grid.  Spans whose cell box lies beyond the acceptance
+// bound are skipped: on leading coordinates the gaps bound the full distance
+// from below (bound r2); on principal axes they bound the computed projected
+// distance, whose bound P.pre_r2 carries the projections' rounding slack.
 template <int NV, int G>
 __global__ void __launch_bounds__(256)
     collect_nd_kernel(const float4* __restrict__ rows, const int* __restrict__ ids,
                       const int* __restrict__ starts, GridPlan P, float r2, int cap,
                       unsigned long long* __restrict__ lists, int* __restrict__ counts,
                       int* __restrict__ overflow, int* __restrict__ n_overflow, int q0, int q1,
-                      const float4* __restrict__ qrows, const float4* __restrict__ qproj, int prune) {
+                      const float4* __restrict__ qrows, const float4* __restrict__ qproj) {
+    // the bound span gaps are tested against
+    const float gap_r2 = qproj ? P.pre_r2 : r2;
     constexpr int W = NV == 1 ? 8 : (NV == 2 ? 4 : 2);  // rows in flight per pass
     static_assert(W <= kCollectRowPad, "passes read at most kCollectRowPad rows past a span");
     const int sq = q0 + blockIdx.x * blockDim.x + threadIdx.x;
@@ -145,15 +147,13 @@ __global__ void __launch_bounds__(256)
             const int c = gc[a] + (u % 3) - 1;
             u /= 3;
             ok &= (c >= 0) & (c < P.res[a]);
-            if (prune) gap += axis_gap(y[a], c, P.origin[a], P.cell, P.eps);
+            gap += axis_gap(y[a], c, P.origin[a], P.cell, P.eps);
             rb += (long long)c * P.stride[a];
         }
-        if (!ok || gap * kPruneScale > r2) continue;
+        if (!ok || gap * kPruneScale > gap_r2) continue;
         int xlo = max(gc[0] - 1, 0), xhi = min(gc[0] + 1, P.res[0] - 1);
-        if (prune) {
-            if (xlo < gc[0] && (gap + axis_gap(y[0], xlo, P.origin[0], P.cell, P.eps)) * kPruneScale > r2) xlo = gc[0];
-            if (xhi > gc[0] && (gap + axis_gap(y[0], xhi, P.origin[0], P.cell, P.eps)) * kPruneScale > r2) xhi = gc[0];
-        }
+        if (xlo < gc[0] && (gap + axis_gap(y[0], xlo, P.origin[0], P.cell, P.eps)) * kPruneScale > gap_r2) xlo = gc[0];
+        if (xhi > gc[0] && (gap + axis_gap(y[0], xhi, P.origin[0], P.cell, P.eps)) * kPruneScale > gap_r2) xhi = gc[0];
         // clamped to [0, n): a corrupt start table never reads out of bounds
         int j = min(max(__ldg(&starts[rb + xlo]), 0), P.n);
         const int e = min(max(__ldg(&starts[rb + xhi + 1]), j), P.n);
@@ -339,11 +339,10 @@ namespace {
 template <int NV, int G>
 cudaError_t launch_nd(const float* rows, const int* ids, const int* starts, const GridPlan& P, float r2,
                       int cap, unsigned long long* lists, int* counts, int* overflow, int* n_overflow, int q0,
-                      int q1, cudaStream_t s, const float* qrows, const float* qproj, bool prune) {
+                      int q1, cudaStream_t s, const float* qrows, const float* qproj) {
     collect_nd_kernel<NV, G><<<(q1 - q0 + 255) / 256, 256, 0, s>>>(
         reinterpret_cast<const float4*>(rows), ids, starts, P, r2, cap, lists, counts, overflow, n_overflow,
-        q0, q1, reinterpret_cast<const float4*>(qrows ? qrows : rows), reinterpret_cast<const float4*>(qproj),
-        prune ? 1 : 0);
+        q0, q1, reinterpret_cast<const float4*>(qrows ? qrows : rows), reinterpret_cast<const float4*>(qproj));
     return cudaGetLastError();
 }
 }  // namespace
@@ -353,10 +352,10 @@ cudaError_t launch_collect_nd(const float* rows, const int* ids, const int* star
                               int* n_overflow, int q0, int q1, cudaStream_t s, const float* qrows,
                               const float* qproj) {
     if (q1 <= q0) return cudaSuccess;
-    const bool prune = qproj == nullptr;
+    if (qproj && !(P.pre_r2 > 0.0f)) return cudaErrorInvalidValue;  // a principal grid carries its bound
     const int nv = P.row / 4;
 #define FRNN_ND(NV, G) return launch_nd<NV, G>(rows, ids, starts, P, r2, cap, lists, counts, overflow, \
-                                                n_overflow, q0, q1, s, qrows, qproj, prune)
+                                                n_overflow, q0, q1, s, qrows, qproj)
     if (nv == 1 && !qproj) {
         if (P.g == 1) FRNN_ND(1, 1);
         if (P.g == 2) FRNN_ND(1, 2);

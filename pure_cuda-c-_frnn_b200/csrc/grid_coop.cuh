@@ -46,10 +46,11 @@ constexpr int kGroup = 8;    // queries per group
 __host__ __device__ constexpr int list_cap(int K) { return K <= 32 ? 64 : (K <= 96 ? 128 : 256); }
 
 // Per-warp shared memory: the group's query rows, its 64-bit acceptance
-// bounds, then the group's candidate lists.
+// bounds, the group's projected query coordinates (principal-axis grids),
+// then the group's candidate lists.
 template <int NV, bool D3>
 __host__ __device__ constexpr size_t rows_bytes() {
-    return (size_t)kGroup * NV * 16 + (size_t)kGroup * 8;
+    return (size_t)kGroup * NV * 16 + (size_t)kGroup * 8 + (size_t)kGroup * kProjStride * 4;
 }
 template <int NV, bool D3>
 __host__ __device__ constexpr size_t warp_bytes(int K) {
@@ -218,11 +219,16 @@ struct Shell<1> {
 };
 
 // NV float4 per sorted row; G grid axes; D3: rows are (x, y, z, index bits)
-// and the index comes from .w, otherwise from ids[].
+// and the index comes from .w, otherwise from ids[].  PRJ: the grid is on
+// principal axes and every candidate is first tested on its projected
+// coordinates: a pair whose projected squared distance exceeds P.pre_r2 (the
+// radius widened by the projections' rounding bound) cannot be within r in
+// the full dimension, because projection onto orthonormal axes never
+// lengthens a distance -- so only candidates that pass load their full row.
 //
 // Group state (query rows, bounds, list lengths) is warp-uniform and lives in
 // registers of every lane; the group loop is unrolled over kGroup slots.
-template <int NV, int G, bool D3>
+template <int NV, int G, bool D3, bool PRJ>
 __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FRNN_COOP_ND_MIN_BLOCKS)
     grid_coop_kernel(const float4* __restrict__ rows, const int* __restrict__ ids,
                      const int* __restrict__ starts, GridPlan P, int K, float r2, int q0, int q1,
@@ -241,6 +247,7 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
     float4* qrows = reinterpret_cast<float4*>(wbase);  // [kGroup][NV]
     unsigned long long* gthr =
         reinterpret_cast<unsigned long long*>(wbase + (size_t)kGroup * NV * 16);  // [kGroup]
+    float4* qprj = reinterpret_cast<float4*>(wbase + (size_t)kGroup * NV * 16 + (size_t)kGroup * 8);
     unsigned long long* lists = reinterpret_cast<unsigned long long*>(wbase + rows_bytes<NV, D3>());
 
     const int base = q0 + (blockIdx.x * kWarps + warp) * 32;
@@ -296,6 +303,11 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
 #pragma unroll
                 for (int v = 0; v < NV; ++v) qrows[g * NV + v] = myq[v];
                 gthr[g] = make_key(r2, 0);
+                if constexpr (PRJ) {
+#pragma unroll
+                    for (int v = 0; v < kProjStride / 4; ++v)
+                        qprj[g * (kProjStride / 4) + v] = __ldg(&qproj[mysq * (kProjStride / 4) + v]);
+                }
             }
             __syncwarp();
         }
@@ -348,11 +360,40 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
             const int js = __shfl_sync(0xffffffffu, sstart, k);
             const int je = __shfl_sync(0xffffffffu, excl, k);
             const int j = valid ? js + (t - je) : 0;
+            // PRJ: which group queries this candidate can be a neighbour of,
+            // from the projected coordinates alone (bit g)
+            unsigned near = valid ? 0xffu : 0u;
+            if constexpr (PRJ) {
+                near = 0u;
+                if (valid) {
+                    float4 pp[kProjStride / 4];
+#pragma unroll
+                    for (int v = 0; v < kProjStride / 4; ++v) pp[v] = __ldg(&proj[(long long)j * (kProjStride / 4) + v]);
+#pragma unroll
+                    for (int g = 0; g < kGroup; ++g) {
+                        if (g < gq) {
+                            float d2p = 0.0f;
+#pragma unroll
+                            for (int a = 0; a < G; ++a) {
+                                const float4 qv = qprj[g * (kProjStride / 4) + (a >> 2)];
+                                const float4 pv = pp[a >> 2];
+                                const float qa = (a & 3) == 0 ? qv.x : (a & 3) == 1 ? qv.y : (a & 3) == 2 ? qv.z : qv.w;
+                                const float pa = (a & 3) == 0 ? pv.x : (a & 3) == 1 ? pv.y : (a & 3) == 2 ? pv.z : pv.w;
+                                const float df = qa - pa;
+                                d2p = __fmaf_rn(df, df, d2p);
+                            }
+                            near |= (d2p <= P.pre_r2 ? 1u : 0u) << g;
+                        }
+                    }
+                }
+                // no lane's candidate is near any query of the group: next chunk
+                if (!__any_sync(0xffffffffu, near != 0u)) continue;
+            }
             float4 p[NV];
 #pragma unroll
             for (int v = 0; v < NV; ++v)
-                p[v] = valid ? __ldg(&rows[(long long)j * NV + v]) : make_float4(0, 0, 0, 0);
-            const int pid = D3 ? __float_as_int(p[0].w) : (valid ? __ldg(&ids[j]) : 0);
+                p[v] = near ? __ldg(&rows[(long long)j * NV + v]) : make_float4(0, 0, 0, 0);
+            const int pid = D3 ? __float_as_int(p[0].w) : (near ? __ldg(&ids[j]) : 0);
 
 #pragma unroll
             for (int g = 0; g < kGroup; ++g) {
@@ -364,8 +405,9 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
                     } else {
                         d2 = chain_dist2<NV>(qrows + g * NV, p);
                     }
-                    bool acc = valid && d2 < glim[g];
-                    const bool tie = valid && d2 == glim[g];
+                    const bool cand = valid && ((near >> g) & 1u);
+                    bool acc = cand && d2 < glim[g];
+                    const bool tie = cand && d2 == glim[g];
                     if (__any_sync(0xffffffffu, tie)) acc |= tie && make_key(d2, pid) < gthr[g];
                     const unsigned m = __ballot_sync(0xffffffffu, acc);
                     if (m) {

@@ -78,14 +78,14 @@ struct CoopArgs {
     const float* qproj;
 };
 
-template <int NV, int G, bool D3>
+template <int NV, int G, bool D3, bool PRJ = false>
 cudaError_t launch_coop(const CoopArgs& a, cudaStream_t s) {
     const size_t smem = (size_t)coop::kWarps * coop::warp_bytes<NV, D3>(a.K);
-    cudaError_t err = set_smem(coop::grid_coop_kernel<NV, G, D3>, smem);
+    cudaError_t err = set_smem(coop::grid_coop_kernel<NV, G, D3, PRJ>, smem);
     if (err != cudaSuccess) return err;
     const int per_block = coop::kWarps * 32;
     const int blocks = (a.q1 - a.q0 + per_block - 1) / per_block;
-    coop::grid_coop_kernel<NV, G, D3><<<blocks, coop::kWarps * 32, smem, s>>>(
+    coop::grid_coop_kernel<NV, G, D3, PRJ><<<blocks, coop::kWarps * 32, smem, s>>>(
         reinterpret_cast<const float4*>(a.rows), a.ids, a.starts, a.P, a.K, a.r2, a.q0, a.q1, a.oidx,
         a.odist, a.ostride, a.scatter_ids, a.qlist, a.qcount, a.row_base,
         reinterpret_cast<const float4*>(a.proj), reinterpret_cast<const float4*>(a.qrows ? a.qrows : a.rows),
@@ -114,16 +114,28 @@ cudaError_t launch_grid_search(const float* rows, const int* ids, const int* sta
         if (P.g == 4) return launch_coop<1, 4, false>(a, s);
         return cudaErrorInvalidValue;
     }
+    // principal axes: candidates are screened on their projected coordinates
+    // (P.pre_r2 > 0); leading coordinates: G = 4
 #define FRNN_COOP_G(NV)                                                   \
     switch (P.g) {                                                        \
-        case 2: return launch_coop<NV, 2, false>(a, s);                   \
-        case 3: return launch_coop<NV, 3, false>(a, s);                   \
-        case 4: return launch_coop<NV, 4, false>(a, s);                   \
-        case 5: return launch_coop<NV, 5, false>(a, s);                   \
-        case 6: return launch_coop<NV, 6, false>(a, s);                   \
+        case 2: return launch_coop<NV, 2, false, true>(a, s);             \
+        case 3: return launch_coop<NV, 3, false, true>(a, s);             \
+        case 4: return launch_coop<NV, 4, false, true>(a, s);             \
+        case 5: return launch_coop<NV, 5, false, true>(a, s);             \
+        case 6: return launch_coop<NV, 6, false, true>(a, s);             \
         default: return cudaErrorInvalidValue;                            \
     }
-    if (!proj && P.g != 4) return cudaErrorInvalidValue;
+    if (!proj) {
+        if (P.g != 4) return cudaErrorInvalidValue;
+        switch (nv) {
+            case 2: return launch_coop<2, 4, false>(a, s);
+            case 3: return launch_coop<3, 4, false>(a, s);
+            case 4: return launch_coop<4, 4, false>(a, s);
+            case 8: return launch_coop<8, 4, false>(a, s);
+            default: return cudaErrorInvalidValue;
+        }
+    }
+    if (!(P.pre_r2 > 0.0f)) return cudaErrorInvalidValue;
     switch (nv) {
         case 2: FRNN_COOP_G(2)
         case 3: FRNN_COOP_G(3)

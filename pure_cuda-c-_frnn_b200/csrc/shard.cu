@@ -9,10 +9,10 @@
 //   1. root: plan and build -- on the grid path the bounding box, the plan
 //      (principal axes when they pay), the cell histogram, scan and
 //      counting-sort scatter; on the tensor-core path the box and the fp16
-//      scale; per 4,096-cell scan tile the sum of count * (count + 2) over
-//      its cells (each query scans about its own cell's count of candidates
-//      per shell cell) gives the partition of the cell-sorted queries into
-//      slices of equal estimated work (frnn_shard_partition);
+//      scale.  On the grid path the candidates of every 64th cell-sorted
+//      query (the point count of its 3^g shell, what a search scans) sample
+//      the work along the query order, and frnn_shard_partition cuts it into
+//      slices of equal estimated work;
 //   2. header broadcast (plan, sizes, slice bounds, the root's status), then
 //      an all-reduce of every rank's status, so that a rank that cannot take
 //      part makes every rank return the same error instead of waiting;
@@ -22,9 +22,12 @@
 //      prepares its own fp16 tiles from it);
 //   4. every rank searches its slice of the query order (sorted positions
 //      on the grid path, 128-query tiles on the tensor-core path, input order
-//      on SIMT brute force) with the engine's own kernels;
-//   5. the slices go to the root (NCCL send / receive in one group), where one
-//      kernel scatters them into the [K, N] results in original query order.
+//      on SIMT brute force) with the engine's own kernels, in a few chunks;
+//   5. each finished chunk goes to the root at once (NCCL send / receive on a
+//      high-priority communication stream) while the next chunk is searched,
+//      and the root scatters every arrived chunk into the [K, N] results in
+//      original query order -- so the gather overlaps the search and only the
+//      last chunk's transfer remains after it.
 //
 // Every wait on the host is bounded (FRNN_ERR_TIMEOUT after the shard's
 // timeout; the communicator is then aborted and the shard unusable); an NCCL
@@ -63,7 +66,33 @@ struct ShardHeader {
 };
 static_assert(std::is_trivially_copyable<ShardHeader>::value, "sent as bytes");
 
-enum ShardStage { SH_BUILD = 0, SH_HEADER, SH_BCAST, SH_SEARCH, SH_GATHER, SH_SCATTER, SH_STAGES };
+// stages timed when the engine's timing is on: the root's plan and build, the
+// header and status exchange, the data broadcast, the chunked slice search
+// (engine stream), the root's receives and scatters (communication stream)
+enum ShardStage { SH_BUILD = 0, SH_HEADER, SH_BCAST, SH_SEARCH, SH_GATHER, SH_STAGES };
+
+// Chunks of a rank's slice: each is searched, then sent while the next one is
+// searched.  Slices below kChunkMin queries are one chunk.
+constexpr int kMaxChunks = 8;
+constexpr int kChunkMin = 65536;
+// Every kSampleStride-th cell-sorted query samples the search work.
+constexpr int kSampleStride = 64;
+
+// Chunk c of the slice [b0, b1) is [cb[c], cb[c+1]); on the tensor-core path
+// every cut is a multiple of 128 (whole query tiles).  Every rank computes the
+// same cuts for every slice.
+int chunk_bounds(int b0, int b1, int path, int chunks, int* cb) {
+    const int rows = b1 - b0;
+    const int m = std::max(1, std::min(chunks, rows / kChunkMin));
+    cb[0] = b0;
+    for (int c = 1; c < m; ++c) {
+        int x = b0 + (int)((long long)rows * c / m);
+        if (path == FRNN_PATH_BRUTE_TC) x = std::min(b1, (x + 127) / 128 * 128);
+        cb[c] = std::max(x, cb[c - 1]);
+    }
+    cb[m] = b1;
+    return m;
+}
 
 }  // namespace
 
@@ -73,12 +102,16 @@ struct frnn_shard {
     int rank = 0, nranks = 1;
     bool broken = false;
     double timeout_s = 120.0;
-    DevBuf d_hdr, d_stat, tile_work, tile_start, pts, st_idx, st_dist, res_idx, res_dist;
+    DevBuf d_hdr, d_stat, work, pts, st_idx, st_dist, res_idx, res_dist;
     ShardHeader* h_hdr = nullptr;   // pinned
     int* h_stat = nullptr;          // pinned, 16 ints
-    uint64_t* h_work = nullptr;  // pinned, grows with the tile count
-    int* h_tstart = nullptr;
-    size_t h_tiles = 0;
+    uint64_t* h_work = nullptr;     // pinned, grows with the sample count
+    int* h_wstart = nullptr;
+    size_t h_samples = 0;
+    cudaStream_t cs = nullptr;      // communication stream (gather)
+    int chunks = 1;                 // FRNN_SHARD_OPT_CHUNKS
+    int comm_priority = 0;          // FRNN_SHARD_OPT_COMM_PRIORITY
+    cudaEvent_t chunk_ev[kMaxChunks] = {}, comm_done = nullptr;
     cudaEvent_t ev[2 * SH_STAGES] = {};
     bool ev_used[SH_STAGES] = {};
     long long bcast_bytes = 0, gather_bytes = 0;
@@ -143,62 +176,85 @@ int wait_stream(frnn_shard* sh, const char* what) {
     }
 }
 
-// Root side of step 5: slice r of the query order, [b[r], b[r+1]), arrived as
-// [K, rows_r] at st + K*b[r] (the root's own slice at own); row j is query
-// order position b[r] + j.  One thread per (original query q, slot k): the
-// query's position is inv[q] on the grid path (cell order), q itself on the
-// brute-force paths; the stores to out[k*N + q] are coalesced and the loads
-// gather from a slice row that stays in L2 while its k is being written.
-__global__ void shard_scatter_kernel(const int* __restrict__ st_idx, const float* __restrict__ st_dist,
-                                     const int* __restrict__ own_idx, const float* __restrict__ own_dist,
-                                     int own, const int* __restrict__ bounds, int nparts,
-                                     const int* __restrict__ inv, int N, int* __restrict__ out_idx,
+// Root side of step 5: one arrived chunk, [K, rows] at src (row j = query
+// order position q0 + j), into out[k*N + q] with q = ids[q0 + j] on the grid
+// path (cell order) or q0 + j on the brute-force paths.
+__global__ void shard_scatter_kernel(const int* __restrict__ src_idx, const float* __restrict__ src_dist, int q0,
+                                     int rows, const int* __restrict__ ids, int N, int* __restrict__ out_idx,
                                      float* __restrict__ out_dist) {
-    __shared__ int b[kMaxShardRanks + 1];
-    for (int i = threadIdx.x; i <= nparts; i += blockDim.x) b[i] = bounds[i];
-    __syncthreads();
-    const int q = blockIdx.x * blockDim.x + threadIdx.x;
-    if (q >= N) return;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= rows) return;
     const int k = blockIdx.y;
-    const int sq = inv ? __ldg(&inv[q]) : q;
-    if ((unsigned)sq >= (unsigned)N) return;  // only after a scan gave up (FRNN_ERR_TIMEOUT)
-    int lo = 0, hi = nparts;  // the part r with b[r] <= sq < b[r+1]
-    while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (b[mid] <= sq) lo = mid;
-        else hi = mid;
-    }
-    const int r = lo, rows = b[r + 1] - b[r], j = sq - b[r];
-    const long long src = (long long)k * rows + j;
-    const long long dst = (long long)k * N + q;
-    if (r == own) {
-        out_idx[dst] = __ldg(&own_idx[src]);
-        out_dist[dst] = __ldg(&own_dist[src]);
-    } else {
-        const long long base = (long long)b[r] * gridDim.y;  // K * b[r]
-        out_idx[dst] = __ldg(&st_idx[base + src]);
-        out_dist[dst] = __ldg(&st_dist[base + src]);
-    }
+    const int q = ids ? __ldg(&ids[q0 + j]) : q0 + j;
+    if ((unsigned)q >= (unsigned)N) return;  // only after a scan gave up (FRNN_ERR_TIMEOUT)
+    const long long src = (long long)k * rows + j, dst = (long long)k * N + q;
+    out_idx[dst] = __ldg(&src_idx[src]);
+    out_dist[dst] = __ldg(&src_dist[src]);
 }
 
-int grow_pinned_tiles(frnn_shard* sh, size_t tiles) {
-    if (sh->h_tiles >= tiles) return FRNN_OK;
+cudaError_t launch_shard_scatter(const int* src_idx, const float* src_dist, int q0, int rows, int K, const int* ids,
+                                 int N, int* out_idx, float* out_dist, cudaStream_t s) {
+    if (rows <= 0) return cudaSuccess;
+    dim3 grid((unsigned)((rows + 255) / 256), (unsigned)K);
+    shard_scatter_kernel<<<grid, 256, 0, s>>>(src_idx, src_dist, q0, rows, ids, N, out_idx, out_dist);
+    return cudaGetLastError();
+}
+
+// The work of the cell-sorted queries, sampled: for sorted position
+// i * stride, the points in its cell's 3^g shell (the x-merged rows a grid
+// search walks) plus a fixed charge per row.  work[i] covers the stride
+// queries from there.
+__global__ void sample_work_kernel(const float* __restrict__ rows, const float* __restrict__ proj_s,
+                                   const int* __restrict__ starts, GridPlan P, int stride, int nsamples,
+                                   unsigned long long* __restrict__ work) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nsamples) return;
+    const long long sq = (long long)i * stride;
+    int gc[kMaxGridAxes];
+    for (int a = 0; a < P.g; ++a) {
+        const float x = proj_s ? __ldg(&proj_s[sq * kProjStride + a]) : __ldg(&rows[sq * P.row + a]);
+        gc[a] = cell_coord(x, P.origin[a], P.inv_cell, P.res[a]);
+    }
+    int nrows = 1;
+    for (int a = 1; a < P.g; ++a) nrows *= 3;
+    const int xlo = max(gc[0] - 1, 0), xhi = min(gc[0] + 1, P.res[0] - 1);
+    unsigned long long total = 0;
+    for (int t = 0; t < nrows; ++t) {
+        int u = t;
+        long long rb = 0;
+        bool ok = true;
+        for (int a = 1; a < P.g; ++a) {
+            const int c = gc[a] + (u % 3) - 1;
+            u /= 3;
+            ok &= (c >= 0) & (c < P.res[a]);
+            rb += (long long)c * P.stride[a];
+        }
+        if (ok) {
+            const int s0 = __ldg(&starts[rb + xlo]), s1 = __ldg(&starts[rb + xhi + 1]);
+            total += (unsigned long long)max(s1 - s0, 0);
+        }
+    }
+    work[i] = (total + 8ull * nrows) * (unsigned long long)min((long long)stride, (long long)P.n - sq);
+}
+
+int grow_pinned_samples(frnn_shard* sh, size_t n) {
+    if (sh->h_samples >= n) return FRNN_OK;
     if (sh->h_work) cudaFreeHost(sh->h_work);
-    if (sh->h_tstart) cudaFreeHost(sh->h_tstart);
+    if (sh->h_wstart) cudaFreeHost(sh->h_wstart);
     sh->h_work = nullptr;
-    sh->h_tstart = nullptr;
-    sh->h_tiles = 0;
-    const size_t want = tiles + tiles / 8 + 64;
+    sh->h_wstart = nullptr;
+    sh->h_samples = 0;
+    const size_t want = n + n / 8 + 64;
     if (cudaMallocHost(&sh->h_work, want * 8) != cudaSuccess ||
-        cudaMallocHost(&sh->h_tstart, want * 4) != cudaSuccess) {
+        cudaMallocHost(&sh->h_wstart, want * 4) != cudaSuccess) {
         cudaGetLastError();
         return fail(sh->e, FRNN_ERR_OOM, "pinned staging for the partition");
     }
-    sh->h_tiles = want;
+    sh->h_samples = want;
     return FRNN_OK;
 }
 
-// Step 1 on the root: plan, build and partition into h_hdr (status set).
+// Step 1 on the root: plan, build and partition into h_hdr.
 int root_plan(frnn_shard* sh, const float* d_pts, int N, int dim, int K, float radius) {
     frnn_engine* e = sh->e;
     ShardHeader& H = *sh->h_hdr;
@@ -216,30 +272,36 @@ int root_plan(frnn_shard* sh, const float* d_pts, int N, int dim, int K, float r
         if (!H.tc.ok) H.path = FRNN_PATH_BRUTE;
     }
     if (H.path == FRNN_PATH_GRID) {
-        const long long tiles = scan_tiles(H.P.cells);
-        FRNN_GROW(e, sh->tile_work, (size_t)tiles * 8);
-        FRNN_GROW(e, sh->tile_start, (size_t)tiles * 4);
-        // inv: the root's scatter reads each query's row through it
-        int st = build_points(e, d_pts, H.P, H.principal ? e->proj_u.as<float>() : nullptr, true,
-                              sh->tile_work.as<unsigned long long>(), sh->tile_start.as<int>());
-        if (st != FRNN_OK) return st;
-        st = grow_pinned_tiles(sh, (size_t)tiles);
-        if (st != FRNN_OK) return st;
         cudaStream_t s = e->stream;
-        FRNN_CHECK(e, cudaMemcpyAsync(sh->h_work, sh->tile_work.p, (size_t)tiles * 8, cudaMemcpyDeviceToHost, s),
-                   "tile work readback");
-        FRNN_CHECK(e, cudaMemcpyAsync(sh->h_tstart, sh->tile_start.p, (size_t)tiles * 4, cudaMemcpyDeviceToHost, s),
-                   "tile start readback");
-        FRNN_CHECK(e, cudaMemcpyAsync(sh->h_stat, e->err_flag.p, sizeof(int), cudaMemcpyDeviceToHost, s),
-                   "error flag readback");
-        FRNN_CHECK(e, cudaStreamSynchronize(s), "partition sync");
-        if (sh->h_stat[0] != 0) {
-            cudaMemsetAsync(e->err_flag.p, 0, sizeof(int), s);
-            cudaStreamSynchronize(s);
-            return fail(e, FRNN_ERR_TIMEOUT, "a bounded device-side wait gave up");
+        int st = build_points(e, d_pts, H.P, H.principal ? e->proj_u.as<float>() : nullptr, false);
+        if (st != FRNN_OK) return st;
+        if (parts > 1) {
+            const int ns = (N + kSampleStride - 1) / kSampleStride;
+            FRNN_GROW(e, sh->work, (size_t)ns * 8);
+            st = grow_pinned_samples(sh, (size_t)ns);
+            if (st != FRNN_OK) return st;
+            sample_work_kernel<<<(ns + 127) / 128, 128, 0, s>>>(
+                e->rows.as<float>(), H.principal ? e->proj_s.as<float>() : nullptr, e->starts.as<int>(), H.P,
+                kSampleStride, ns, sh->work.as<unsigned long long>());
+            FRNN_CHECK(e, cudaGetLastError(), "work sample launch");
+            e->launches++;
+            FRNN_CHECK(e, cudaMemcpyAsync(sh->h_work, sh->work.p, (size_t)ns * 8, cudaMemcpyDeviceToHost, s),
+                       "work sample readback");
+            FRNN_CHECK(e, cudaMemcpyAsync(sh->h_stat, e->err_flag.p, sizeof(int), cudaMemcpyDeviceToHost, s),
+                       "error flag readback");
+            FRNN_CHECK(e, cudaStreamSynchronize(s), "partition sync");
+            if (sh->h_stat[0] != 0) {
+                cudaMemsetAsync(e->err_flag.p, 0, sizeof(int), s);
+                cudaStreamSynchronize(s);
+                return fail(e, FRNN_ERR_TIMEOUT, "a bounded device-side wait gave up");
+            }
+            for (int i = 0; i < ns; ++i) sh->h_wstart[i] = i * kSampleStride;
+            if (frnn_shard_partition(sh->h_work, sh->h_wstart, ns, N, parts, H.bounds) != FRNN_OK)
+                return fail(e, FRNN_ERR_INVALID_ARG, "partition failed");
+        } else {
+            H.bounds[0] = 0;
+            H.bounds[1] = N;
         }
-        if (frnn_shard_partition(sh->h_work, sh->h_tstart, tiles, N, parts, H.bounds) != FRNN_OK)
-            return fail(e, FRNN_ERR_INVALID_ARG, "partition failed");
     } else if (H.path == FRNN_PATH_BRUTE_TC) {
         const int ntq = (N + 127) / 128;
         for (int r = 0; r <= parts; ++r) H.bounds[r] = std::min(N, (int)((long long)ntq * r / parts) * 128);
@@ -321,12 +383,15 @@ int frnn_shard_create(frnn_engine* e, int nranks, int rank, const unsigned char*
         frnn_shard_destroy(sh);
         return fail(e, FRNN_ERR_OOM, "pinned shard staging");
     }
-    for (cudaEvent_t& ev : sh->ev)
-        if (cudaEventCreate(&ev) != cudaSuccess) {
-            cudaGetLastError();
-            frnn_shard_destroy(sh);
-            return fail(e, FRNN_ERR_CUDA, "shard events");
-        }
+    bool ok = cudaStreamCreateWithFlags(&sh->cs, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaEventCreateWithFlags(&sh->comm_done, cudaEventDisableTiming) == cudaSuccess;
+    for (cudaEvent_t& ev : sh->chunk_ev) ok = ok && cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) == cudaSuccess;
+    for (cudaEvent_t& ev : sh->ev) ok = ok && cudaEventCreate(&ev) == cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+        frnn_shard_destroy(sh);
+        return fail(e, FRNN_ERR_CUDA, "shard stream and events");
+    }
     *out = sh;
     return FRNN_OK;
 }
@@ -338,15 +403,20 @@ int frnn_shard_destroy(frnn_shard* sh) {
         cudaStreamSynchronize(sh->e->stream);
         const NcclApi* api = nccl_api();
         if (sh->comm && api) api->CommDestroy(sh->comm);
-        for (DevBuf* b : {&sh->d_hdr, &sh->d_stat, &sh->tile_work, &sh->tile_start, &sh->pts, &sh->st_idx,
-                          &sh->st_dist, &sh->res_idx, &sh->res_dist})
+        if (sh->cs) cudaStreamSynchronize(sh->cs);
+        for (DevBuf* b : {&sh->d_hdr, &sh->d_stat, &sh->work, &sh->pts, &sh->st_idx, &sh->st_dist, &sh->res_idx,
+                          &sh->res_dist})
             if (b->p) cudaFree(b->p);
         if (sh->h_hdr) cudaFreeHost(sh->h_hdr);
         if (sh->h_stat) cudaFreeHost(sh->h_stat);
         if (sh->h_work) cudaFreeHost(sh->h_work);
-        if (sh->h_tstart) cudaFreeHost(sh->h_tstart);
+        if (sh->h_wstart) cudaFreeHost(sh->h_wstart);
         for (cudaEvent_t ev : sh->ev)
             if (ev) cudaEventDestroy(ev);
+        for (cudaEvent_t ev : sh->chunk_ev)
+            if (ev) cudaEventDestroy(ev);
+        if (sh->comm_done) cudaEventDestroy(sh->comm_done);
+        if (sh->cs) cudaStreamDestroy(sh->cs);
     }
     delete sh;
     return FRNN_OK;
@@ -356,6 +426,35 @@ int frnn_shard_set_timeout(frnn_shard* sh, double seconds) {
     if (!sh || !(seconds > 0.0)) return FRNN_ERR_INVALID_ARG;
     sh->timeout_s = seconds;
     return FRNN_OK;
+}
+
+int frnn_shard_set_option(frnn_shard* sh, int option, int64_t value) {
+    if (!sh) return FRNN_ERR_INVALID_ARG;
+    switch (option) {
+        case FRNN_SHARD_OPT_CHUNKS:
+            if (value < 1 || value > kMaxChunks) return fail(sh->e, FRNN_ERR_INVALID_ARG, "chunks must be in [1, 8]");
+            sh->chunks = (int)value;
+            return FRNN_OK;
+        case FRNN_SHARD_OPT_COMM_PRIORITY: {
+            if (value != 0 && value != 1) return fail(sh->e, FRNN_ERR_INVALID_ARG, "priority must be 0 or 1");
+            if ((int)value == sh->comm_priority) return FRNN_OK;
+            DeviceGuard g(sh->e->device);
+            int lo = 0, hi = 0;
+            cudaStream_t ns = nullptr;
+            if (cudaDeviceGetStreamPriorityRange(&lo, &hi) != cudaSuccess ||
+                cudaStreamCreateWithPriority(&ns, cudaStreamNonBlocking, value ? hi : lo) != cudaSuccess) {
+                cudaGetLastError();
+                return fail(sh->e, FRNN_ERR_CUDA, "communication stream");
+            }
+            cudaStreamSynchronize(sh->cs);
+            cudaStreamDestroy(sh->cs);
+            sh->cs = ns;
+            sh->comm_priority = (int)value;
+            return FRNN_OK;
+        }
+        default:
+            return fail(sh->e, FRNN_ERR_INVALID_ARG, "unknown shard option");
+    }
 }
 
 int frnn_search_sharded(frnn_shard* sh, int root, const float* d_points_soa, int N, int dim, int K,
@@ -475,59 +574,113 @@ int frnn_search_sharded(frnn_shard* sh, int root, const float* d_points_soa, int
     SH_NCCL(sh, api->GroupEnd(), "group end");
     sh_end(sh, SH_BCAST);
 
-    // 4. this rank's slice
-    sh_begin(sh, SH_SEARCH);
+    // 4 and 5. this rank's slice, chunk by chunk; every finished chunk goes to
+    // the root on the communication stream while the next is searched, and
+    // the root scatters each arrived chunk
     const float r2 = radius * radius;
-    if (rows > 0) {
-        if (path == FRNN_PATH_GRID) {
-            st = search_built(e, P, H.principal != 0, K, r2, b0, b1, false, e->out_idx.as<int>(),
-                              e->out_dist.as<float>());
-        } else if (path == FRNN_PATH_BRUTE_TC) {
-            st = tc_search(e, pts, N, dim, K, radius, H.tc, e->out_idx.as<int>(), e->out_dist.as<float>(),
-                           b0 / 128, (b1 + 127) / 128);
-        } else {
-            FRNN_CHECK(e, launch_bruteforce(pts, N, dim, K, r2, b0, b1, e->out_idx.as<int>(),
-                                            e->out_dist.as<float>(), rows, s),
-                       "bruteforce launch");
-            e->launches++;
-        }
+    const int* scatter_ids = path == FRNN_PATH_GRID ? e->ids.as<int>() : nullptr;
+    if (path == FRNN_PATH_BRUTE_TC && rows > 0) {
+        st = tc_prepare(e, pts, N, dim, H.tc);
         if (st != FRNN_OK) return st;
     }
-    sh_end(sh, SH_SEARCH);
-
-    // 5. the slices to the root
-    sh_begin(sh, SH_GATHER);
-    SH_NCCL(sh, api->GroupStart(), "group start");
-    if (is_root) {
-        for (int r = 0; r < parts; ++r) {
-            const int n_r = H.bounds[r + 1] - H.bounds[r];
-            if (r == root || n_r == 0) continue;
-            const size_t off = (size_t)K * H.bounds[r], cnt = (size_t)K * n_r;
-            SH_NCCL(sh, api->Recv(sh->st_idx.as<int>() + off, cnt, ncclInt32, r, sh->comm, s), "idx receive");
-            SH_NCCL(sh, api->Recv(sh->st_dist.as<float>() + off, cnt, ncclFloat32, r, sh->comm, s), "dist receive");
+    int cb[kMaxChunks + 1];
+    const int m = chunk_bounds(b0, b1, path, sh->chunks, cb);
+    sh_begin(sh, SH_SEARCH);
+    if (is_root && sh->e->timing) cudaEventRecord(sh->ev[2 * SH_GATHER], sh->cs);
+    for (int c = 0; c < m; ++c) {
+        const int q0 = cb[c], q1 = cb[c + 1], n_c = q1 - q0;
+        const size_t off = (size_t)K * (q0 - b0);  // chunk c's [K, n_c] block in this rank's output
+        int* oi = e->out_idx.as<int>() + off;
+        float* od = e->out_dist.as<float>() + off;
+        if (n_c > 0) {
+            if (path == FRNN_PATH_GRID)
+                st = search_built(e, P, H.principal != 0, K, r2, q0, q1, false, oi, od);
+            else if (path == FRNN_PATH_BRUTE_TC)
+                st = tc_query_tiles(e, pts, N, dim, K, radius, oi, od, q0 / 128, (q1 + 127) / 128);
+            else {
+                FRNN_CHECK(e, launch_bruteforce(pts, N, dim, K, r2, q0, q1, oi, od, n_c, s), "bruteforce launch");
+                e->launches++;
+            }
+            if (st != FRNN_OK) return st;
+        }
+        FRNN_CHECK(e, cudaEventRecord(sh->chunk_ev[c], s), "chunk event");
+        FRNN_CHECK(e, cudaStreamWaitEvent(sh->cs, sh->chunk_ev[c], 0), "chunk wait");
+        if (is_root) {
+            // chunk c of every other rank's slice, then this rank's own
+            SH_NCCL(sh, api->GroupStart(), "group start");
+            for (int r = 0; r < parts; ++r) {
+                int rc[kMaxChunks + 1];
+                const int mr = chunk_bounds(H.bounds[r], H.bounds[r + 1], path, sh->chunks, rc);
+                if (r == root || c >= mr || rc[c + 1] == rc[c]) continue;
+                const size_t o = (size_t)K * rc[c], cnt = (size_t)K * (rc[c + 1] - rc[c]);
+                SH_NCCL(sh, api->Recv(sh->st_idx.as<int>() + o, cnt, ncclInt32, r, sh->comm, sh->cs), "idx receive");
+                SH_NCCL(sh, api->Recv(sh->st_dist.as<float>() + o, cnt, ncclFloat32, r, sh->comm, sh->cs),
+                        "dist receive");
+                sh->gather_bytes += (long long)cnt * 8;
+            }
+            SH_NCCL(sh, api->GroupEnd(), "group end");
+            for (int r = 0; r < parts; ++r) {
+                int rc[kMaxChunks + 1];
+                const int mr = chunk_bounds(H.bounds[r], H.bounds[r + 1], path, sh->chunks, rc);
+                if (c >= mr) continue;
+                const int n_rc = rc[c + 1] - rc[c];
+                const int* si = r == root ? oi : sh->st_idx.as<int>() + (size_t)K * rc[c];
+                const float* sd = r == root ? od : sh->st_dist.as<float>() + (size_t)K * rc[c];
+                FRNN_CHECK(e, launch_shard_scatter(si, sd, rc[c], n_rc, K, scatter_ids, N, sh->res_idx.as<int>(),
+                                                   sh->res_dist.as<float>(), sh->cs),
+                           "scatter launch");
+                if (n_rc > 0) e->launches++;
+            }
+        } else if (n_c > 0) {
+            const size_t cnt = (size_t)K * n_c;
+            SH_NCCL(sh, api->GroupStart(), "group start");
+            SH_NCCL(sh, api->Send(oi, cnt, ncclInt32, root, sh->comm, sh->cs), "idx send");
+            SH_NCCL(sh, api->Send(od, cnt, ncclFloat32, root, sh->comm, sh->cs), "dist send");
+            SH_NCCL(sh, api->GroupEnd(), "group end");
             sh->gather_bytes += (long long)cnt * 8;
         }
-    } else if (rows > 0) {
-        const size_t cnt = (size_t)K * rows;
-        SH_NCCL(sh, api->Send(e->out_idx.p, cnt, ncclInt32, root, sh->comm, s), "idx send");
-        SH_NCCL(sh, api->Send(e->out_dist.p, cnt, ncclFloat32, root, sh->comm, s), "dist send");
-        sh->gather_bytes = (long long)cnt * 8;
     }
-    SH_NCCL(sh, api->GroupEnd(), "group end");
-    sh_end(sh, SH_GATHER);
     if (is_root) {
-        sh_begin(sh, SH_SCATTER);
-        dim3 grid((unsigned)((N + 255) / 256), (unsigned)K);
-        shard_scatter_kernel<<<grid, 256, 0, s>>>(sh->st_idx.as<int>(), sh->st_dist.as<float>(), e->out_idx.as<int>(),
-                                                  e->out_dist.as<float>(), root,
-                                                  reinterpret_cast<const int*>(static_cast<const char*>(sh->d_hdr.p) +
-                                                                               offsetof(ShardHeader, bounds)),
-                                                  parts, path == FRNN_PATH_GRID ? e->inv.as<int>() : nullptr, N,
-                                                  sh->res_idx.as<int>(), sh->res_dist.as<float>());
-        FRNN_CHECK(e, cudaGetLastError(), "scatter launch");
-        e->launches++;
-        sh_end(sh, SH_SCATTER);
+        // chunks of other slices beyond this rank's own chunk count
+        int mmax = m;
+        for (int r = 0; r < parts; ++r) {
+            int rc[kMaxChunks + 1];
+            mmax = std::max(mmax, chunk_bounds(H.bounds[r], H.bounds[r + 1], path, sh->chunks, rc));
+        }
+        for (int c = m; c < mmax; ++c) {
+            SH_NCCL(sh, api->GroupStart(), "group start");
+            for (int r = 0; r < parts; ++r) {
+                int rc[kMaxChunks + 1];
+                const int mr = chunk_bounds(H.bounds[r], H.bounds[r + 1], path, sh->chunks, rc);
+                if (r == root || c >= mr || rc[c + 1] == rc[c]) continue;
+                const size_t o = (size_t)K * rc[c], cnt = (size_t)K * (rc[c + 1] - rc[c]);
+                SH_NCCL(sh, api->Recv(sh->st_idx.as<int>() + o, cnt, ncclInt32, r, sh->comm, sh->cs), "idx receive");
+                SH_NCCL(sh, api->Recv(sh->st_dist.as<float>() + o, cnt, ncclFloat32, r, sh->comm, sh->cs),
+                        "dist receive");
+                sh->gather_bytes += (long long)cnt * 8;
+            }
+            SH_NCCL(sh, api->GroupEnd(), "group end");
+            for (int r = 0; r < parts; ++r) {
+                int rc[kMaxChunks + 1];
+                const int mr = chunk_bounds(H.bounds[r], H.bounds[r + 1], path, sh->chunks, rc);
+                if (r == root || c >= mr) continue;
+                FRNN_CHECK(e, launch_shard_scatter(sh->st_idx.as<int>() + (size_t)K * rc[c],
+                                                   sh->st_dist.as<float>() + (size_t)K * rc[c], rc[c],
+                                                   rc[c + 1] - rc[c], K, scatter_ids, N, sh->res_idx.as<int>(),
+                                                   sh->res_dist.as<float>(), sh->cs),
+                           "scatter launch");
+                e->launches++;
+            }
+        }
     }
+    sh_end(sh, SH_SEARCH);
+    if (is_root && sh->e->timing) {
+        cudaEventRecord(sh->ev[2 * SH_GATHER + 1], sh->cs);
+        sh->ev_used[SH_GATHER] = true;
+    }
+    // the engine stream waits for the communication stream's work
+    FRNN_CHECK(e, cudaEventRecord(sh->comm_done, sh->cs), "comm event");
+    FRNN_CHECK(e, cudaStreamWaitEvent(s, sh->comm_done, 0), "comm wait");
     FRNN_CHECK(e, cudaMemcpyAsync(sh->h_stat + 2, e->err_flag.p, sizeof(int), cudaMemcpyDeviceToHost, s),
                "error flag readback");
     st = wait_stream(sh, "sharded search");

@@ -84,6 +84,7 @@ def load_library() -> ctypes.CDLL:
         "frnn_shard_create": (I, [P, I, I, P, ctypes.POINTER(P)]),
         "frnn_shard_destroy": (I, [P]),
         "frnn_shard_set_timeout": (I, [P, ctypes.c_double]),
+        "frnn_shard_set_option": (I, [P, I, L]),
         "frnn_search_sharded": (I, [P, I, P, I, I, I, F, ctypes.POINTER(P), ctypes.POINTER(P)]),
         "frnn_shard_last_stats": (I, [P, ctypes.POINTER(F), I, ctypes.POINTER(L), ctypes.POINTER(L),
                                       ctypes.POINTER(I)]),
@@ -356,7 +357,7 @@ class FRNNShard:
     to the [K, N] results, valid until the next call."""
 
     ID_BYTES = 128
-    STAGES = ("build", "header", "broadcast", "search", "gather", "scatter")
+    STAGES = ("build", "header", "broadcast", "search", "gather")
 
     @staticmethod
     def unique_id() -> bytes:
@@ -394,6 +395,13 @@ class FRNNShard:
         st = self._lib.frnn_shard_set_timeout(self._sh, float(seconds))
         if st != _OK:
             _raise(self._lib, self._engine._eng, st, "shard set_timeout")
+
+    OPT_CHUNKS, OPT_COMM_PRIORITY = 1, 2
+
+    def set_option(self, option: int, value: int) -> None:
+        st = self._lib.frnn_shard_set_option(self._sh, int(option), int(value))
+        if st != _OK:
+            _raise(self._lib, self._engine._eng, st, "shard set_option")
 
     def search(self, root: int, dev_ptr: int, N: int, dim: int, K: int, radius: float):
         """frnn_search_sharded: (idx_ptr, dist_ptr) of the [K, N] results on
