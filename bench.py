@@ -251,6 +251,46 @@ def per_config_engine(torch, dev, flush, steps: int = 5, warmup: int = 3) -> dic
     return out
 
 
+def per_config_sharded(torch, dist, rank, world, dev, flush, a, steps: int = 5, warmup: int = 3) -> dict:
+    """Every configuration at full size, sharded over the ranks (rank 0's
+    cloud): median over ``steps`` of the max-over-ranks search time."""
+    import frnn_cuda
+    from frnn_cuda.sharded import nccl_shard
+    nmax = max(datagen.config(c).N for c in datagen.CONFIGS)
+    eng = frnn_cuda.FRNNEngine(max_points=nmax, device=dev)
+    shard = nccl_shard(eng)
+    shard.set_timeout(300.0)
+    shard.set_option(shard.OPT_CHUNKS, a.shard_chunks)
+    out = {}
+    for cfg in sorted(datagen.CONFIGS):
+        c = datagen.config(cfg)
+        x = None
+        if rank == 0:
+            _, pts, r = workload(cfg, None)
+            x = torch.from_numpy(datagen.soa(pts)).to(dev)
+            del pts
+        r = c.radius
+        xp = x.data_ptr() if x is not None else 0
+        step = lambda: shard.search(0, xp, c.N, c.D, c.K, r)  # noqa: E731
+        for _ in range(warmup):
+            step()
+        n = steps if cfg != 5 else 3
+        dist.barrier()
+        ms = step_times(torch, step, n, flush)
+        t = torch.tensor(ms, dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = [float(v) for v in t.tolist()]
+        med = statistics.median(ms)
+        plan = eng.last_plan()
+        out[f"cfg{cfg}"] = {"workload": c.name, "steps": n, "ms_median": med, "ms": ms,
+                            "queries_per_s": c.N / (med / 1e3), "plan": plan,
+                            "shard": shard.last_stats()}
+        del x
+        torch.cuda.empty_cache()
+    shard.close()
+    return out
+
+
 def per_config_reference(torch, dev, flush) -> dict:
     """The reference engine on every configuration at full size (its own
     dispatch): median of 5 timed searches, 2 for configuration 5, whose brute
@@ -411,6 +451,11 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
 
     if shard is not None:
         shard.close()  # before the process group goes: NCCL resources of this rank
+    per_cfg = None
+    if strong and not a.no_per_config:
+        del x
+        torch.cuda.empty_cache()
+        per_cfg = per_config_sharded(torch, dist, rank, world, dev, flush, a)
     if rank != 0:
         return None
 
@@ -506,6 +551,8 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
         del x
         torch.cuda.empty_cache()
         line["per_config"] = per_config_engine(torch, dev, flush)
+    if per_cfg is not None:
+        line["per_config"] = per_cfg
     return line
 
 

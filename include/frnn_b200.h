@@ -260,13 +260,14 @@ int frnn_last_overflow(frnn_engine* e, int* count, int* h_query_ids, int max_ids
  *
  * Per call of frnn_search_sharded (every rank calls it, with the same root,
  * N, dim, K and radius): the root plans and builds the search structure once
- * (on the grid path the cell-sorted rows, their ids and the cell starts), cuts
- * the query order into one slice per rank of equal estimated work, and
- * broadcasts the plan and the structure (the cloud itself on the brute-force
- * paths); every rank searches its slice; the slices are gathered to the root,
- * whose results -- [k*N + q], the same values as frnn_search_gpu on the whole
- * cloud -- are returned in shard-owned device buffers valid until the next
- * call.  Host waits are bounded by the shard's timeout (default 120 s):
+ * (on the grid path the cell-sorted rows, their ids and the cell starts),
+ * gives every rank one range of original query indices of equal estimated
+ * work, and broadcasts the plan and the structure (the cloud itself on the
+ * brute-force paths); every rank searches its queries in cell order and
+ * copies its rows -- one contiguous column block -- into the root's result
+ * buffers over NVLink with the copy engines (CUDA IPC mappings); the root's
+ * results -- [k*N + q], the same values as frnn_search_gpu on the whole cloud
+ * -- are returned in shard-owned device buffers valid until the next call.  Host waits are bounded by the shard's timeout (default 120 s):
  * FRNN_ERR_TIMEOUT when a rank does not take part, FRNN_ERR_COMM when NCCL
  * reports an error; after either the shard is unusable (FRNN_ERR_STATE).  An
  * error on one rank before the data exchange (bad arguments, allocation) is
@@ -287,9 +288,9 @@ int frnn_shard_set_timeout(frnn_shard* sh, double seconds);
 
 /* Tuning of the gather (frnn_shard_set_option). */
 enum frnn_shard_option {
-    /* Chunks a rank's slice is searched in (1..8, default 1): each finished
-     * chunk is sent to the root while the next one is searched, and the root
-     * scatters each chunk as it arrives.  Chunks are at least 65,536 queries. */
+    /* Chunks a rank's queries are searched in (1..8, default 1): each
+     * finished chunk is copied into the root's results while the next one is
+     * searched.  Chunks are at least 65,536 queries. */
     FRNN_SHARD_OPT_CHUNKS = 1,
     /* 1: the gather's stream gets the device's highest priority; 0 (default)
      * normal priority. */
@@ -305,18 +306,18 @@ int frnn_search_sharded(frnn_shard* sh, int root, const float* d_points_soa, int
 
 /* The last sharded call on this rank: device milliseconds of its stages
  * (0 root plan and build, 1 header and status exchange, 2 data broadcast,
- * 3 slice search -- chunk by chunk, each chunk sent as soon as it is done --,
- * 4 on the root its receives and scatters, which overlap stage 3; -1 when not
- * run or timing is off, see frnn_set_timing on the engine), the bytes this
- * rank broadcast or received and sent or gathered, and its slice's rows. */
+ * 3 the rank's search, chunk by chunk, 4 its copies into the root's results,
+ * which overlap stage 3 when there are several chunks; -1 when not run or
+ * timing is off, see frnn_set_timing on the engine), the bytes this rank
+ * broadcast or received and copied or gathered, and its number of queries. */
 int frnn_shard_last_stats(frnn_shard* sh, float* stage_ms, int n, int64_t* bcast_bytes, int64_t* gather_bytes,
                           int* rows);
 
-/* The partition the root applies (host code, no GPU): tile t of the query
- * order starts at position tile_start[t] (ascending) and carries tile_work[t]
- * units of estimated work; bounds[0..nparts] receive the cut points, each a
- * tile start (or N) nearest to the r/nparts quantile of the cumulative work;
- * slice r is [bounds[r], bounds[r+1]), possibly empty. */
+/* The partition the root applies (host code, no GPU): bucket t of the
+ * original query indices starts at index tile_start[t] (ascending) and
+ * carries tile_work[t] units of estimated work; bounds[0..nparts] receive the
+ * cut points, each a bucket start (or N) nearest to the r/nparts quantile of
+ * the cumulative work; rank r owns [bounds[r], bounds[r+1]), possibly empty. */
 int frnn_shard_partition(const uint64_t* tile_work, const int* tile_start, int64_t tiles, int N, int nparts,
                          int* bounds);
 

@@ -191,15 +191,36 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 
 // ---- prep -------------------------------------------------------------------
 
-// Per-dimension min / max of the SoA input (one block per dimension) and a
-// flag for non-finite coordinates.  box[2d] = min, box[2d+1] = max.
+// Per-dimension min / max of the SoA input and a flag for non-finite
+// coordinates.  box[2d] = min, box[2d+1] = max.  Blocks of 4,096 values of one
+// dimension each (grid: chunks x dimensions) fold into the box with atomic
+// min / max on an order-preserving unsigned encoding of the floats; the box
+// words hold the encoding until box_final_kernel decodes them.
+constexpr int kBoxChunk = 4096;
+
+__device__ __forceinline__ unsigned order_key(float f) {
+    const unsigned b = __float_as_uint(f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float order_value(unsigned k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+__global__ void box_init_kernel(unsigned* __restrict__ keys, int dim) {
+    const int d = blockIdx.x * blockDim.x + threadIdx.x;
+    if (d >= dim) return;
+    keys[2 * d] = 0xffffffffu;
+    keys[2 * d + 1] = 0u;
+}
+
 __global__ void __launch_bounds__(256) dim_box_kernel(const float* __restrict__ pts, int n,
-                                                      float* __restrict__ box, int* __restrict__ nonfinite) {
-    const int d = blockIdx.x;
+                                                      unsigned* __restrict__ keys, int* __restrict__ nonfinite) {
+    const int d = blockIdx.y;
     const float* col = pts + (long long)d * n;
+    const int i0 = blockIdx.x * kBoxChunk, i1 = min(n, i0 + kBoxChunk);
     float lo = __int_as_float(0x7f800000), hi = -__int_as_float(0x7f800000);
     bool bad = false;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
         const float x = __ldg(&col[i]);
         bad |= !isfinite(x);
         lo = fminf(lo, x);
@@ -226,10 +247,16 @@ __global__ void __launch_bounds__(256) dim_box_kernel(const float* __restrict__ 
             lo = fminf(lo, slo[w]);
             hi = fmaxf(hi, shi[w]);
         }
-        box[2 * d] = lo;
-        box[2 * d + 1] = hi;
+        atomicMin(&keys[2 * d], order_key(lo));
+        atomicMax(&keys[2 * d + 1], order_key(hi));
         if (sbad) atomicOr(nonfinite, 1);
     }
+}
+
+__global__ void box_final_kernel(unsigned* __restrict__ keys, int dim) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= 2 * dim) return;
+    reinterpret_cast<float*>(keys)[i] = order_value(keys[i]);
 }
 
 // One thread per (padded) point: fp16 swizzled tile rows, fp32 rows, and the
@@ -632,7 +659,11 @@ int tc_row_floats(int dim) { return (dim + 3) / 4 * 4; }
 int tc_list_cap(int K) { return 4 * K > 256 ? 4 * K : 256; }
 
 cudaError_t launch_tc_box(const float* pts, int n, int dim, float* box, int* nonfinite, cudaStream_t s) {
-    tc::dim_box_kernel<<<dim, 256, 0, s>>>(pts, n, box, nonfinite);
+    unsigned* keys = reinterpret_cast<unsigned*>(box);
+    tc::box_init_kernel<<<1, 128, 0, s>>>(keys, dim);
+    const dim3 grid((unsigned)((n + tc::kBoxChunk - 1) / tc::kBoxChunk), (unsigned)dim);
+    tc::dim_box_kernel<<<grid, 256, 0, s>>>(pts, n, keys, nonfinite);
+    tc::box_final_kernel<<<1, 256, 0, s>>>(keys, dim);
     return cudaGetLastError();
 }
 

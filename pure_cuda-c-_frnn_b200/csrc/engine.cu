@@ -623,10 +623,10 @@ int tc_plan(frnn_engine* e, const float* d_pts, int N, int dim, float radius, Tc
     stage_begin(e, ST_BBOX);
     FRNN_CHECK(e, cudaMemsetAsync(nonfinite, 0, sizeof(int), s), "memset non-finite flag");
     FRNN_CHECK(e, launch_tc_box(d_pts, N, dim, e->tc_box.as<float>(), nonfinite, s), "box launch");
-    e->launches++;
+    e->launches += 3;
     if (sep) {
         FRNN_CHECK(e, launch_tc_box(d_q, M, dim, e->tc_box.as<float>() + 512, nonfinite, s), "box launch");
-        e->launches++;
+        e->launches += 3;
     }
     stage_end(e, ST_BBOX);
     float* hq = static_cast<float*>(e->h_pca) + 6144;  // the query set's box

@@ -33,7 +33,8 @@ cudaError_t launch_scatter(const float* pts, const GridPlan& P, const int2* cell
 // grid_search.cu
 // Searches sorted query positions [q0, q1).  Results for sorted position sq go
 // to row (sq - q0) of the outputs: out[k*ostride + (sq - q0)], or, when
-// scatter_ids is non-null, straight to out[k*ostride + scatter_ids[sq]].
+// scatter_ids is non-null, straight to out[k*ostride + scatter_ids[sq] -
+// row_base] (row_base 0 unless given).
 // qlist (optional): the searched sorted positions are qlist[q0..q1) instead
 // of q0..q1; qcount (optional, device): only the first *qcount of them.
 // row_base (>= 0): without scatter_ids, sorted position sq goes to row
@@ -55,12 +56,14 @@ constexpr int kCollectRowPad = 8;
 // collect: for sorted queries sq in [q0, q1), every in-radius key goes to
 // lists[sq*cap + j]; counts[sq] = number found; queries with more than cap are
 // appended to overflow[0..*n_overflow).  qrows (optional): a separate query
-// set's rows in the grid's cell order.  rows must be readable kCollectRowPad
-// rows past P.n (the kernel loads whole 8-row passes and masks the excess).
+// set's rows in the grid's cell order.  qlist (optional): the searched sorted
+// positions are qlist[q0..q1) instead of q0..q1.  rows must be readable
+// kCollectRowPad rows past P.n (the kernel loads whole 8-row passes and masks
+// the excess).
 cudaError_t launch_collect_d3(const float* rows, const int* starts, const GridPlan& P, float r2,
                               int cap, unsigned long long* lists, int* counts, int* overflow,
                               int* n_overflow, int q0, int q1, cudaStream_t s,
-                              const float* qrows = nullptr);
+                              const float* qrows = nullptr, const int* qlist = nullptr);
 // collect for D != 3 (any grid the planner makes, K-independent): the same
 // lists as launch_collect_d3 from one thread per query over its 3^g shell;
 // qproj: the queries' projected coordinates on a principal-axis grid (the
@@ -68,13 +71,14 @@ cudaError_t launch_collect_d3(const float* rows, const int* starts, const GridPl
 cudaError_t launch_collect_nd(const float* rows, const int* ids, const int* starts, const GridPlan& P,
                               float r2, int cap, unsigned long long* lists, int* counts, int* overflow,
                               int* n_overflow, int q0, int q1, cudaStream_t s, const float* qrows = nullptr,
-                              const float* qproj = nullptr);
+                              const float* qproj = nullptr, const int* qlist = nullptr);
 // emit: for output rows q < n -- sorted position map[q] (map = inv: rows in
 // original order), or q0 + q without map -- whose count is at most cap, the K
-// smallest keys ascending to out[k*n + q], padded (-1, r2).
+// smallest keys ascending to out[k*n + q], padded (-1, r2).  map_range: the
+// number of sorted positions map's entries index (default n).
 cudaError_t launch_emit_lists(const unsigned long long* lists, const int* counts, const int* map,
                               int q0, int n, int K, int cap, float r2, int* oidx, float* odist,
-                              cudaStream_t s);
+                              cudaStream_t s, int map_range = -1);
 // out[k*N + ids[sq]] = in[k*N + sq]
 cudaError_t launch_unpermute(const int* in_idx, const float* in_dist, const int* ids, int n,
                              int K, int* out_idx, float* out_dist, cudaStream_t s);

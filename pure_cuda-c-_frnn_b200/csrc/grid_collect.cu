@@ -53,11 +53,12 @@ __global__ void __launch_bounds__(256)
                       float r2, int cap, unsigned long long* __restrict__ lists,
                       int* __restrict__ counts, int* __restrict__ overflow,
                       int* __restrict__ n_overflow, int q0, int q1,
-                      const float4* __restrict__ qrows) {
+                      const float4* __restrict__ qrows, const int* __restrict__ qlist) {
     // queries: the points themselves (qrows == rows) or a separate set in
-    // the same grid's cell order
-    const int sq = q0 + blockIdx.x * blockDim.x + threadIdx.x;
-    if (sq >= q1) return;
+    // the same grid's cell order; sorted positions [q0, q1), or qlist[q0..q1)
+    const int qi = q0 + blockIdx.x * blockDim.x + threadIdx.x;
+    if (qi >= q1) return;
+    const int sq = qlist ? __ldg(&qlist[qi]) : qi;
     const float4 q = __ldg(&qrows[sq]);
     const float cs = P.cell, eps = P.eps;
     const int gx = cell_coord(q.x, P.origin[0], P.inv_cell, P.res[0]);
@@ -114,13 +115,15 @@ __global__ void __launch_bounds__(256)
                       const int* __restrict__ starts, GridPlan P, float r2, int cap,
                       unsigned long long* __restrict__ lists, int* __restrict__ counts,
                       int* __restrict__ overflow, int* __restrict__ n_overflow, int q0, int q1,
-                      const float4* __restrict__ qrows, const float4* __restrict__ qproj) {
+                      const float4* __restrict__ qrows, const float4* __restrict__ qproj,
+                      const int* __restrict__ qlist) {
     // the bound span gaps are tested against
     const float gap_r2 = qproj ? P.pre_r2 : r2;
     constexpr int W = NV == 1 ? 8 : (NV == 2 ? 4 : 2);  // rows in flight per pass
     static_assert(W <= kCollectRowPad, "passes read at most kCollectRowPad rows past a span");
-    const int sq = q0 + blockIdx.x * blockDim.x + threadIdx.x;
-    if (sq >= q1) return;
+    const int qi = q0 + blockIdx.x * blockDim.x + threadIdx.x;
+    if (qi >= q1) return;
+    const int sq = qlist ? __ldg(&qlist[qi]) : qi;
     float4 q[NV];
 #pragma unroll
     for (int v = 0; v < NV; ++v) q[v] = __ldg(&qrows[(long long)sq * NV + v]);
@@ -278,7 +281,7 @@ template <int KN>
 __global__ void __launch_bounds__(128, 5)
     emit_lists_kernel(const unsigned long long* __restrict__ lists, const int* __restrict__ counts,
                       const int* __restrict__ map, int q0, int n, int K, int cap, float r2,
-                      int* __restrict__ oidx, float* __restrict__ odist) {
+                      int* __restrict__ oidx, float* __restrict__ odist, int map_range) {
     // output row q: sorted position map[q] (original order), or q0 + q (a
     // slice of the sorted order).  The block's 128 rows are dealt to its
     // threads by the number of 16-key batches their lists need, so a warp's
@@ -292,7 +295,7 @@ __global__ void __launch_bounds__(128, 5)
     if (q_own < n) {
         sq_own = map ? __ldg(&map[q_own]) : q0 + q_own;
         // a map entry outside [0, n) only exists after a scan gave up
-        cnt_own = (unsigned)sq_own < (unsigned)(map ? n : q0 + n) ? __ldg(&counts[sq_own]) : 0;
+        cnt_own = (unsigned)sq_own < (unsigned)(map ? map_range : q0 + n) ? __ldg(&counts[sq_own]) : 0;
         cls = cnt_own > cap ? 0 : min((cnt_own + 15) >> 4, kEmitClasses - 1);
     }
     if (t <= kEmitClasses) hist[t] = 0;
@@ -308,7 +311,7 @@ __global__ void __launch_bounds__(128, 5)
     const int q = blockIdx.x * 128 + src;
     if (q >= n) return;
     const int sq = map ? __ldg(&map[q]) : q0 + q;
-    if (map && (unsigned)sq >= (unsigned)n) return;  // only after a scan gave up
+    if (map && (unsigned)sq >= (unsigned)map_range) return;  // only after a scan gave up
     const int cnt = __ldg(&counts[sq]);
     if (cnt > cap) return;  // searched by the overflow pass
     unsigned long long a[KN];
@@ -327,11 +330,12 @@ __global__ void __launch_bounds__(128, 5)
 
 cudaError_t launch_collect_d3(const float* rows, const int* starts, const GridPlan& P, float r2,
                               int cap, unsigned long long* lists, int* counts, int* overflow,
-                              int* n_overflow, int q0, int q1, cudaStream_t s, const float* qrows) {
+                              int* n_overflow, int q0, int q1, cudaStream_t s, const float* qrows,
+                              const int* qlist) {
     if (q1 <= q0) return cudaSuccess;
     collect_d3_kernel<<<(q1 - q0 + 255) / 256, 256, 0, s>>>(
         reinterpret_cast<const float4*>(rows), starts, P, r2, cap, lists, counts, overflow, n_overflow,
-        q0, q1, reinterpret_cast<const float4*>(qrows ? qrows : rows));
+        q0, q1, reinterpret_cast<const float4*>(qrows ? qrows : rows), qlist);
     return cudaGetLastError();
 }
 
@@ -339,10 +343,11 @@ namespace {
 template <int NV, int G>
 cudaError_t launch_nd(const float* rows, const int* ids, const int* starts, const GridPlan& P, float r2,
                       int cap, unsigned long long* lists, int* counts, int* overflow, int* n_overflow, int q0,
-                      int q1, cudaStream_t s, const float* qrows, const float* qproj) {
+                      int q1, cudaStream_t s, const float* qrows, const float* qproj, const int* qlist) {
     collect_nd_kernel<NV, G><<<(q1 - q0 + 255) / 256, 256, 0, s>>>(
         reinterpret_cast<const float4*>(rows), ids, starts, P, r2, cap, lists, counts, overflow, n_overflow,
-        q0, q1, reinterpret_cast<const float4*>(qrows ? qrows : rows), reinterpret_cast<const float4*>(qproj));
+        q0, q1, reinterpret_cast<const float4*>(qrows ? qrows : rows), reinterpret_cast<const float4*>(qproj),
+        qlist);
     return cudaGetLastError();
 }
 }  // namespace
@@ -350,12 +355,12 @@ cudaError_t launch_nd(const float* rows, const int* ids, const int* starts, cons
 cudaError_t launch_collect_nd(const float* rows, const int* ids, const int* starts, const GridPlan& P,
                               float r2, int cap, unsigned long long* lists, int* counts, int* overflow,
                               int* n_overflow, int q0, int q1, cudaStream_t s, const float* qrows,
-                              const float* qproj) {
+                              const float* qproj, const int* qlist) {
     if (q1 <= q0) return cudaSuccess;
     if (qproj && !(P.pre_r2 > 0.0f)) return cudaErrorInvalidValue;  // a principal grid carries its bound
     const int nv = P.row / 4;
 #define FRNN_ND(NV, G) return launch_nd<NV, G>(rows, ids, starts, P, r2, cap, lists, counts, overflow, \
-                                                n_overflow, q0, q1, s, qrows, qproj)
+                                                n_overflow, q0, q1, s, qrows, qproj, qlist)
     if (nv == 1 && !qproj) {
         if (P.g == 1) FRNN_ND(1, 1);
         if (P.g == 2) FRNN_ND(1, 2);
@@ -386,15 +391,16 @@ cudaError_t launch_collect_nd(const float* rows, const int* ids, const int* star
 
 cudaError_t launch_emit_lists(const unsigned long long* lists, const int* counts, const int* map,
                               int q0, int n, int K, int cap, float r2, int* oidx, float* odist,
-                              cudaStream_t s) {
+                              cudaStream_t s, int map_range) {
     if (K > 32) return cudaErrorInvalidValue;  // the register top-K holds at most 32 keys
     if (n <= 0) return cudaSuccess;
+    if (map_range < 0) map_range = n;
     if (K <= 16)
         emit_lists_kernel<16><<<(n + 127) / 128, 128, 0, s>>>(lists, counts, map, q0, n, K, cap, r2,
-                                                              oidx, odist);
+                                                              oidx, odist, map_range);
     else
         emit_lists_kernel<32><<<(n + 127) / 128, 128, 0, s>>>(lists, counts, map, q0, n, K, cap, r2,
-                                                              oidx, odist);
+                                                              oidx, odist, map_range);
     return cudaGetLastError();
 }
 

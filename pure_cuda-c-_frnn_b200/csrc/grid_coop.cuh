@@ -28,6 +28,14 @@ namespace coop {
 
 constexpr int kWarps = 4;    // warps per block
 constexpr int kGroup = 8;    // queries per group
+// Queries per group on principal-axis grids, where a cell rarely holds more
+// than one query (fewer group slots keep the screening loop in registers).
+// Build-time launch-policy knob.
+#ifndef FRNN_COOP_PRJ_GROUP
+#define FRNN_COOP_PRJ_GROUP 8
+#endif
+constexpr int kGroupPrj = FRNN_COOP_PRJ_GROUP;
+static_assert(kGroupPrj >= 1 && kGroupPrj <= 8, "group slots fit the 8-bit candidate masks");
 
 // Launch policy: minimum resident blocks per SM (which caps registers per
 // thread) for the D = 3 kernel and for the wider-row kernels; build-time
@@ -40,6 +48,9 @@ constexpr int kGroup = 8;    // queries per group
 #ifndef FRNN_COOP_ND_MIN_BLOCKS
 #define FRNN_COOP_ND_MIN_BLOCKS 4
 #endif
+#ifndef FRNN_COOP_PRJ_MIN_BLOCKS
+#define FRNN_COOP_PRJ_MIN_BLOCKS 4
+#endif
 
 // List capacity for K: room for a whole chunk of acceptances (32) on top of K,
 // rounded to the bitonic network sizes the warp sort handles.
@@ -48,13 +59,13 @@ __host__ __device__ constexpr int list_cap(int K) { return K <= 32 ? 64 : (K <= 
 // Per-warp shared memory: the group's query rows, its 64-bit acceptance
 // bounds, the group's projected query coordinates (principal-axis grids),
 // then the group's candidate lists.
-template <int NV, bool D3>
+template <int NV, bool D3, int GR = kGroup>
 __host__ __device__ constexpr size_t rows_bytes() {
-    return (size_t)kGroup * NV * 16 + (size_t)kGroup * 8 + (size_t)kGroup * kProjStride * 4;
+    return (size_t)GR * NV * 16 + (size_t)GR * 8 + (size_t)GR * kProjStride * 4;
 }
-template <int NV, bool D3>
+template <int NV, bool D3, int GR = kGroup>
 __host__ __device__ constexpr size_t warp_bytes(int K) {
-    return rows_bytes<NV, D3>() + (size_t)kGroup * list_cap(K) * 8;
+    return rows_bytes<NV, D3, GR>() + (size_t)GR * list_cap(K) * 8;
 }
 
 // Warp-wide ascending bitonic sort of 32*E keys held E per lane; element p of
@@ -227,9 +238,11 @@ struct Shell<1> {
 // lengthens a distance -- so only candidates that pass load their full row.
 //
 // Group state (query rows, bounds, list lengths) is warp-uniform and lives in
-// registers of every lane; the group loop is unrolled over kGroup slots.
-template <int NV, int G, bool D3, bool PRJ>
-__global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FRNN_COOP_ND_MIN_BLOCKS)
+// registers of every lane; the group loop is unrolled over GR slots.
+template <int NV, int G, bool D3, bool PRJ, int GR = kGroup>
+__global__ void __launch_bounds__(kWarps * 32, D3    ? FRNN_COOP_D3_MIN_BLOCKS
+                                               : PRJ ? FRNN_COOP_PRJ_MIN_BLOCKS
+                                                     : FRNN_COOP_ND_MIN_BLOCKS)
     grid_coop_kernel(const float4* __restrict__ rows, const int* __restrict__ ids,
                      const int* __restrict__ starts, GridPlan P, int K, float r2, int q0, int q1,
                      int* __restrict__ oidx, float* __restrict__ odist, long long ostride,
@@ -243,12 +256,12 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
     if (qcount) q1 = min(q1, q0 + __ldg(qcount));  // list length known only on the device
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int cap = list_cap(K);
-    unsigned char* wbase = smem + (size_t)warp * warp_bytes<NV, D3>(K);
-    float4* qrows = reinterpret_cast<float4*>(wbase);  // [kGroup][NV]
+    unsigned char* wbase = smem + (size_t)warp * warp_bytes<NV, D3, GR>(K);
+    float4* qrows = reinterpret_cast<float4*>(wbase);  // [GR][NV]
     unsigned long long* gthr =
-        reinterpret_cast<unsigned long long*>(wbase + (size_t)kGroup * NV * 16);  // [kGroup]
-    float4* qprj = reinterpret_cast<float4*>(wbase + (size_t)kGroup * NV * 16 + (size_t)kGroup * 8);
-    unsigned long long* lists = reinterpret_cast<unsigned long long*>(wbase + rows_bytes<NV, D3>());
+        reinterpret_cast<unsigned long long*>(wbase + (size_t)GR * NV * 16);  // [GR]
+    float4* qprj = reinterpret_cast<float4*>(wbase + (size_t)GR * NV * 16 + (size_t)GR * 8);
+    unsigned long long* lists = reinterpret_cast<unsigned long long*>(wbase + rows_bytes<NV, D3, GR>());
 
     const int base = q0 + (blockIdx.x * kWarps + warp) * 32;
     if (base >= q1) return;
@@ -280,20 +293,20 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
     constexpr int kRows = Shell<G>::rows;  // rows of the shell (axis 0 merged), 32 per pass
     int g0 = 0;
     while (g0 < nq) {
-        // ---- the group: lanes g0.. with the same cell, at most kGroup -------
+        // ---- the group: lanes g0.. with the same cell, at most GR -------
         const long long c0 = __shfl_sync(0xffffffffu, mycell, g0);
         const unsigned same = __ballot_sync(0xffffffffu, mycell == c0);
         const unsigned from = same >> g0;
         const int run = (~from == 0u) ? 32 - g0 : __ffs(~from) - 1;
-        const int gq = min(run, kGroup);
+        const int gq = min(run, GR);
 
         // group state: bounds and list lengths are warp-uniform registers;
         // query rows and the 64-bit bounds (read only on exact ties) are in
         // shared memory
-        float glim[kGroup];
-        int gcnt[kGroup];
+        float glim[GR];
+        int gcnt[GR];
 #pragma unroll
-        for (int g = 0; g < kGroup; ++g) {
+        for (int g = 0; g < GR; ++g) {
             glim[g] = r2;
             gcnt[g] = 0;
         }
@@ -362,7 +375,7 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
             const int j = valid ? js + (t - je) : 0;
             // PRJ: which group queries this candidate can be a neighbour of,
             // from the projected coordinates alone (bit g)
-            unsigned near = valid ? 0xffu : 0u;
+            unsigned near = valid ? (1u << GR) - 1u : 0u;
             if constexpr (PRJ) {
                 near = 0u;
                 if (valid) {
@@ -370,7 +383,7 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
 #pragma unroll
                     for (int v = 0; v < kProjStride / 4; ++v) pp[v] = __ldg(&proj[(long long)j * (kProjStride / 4) + v]);
 #pragma unroll
-                    for (int g = 0; g < kGroup; ++g) {
+                    for (int g = 0; g < GR; ++g) {
                         if (g < gq) {
                             float d2p = 0.0f;
 #pragma unroll
@@ -396,7 +409,7 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
             const int pid = D3 ? __float_as_int(p[0].w) : (near ? __ldg(&ids[j]) : 0);
 
 #pragma unroll
-            for (int g = 0; g < kGroup; ++g) {
+            for (int g = 0; g < GR; ++g) {
                 if (g < gq) {
                     float d2;
                     if constexpr (D3) {
@@ -433,12 +446,12 @@ __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FR
 
         // ---- emit the group ------------------------------------------------
 #pragma unroll
-        for (int g = 0; g < kGroup; ++g) {
+        for (int g = 0; g < GR; ++g) {
             if (g < gq) {
                 const int n = gcnt[g];
                 const int sq = qlist ? __ldg(&qlist[base + g0 + g]) : base + g0 + g;
                 const long long orow =
-                    scatter_ids ? (long long)__ldg(&scatter_ids[sq]) : (long long)sq - row_base;
+                    (scatter_ids ? (long long)__ldg(&scatter_ids[sq]) : (long long)sq) - row_base;
                 const unsigned long long* list = lists + (size_t)g * cap;
                 // an output row outside [0, ostride) only comes from a
                 // permutation left incomplete by a scan that gave up

@@ -80,12 +80,13 @@ struct CoopArgs {
 
 template <int NV, int G, bool D3, bool PRJ = false>
 cudaError_t launch_coop(const CoopArgs& a, cudaStream_t s) {
-    const size_t smem = (size_t)coop::kWarps * coop::warp_bytes<NV, D3>(a.K);
-    cudaError_t err = set_smem(coop::grid_coop_kernel<NV, G, D3, PRJ>, smem);
+    constexpr int GR = PRJ ? coop::kGroupPrj : coop::kGroup;
+    const size_t smem = (size_t)coop::kWarps * coop::warp_bytes<NV, D3, GR>(a.K);
+    cudaError_t err = set_smem(coop::grid_coop_kernel<NV, G, D3, PRJ, GR>, smem);
     if (err != cudaSuccess) return err;
     const int per_block = coop::kWarps * 32;
     const int blocks = (a.q1 - a.q0 + per_block - 1) / per_block;
-    coop::grid_coop_kernel<NV, G, D3, PRJ><<<blocks, coop::kWarps * 32, smem, s>>>(
+    coop::grid_coop_kernel<NV, G, D3, PRJ, GR><<<blocks, coop::kWarps * 32, smem, s>>>(
         reinterpret_cast<const float4*>(a.rows), a.ids, a.starts, a.P, a.K, a.r2, a.q0, a.q1, a.oidx,
         a.odist, a.ostride, a.scatter_ids, a.qlist, a.qcount, a.row_base,
         reinterpret_cast<const float4*>(a.proj), reinterpret_cast<const float4*>(a.qrows ? a.qrows : a.rows),
@@ -103,7 +104,8 @@ cudaError_t launch_grid_search(const float* rows, const int* ids, const int* sta
                                const float* qproj) {
     if (q1 <= q0) return cudaSuccess;
     const CoopArgs a{rows, ids, starts, P, K, r2, q0, q1, oidx, odist, ostride, scatter_ids,
-                     qlist, qcount, row_base < 0 ? (long long)q0 : row_base, proj, qrows, qproj};
+                     qlist, qcount, row_base >= 0 ? row_base : (scatter_ids ? 0LL : (long long)q0), proj, qrows,
+                     qproj};
     if (P.dim == 3 && P.g == 3 && !proj) return launch_coop<1, 3, true>(a, s);
     // (row float4s, grid axes) pairs the planner produces: leading coordinates
     // G = min(D, 4); principal axes (D > 4) G in 2..6

@@ -9,31 +9,34 @@
 //   1. root: plan and build -- on the grid path the bounding box, the plan
 //      (principal axes when they pay), the cell histogram, scan and
 //      counting-sort scatter; on the tensor-core path the box and the fp16
-//      scale.  On the grid path the candidates of every 64th cell-sorted
-//      query (the point count of its 3^g shell, what a search scans) sample
-//      the work along the query order, and frnn_shard_partition cuts it into
-//      slices of equal estimated work;
-//   2. header broadcast (plan, sizes, slice bounds, the root's status), then
-//      an all-reduce of every rank's status, so that a rank that cannot take
-//      part makes every rank return the same error instead of waiting;
+//      scale.  Rank r owns the queries of one range of ORIGINAL indices, so
+//      its results are one contiguous column block of the [K, N] output.  On
+//      the grid path the ranges are cut so that every rank gets the same
+//      estimated work: the candidates of every 64th cell-sorted query (the
+//      point count of its 3^g shell, what a search scans) are summed into
+//      4,096 buckets of original index, and frnn_shard_partition cuts them;
+//   2. header broadcast (plan, sizes, ranges, the root's status and the IPC
+//      handles of its result buffers), then an all-reduce of every rank's
+//      status, so that a rank that cannot take part makes every rank return
+//      the same error instead of waiting;
 //   3. data broadcast in one NCCL group: the cell-sorted rows, their ids, the
 //      cell starts (and the sorted projected coordinates of a principal-axis
 //      grid); on the brute-force paths the cloud itself (every rank then
 //      prepares its own fp16 tiles from it);
-//   4. every rank searches its slice of the query order (sorted positions
-//      on the grid path, 128-query tiles on the tensor-core path, input order
-//      on SIMT brute force) with the engine's own kernels, in a few chunks;
-//   5. each finished chunk goes to the root at once (NCCL send / receive on a
-//      high-priority communication stream) while the next chunk is searched,
-//      and the root scatters every arrived chunk into the [K, N] results in
-//      original query order -- so the gather overlaps the search and only the
-//      last chunk's transfer remains after it.
+//   4. every rank searches its queries in cell order (the grid path lists
+//      their sorted positions with a scan), writing rows in original order;
+//   5. each rank's block goes straight into the root's result buffers with
+//      a 2-D copy over NVLink on a copy engine (the root's buffers are mapped
+//      through CUDA IPC); no SM takes part in the gather, so with several
+//      chunks per rank the copy of one chunk overlaps the search of the
+//      next.  A final all-reduce on every rank's stream, after its copies,
+//      tells the root that every block has landed.
 //
 // Every wait on the host is bounded (FRNN_ERR_TIMEOUT after the shard's
 // timeout; the communicator is then aborted and the shard unusable); an NCCL
 // error reported by the communicator ends the call with FRNN_ERR_COMM.
-// The only inter-GPU traffic is NCCL's: no kernel here touches another GPU's
-// memory.
+// No kernel here touches another GPU's memory; the gather's writes to the
+// root are copy-engine copies.
 #include <algorithm>
 #include <chrono>
 #include <cstring>
@@ -62,25 +65,27 @@ struct ShardHeader {
     int nparts;
     GridPlan P;
     TcPlan tc;
-    int bounds[kMaxShardRanks + 1];  // slice r = query order [bounds[r], bounds[r+1])
+    cudaIpcMemHandle_t res_idx, res_dist;  // the root's result buffers
+    int bounds[kMaxShardRanks + 1];  // rank r owns original query indices [bounds[r], bounds[r+1])
 };
 static_assert(std::is_trivially_copyable<ShardHeader>::value, "sent as bytes");
 
 // stages timed when the engine's timing is on: the root's plan and build, the
-// header and status exchange, the data broadcast, the chunked slice search
-// (engine stream), the root's receives and scatters (communication stream)
+// header and status exchange, the data broadcast, the rank's search (engine
+// stream), its copies into the root's buffers (communication stream)
 enum ShardStage { SH_BUILD = 0, SH_HEADER, SH_BCAST, SH_SEARCH, SH_GATHER, SH_STAGES };
 
-// Chunks of a rank's slice: each is searched, then sent while the next one is
-// searched.  Slices below kChunkMin queries are one chunk.
+// Chunks of a rank's range: each is searched, then copied to the root while
+// the next one is searched.  Chunks hold at least kChunkMin queries.
 constexpr int kMaxChunks = 8;
 constexpr int kChunkMin = 65536;
-// Every kSampleStride-th cell-sorted query samples the search work.
+// Every kSampleStride-th cell-sorted query samples the search work, summed
+// into kWorkBuckets ranges of original index.
 constexpr int kSampleStride = 64;
+constexpr int kWorkBuckets = 4096;
 
-// Chunk c of the slice [b0, b1) is [cb[c], cb[c+1]); on the tensor-core path
-// every cut is a multiple of 128 (whole query tiles).  Every rank computes the
-// same cuts for every slice.
+// Chunk c of the range [b0, b1) is [cb[c], cb[c+1]); on the tensor-core path
+// every cut is a multiple of 128 (whole query tiles).
 int chunk_bounds(int b0, int b1, int path, int chunks, int* cb) {
     const int rows = b1 - b0;
     const int m = std::max(1, std::min(chunks, rows / kChunkMin));
@@ -102,18 +107,25 @@ struct frnn_shard {
     int rank = 0, nranks = 1;
     bool broken = false;
     double timeout_s = 120.0;
-    DevBuf d_hdr, d_stat, work, pts, st_idx, st_dist, res_idx, res_dist;
+    DevBuf d_hdr, d_stat, work, pts, res_idx, res_dist;
+    // the grid path's per-rank query lists: original -> sorted position, the
+    // range's flags and their prefix, the sorted positions of each chunk
+    DevBuf inv, flags, fpos, fstatus, qlist;
+    unsigned fepoch = 0;
     ShardHeader* h_hdr = nullptr;   // pinned
     int* h_stat = nullptr;          // pinned, 16 ints
-    uint64_t* h_work = nullptr;     // pinned, grows with the sample count
-    int* h_wstart = nullptr;
-    size_t h_samples = 0;
-    cudaStream_t cs = nullptr;      // communication stream (gather)
+    uint64_t* h_work = nullptr;     // pinned, kWorkBuckets
+    int* h_wstart = nullptr;        // pinned, kWorkBuckets
+    cudaStream_t cs = nullptr;      // communication stream (the copies to the root)
     int chunks = 1;                 // FRNN_SHARD_OPT_CHUNKS
     int comm_priority = 0;          // FRNN_SHARD_OPT_COMM_PRIORITY
     cudaEvent_t chunk_ev[kMaxChunks] = {}, comm_done = nullptr;
     cudaEvent_t ev[2 * SH_STAGES] = {};
     bool ev_used[SH_STAGES] = {};
+    // the root's result buffers as mapped on this rank (other ranks)
+    cudaIpcMemHandle_t open_h_idx{}, open_h_dist{};
+    int* peer_idx = nullptr;
+    float* peer_dist = nullptr;
     long long bcast_bytes = 0, gather_bytes = 0;
     int last_rows = 0, last_path = 0;
 };
@@ -135,12 +147,12 @@ int comm_fail(frnn_shard* sh, ncclResult_t r, const char* what) {
         if (r__ != ncclSuccess) return comm_fail(sh, r__, what);      \
     } while (0)
 
-void sh_begin(frnn_shard* sh, int st) {
-    if (sh->e->timing) cudaEventRecord(sh->ev[2 * st], sh->e->stream);
+void sh_begin(frnn_shard* sh, int st, cudaStream_t s) {
+    if (sh->e->timing) cudaEventRecord(sh->ev[2 * st], s);
 }
-void sh_end(frnn_shard* sh, int st) {
+void sh_end(frnn_shard* sh, int st, cudaStream_t s) {
     if (sh->e->timing) {
-        cudaEventRecord(sh->ev[2 * st + 1], sh->e->stream);
+        cudaEventRecord(sh->ev[2 * st + 1], s);
         sh->ev_used[st] = true;
     }
 }
@@ -176,37 +188,13 @@ int wait_stream(frnn_shard* sh, const char* what) {
     }
 }
 
-// Root side of step 5: one arrived chunk, [K, rows] at src (row j = query
-// order position q0 + j), into out[k*N + q] with q = ids[q0 + j] on the grid
-// path (cell order) or q0 + j on the brute-force paths.
-__global__ void shard_scatter_kernel(const int* __restrict__ src_idx, const float* __restrict__ src_dist, int q0,
-                                     int rows, const int* __restrict__ ids, int N, int* __restrict__ out_idx,
-                                     float* __restrict__ out_dist) {
-    const int j = blockIdx.x * blockDim.x + threadIdx.x;
-    if (j >= rows) return;
-    const int k = blockIdx.y;
-    const int q = ids ? __ldg(&ids[q0 + j]) : q0 + j;
-    if ((unsigned)q >= (unsigned)N) return;  // only after a scan gave up (FRNN_ERR_TIMEOUT)
-    const long long src = (long long)k * rows + j, dst = (long long)k * N + q;
-    out_idx[dst] = __ldg(&src_idx[src]);
-    out_dist[dst] = __ldg(&src_dist[src]);
-}
-
-cudaError_t launch_shard_scatter(const int* src_idx, const float* src_dist, int q0, int rows, int K, const int* ids,
-                                 int N, int* out_idx, float* out_dist, cudaStream_t s) {
-    if (rows <= 0) return cudaSuccess;
-    dim3 grid((unsigned)((rows + 255) / 256), (unsigned)K);
-    shard_scatter_kernel<<<grid, 256, 0, s>>>(src_idx, src_dist, q0, rows, ids, N, out_idx, out_dist);
-    return cudaGetLastError();
-}
-
 // The work of the cell-sorted queries, sampled: for sorted position
 // i * stride, the points in its cell's 3^g shell (the x-merged rows a grid
-// search walks) plus a fixed charge per row.  work[i] covers the stride
-// queries from there.
+// search walks) plus a fixed charge per row, for the stride queries from
+// there, added to the bucket of the sample's original index.
 __global__ void sample_work_kernel(const float* __restrict__ rows, const float* __restrict__ proj_s,
-                                   const int* __restrict__ starts, GridPlan P, int stride, int nsamples,
-                                   unsigned long long* __restrict__ work) {
+                                   const int* __restrict__ starts, const int* __restrict__ ids, GridPlan P,
+                                   int stride, int nsamples, unsigned long long* __restrict__ bucket_work) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= nsamples) return;
     const long long sq = (long long)i * stride;
@@ -234,27 +222,39 @@ __global__ void sample_work_kernel(const float* __restrict__ rows, const float* 
             total += (unsigned long long)max(s1 - s0, 0);
         }
     }
-    work[i] = (total + 8ull * nrows) * (unsigned long long)min((long long)stride, (long long)P.n - sq);
+    const long long q = __ldg(&ids[sq]);
+    if ((unsigned long long)q >= (unsigned long long)P.n) return;  // only after a scan gave up
+    const int b = (int)(q * kWorkBuckets / P.n);
+    atomicAdd(&bucket_work[b], (total + 8ull * nrows) * (unsigned long long)min((long long)stride, (long long)P.n - sq));
 }
 
-int grow_pinned_samples(frnn_shard* sh, size_t n) {
-    if (sh->h_samples >= n) return FRNN_OK;
-    if (sh->h_work) cudaFreeHost(sh->h_work);
-    if (sh->h_wstart) cudaFreeHost(sh->h_wstart);
-    sh->h_work = nullptr;
-    sh->h_wstart = nullptr;
-    sh->h_samples = 0;
-    const size_t want = n + n / 8 + 64;
-    if (cudaMallocHost(&sh->h_work, want * 8) != cudaSuccess ||
-        cudaMallocHost(&sh->h_wstart, want * 4) != cudaSuccess) {
-        cudaGetLastError();
-        return fail(sh->e, FRNN_ERR_OOM, "pinned staging for the partition");
-    }
-    sh->h_samples = want;
-    return FRNN_OK;
+// inv[ids[sq]] = sq: each query's sorted position
+__global__ void inv_kernel(const int* __restrict__ ids, int n, int* __restrict__ inv) {
+    const int sq = blockIdx.x * blockDim.x + threadIdx.x;
+    if (sq >= n) return;
+    const int q = __ldg(&ids[sq]);
+    if ((unsigned)q < (unsigned)n) inv[q] = sq;
 }
 
-// Step 1 on the root: plan, build and partition into h_hdr.
+// flags[sq] = 1 when the query at sorted position sq has an original index in [lo, hi)
+__global__ void range_flags_kernel(const int* __restrict__ ids, int n, int lo, int hi, int* __restrict__ flags) {
+    const int sq = blockIdx.x * blockDim.x + threadIdx.x;
+    if (sq >= n) return;
+    const int q = __ldg(&ids[sq]);
+    flags[sq] = (q >= lo && q < hi) ? 1 : 0;
+}
+
+// qlist[pos[sq]] = sq for every flagged sq (pos: exclusive prefix of flags;
+// at most cap entries)
+__global__ void compact_kernel(const int* __restrict__ flags, const int* __restrict__ pos, int n, int cap,
+                               int* __restrict__ qlist) {
+    const int sq = blockIdx.x * blockDim.x + threadIdx.x;
+    if (sq >= n || !__ldg(&flags[sq])) return;
+    const int p = __ldg(&pos[sq]);
+    if ((unsigned)p < (unsigned)cap) qlist[p] = sq;
+}
+
+// Step 1 on the root: plan, build and the owners' ranges into h_hdr.
 int root_plan(frnn_shard* sh, const float* d_pts, int N, int dim, int K, float radius) {
     frnn_engine* e = sh->e;
     ShardHeader& H = *sh->h_hdr;
@@ -271,22 +271,22 @@ int root_plan(frnn_shard* sh, const float* d_pts, int N, int dim, int K, float r
         if (st != FRNN_OK) return st;
         if (!H.tc.ok) H.path = FRNN_PATH_BRUTE;
     }
+    for (int r = 0; r <= parts; ++r) H.bounds[r] = (int)((long long)N * r / parts);
     if (H.path == FRNN_PATH_GRID) {
         cudaStream_t s = e->stream;
         int st = build_points(e, d_pts, H.P, H.principal ? e->proj_u.as<float>() : nullptr, false);
         if (st != FRNN_OK) return st;
         if (parts > 1) {
             const int ns = (N + kSampleStride - 1) / kSampleStride;
-            FRNN_GROW(e, sh->work, (size_t)ns * 8);
-            st = grow_pinned_samples(sh, (size_t)ns);
-            if (st != FRNN_OK) return st;
+            FRNN_GROW(e, sh->work, (size_t)kWorkBuckets * 8);
+            FRNN_CHECK(e, cudaMemsetAsync(sh->work.p, 0, (size_t)kWorkBuckets * 8, s), "memset work");
             sample_work_kernel<<<(ns + 127) / 128, 128, 0, s>>>(
-                e->rows.as<float>(), H.principal ? e->proj_s.as<float>() : nullptr, e->starts.as<int>(), H.P,
-                kSampleStride, ns, sh->work.as<unsigned long long>());
+                e->rows.as<float>(), H.principal ? e->proj_s.as<float>() : nullptr, e->starts.as<int>(),
+                e->ids.as<int>(), H.P, kSampleStride, ns, sh->work.as<unsigned long long>());
             FRNN_CHECK(e, cudaGetLastError(), "work sample launch");
             e->launches++;
-            FRNN_CHECK(e, cudaMemcpyAsync(sh->h_work, sh->work.p, (size_t)ns * 8, cudaMemcpyDeviceToHost, s),
-                       "work sample readback");
+            FRNN_CHECK(e, cudaMemcpyAsync(sh->h_work, sh->work.p, (size_t)kWorkBuckets * 8, cudaMemcpyDeviceToHost, s),
+                       "work readback");
             FRNN_CHECK(e, cudaMemcpyAsync(sh->h_stat, e->err_flag.p, sizeof(int), cudaMemcpyDeviceToHost, s),
                        "error flag readback");
             FRNN_CHECK(e, cudaStreamSynchronize(s), "partition sync");
@@ -295,19 +295,137 @@ int root_plan(frnn_shard* sh, const float* d_pts, int N, int dim, int K, float r
                 cudaStreamSynchronize(s);
                 return fail(e, FRNN_ERR_TIMEOUT, "a bounded device-side wait gave up");
             }
-            for (int i = 0; i < ns; ++i) sh->h_wstart[i] = i * kSampleStride;
-            if (frnn_shard_partition(sh->h_work, sh->h_wstart, ns, N, parts, H.bounds) != FRNN_OK)
+            for (int b = 0; b < kWorkBuckets; ++b) sh->h_wstart[b] = (int)((long long)N * b / kWorkBuckets);
+            if (frnn_shard_partition(sh->h_work, sh->h_wstart, kWorkBuckets, N, parts, H.bounds) != FRNN_OK)
                 return fail(e, FRNN_ERR_INVALID_ARG, "partition failed");
-        } else {
-            H.bounds[0] = 0;
-            H.bounds[1] = N;
         }
     } else if (H.path == FRNN_PATH_BRUTE_TC) {
+        // whole 128-query tiles; every query costs the same
         const int ntq = (N + 127) / 128;
         for (int r = 0; r <= parts; ++r) H.bounds[r] = std::min(N, (int)((long long)ntq * r / parts) * 128);
-    } else {
-        for (int r = 0; r <= parts; ++r) H.bounds[r] = (int)((long long)N * r / parts);
     }
+    // the results land in these buffers, on this GPU and (mapped) on the others
+    FRNN_GROW(e, sh->res_idx, (size_t)N * K * 4);
+    FRNN_GROW(e, sh->res_dist, (size_t)N * K * 4);
+    if (parts > 1) {
+        FRNN_CHECK(e, cudaIpcGetMemHandle(&H.res_idx, sh->res_idx.p), "result handle");
+        FRNN_CHECK(e, cudaIpcGetMemHandle(&H.res_dist, sh->res_dist.p), "result handle");
+    }
+    return FRNN_OK;
+}
+
+// The root's result buffers on this (non-root) rank, mapped through IPC; the
+// mapping is renewed when the root reallocated them.
+int map_root_results(frnn_shard* sh, const ShardHeader& H) {
+    if (sh->peer_idx && !std::memcmp(&sh->open_h_idx, &H.res_idx, sizeof(H.res_idx)) &&
+        !std::memcmp(&sh->open_h_dist, &H.res_dist, sizeof(H.res_dist)))
+        return FRNN_OK;
+    if (sh->peer_idx) cudaIpcCloseMemHandle(sh->peer_idx);
+    if (sh->peer_dist) cudaIpcCloseMemHandle(sh->peer_dist);
+    sh->peer_idx = nullptr;
+    sh->peer_dist = nullptr;
+    void* pi = nullptr;
+    void* pd = nullptr;
+    FRNN_CHECK(sh->e, cudaIpcOpenMemHandle(&pi, H.res_idx, cudaIpcMemLazyEnablePeerAccess), "map root results");
+    cudaError_t err = cudaIpcOpenMemHandle(&pd, H.res_dist, cudaIpcMemLazyEnablePeerAccess);
+    if (err != cudaSuccess) {
+        cudaIpcCloseMemHandle(pi);
+        return cuda_fail(sh->e, err, "map root results");
+    }
+    sh->peer_idx = static_cast<int*>(pi);
+    sh->peer_dist = static_cast<float*>(pd);
+    sh->open_h_idx = H.res_idx;
+    sh->open_h_dist = H.res_dist;
+    return FRNN_OK;
+}
+
+// The sorted positions of the queries with original index in [lo, hi), in
+// increasing order, to qlist (hi - lo entries): flags, a scan, a compaction.
+int range_queries(frnn_shard* sh, const int* ids, int N, int lo, int hi, int* qlist) {
+    frnn_engine* e = sh->e;
+    cudaStream_t s = e->stream;
+    const long long tiles = scan_tiles(N);
+    FRNN_GROW(e, sh->flags, (size_t)N * 4);
+    FRNN_GROW(e, sh->fpos, ((size_t)N + 1) * 4);
+    const size_t before = sh->fstatus.bytes;
+    FRNN_GROW(e, sh->fstatus, (size_t)tiles * 8 + 16);
+    // status words carry the scan's epoch; new memory could hold words of the
+    // same epoch, so it is cleared first (as for the engine's own scan)
+    if (sh->fstatus.bytes != before) FRNN_CHECK(e, cudaMemsetAsync(sh->fstatus.p, 0, sh->fstatus.bytes, s), "memset");
+    sh->fepoch = (sh->fepoch + 1) & 0x3fffffffu;
+    if (sh->fepoch == 0) {
+        FRNN_CHECK(e, cudaMemsetAsync(sh->fstatus.p, 0, sh->fstatus.bytes, s), "memset");
+        sh->fepoch = 1;
+    }
+    int* ticket = reinterpret_cast<int*>(static_cast<char*>(sh->fstatus.p) + (size_t)tiles * 8);
+    FRNN_CHECK(e, cudaMemsetAsync(ticket, 0, 4, s), "memset ticket");
+    range_flags_kernel<<<(N + 255) / 256, 256, 0, s>>>(ids, N, lo, hi, sh->flags.as<int>());
+    FRNN_CHECK(e, cudaGetLastError(), "flags launch");
+    FRNN_CHECK(e, launch_scan(sh->flags.as<int>(), sh->fpos.as<int>(), N, sh->fstatus.as<unsigned long long>(), ticket,
+                              sh->fepoch, e->err_flag.as<int>(), s),
+               "range scan launch");
+    compact_kernel<<<(N + 255) / 256, 256, 0, s>>>(sh->flags.as<int>(), sh->fpos.as<int>(), N, hi - lo, qlist);
+    FRNN_CHECK(e, cudaGetLastError(), "compact launch");
+    e->launches += 3;
+    return FRNN_OK;
+}
+
+// Search the queries with original index in [lo, hi) (this rank's chunk),
+// results row q - lo of out[k*(hi-lo) + row].
+int search_range(frnn_shard* sh, const ShardHeader& H, const float* pts, int lo, int hi, int* oi, float* od) {
+    frnn_engine* e = sh->e;
+    cudaStream_t s = e->stream;
+    const int N = H.N, K = H.K, dim = H.dim, rows = hi - lo;
+    const float r2 = H.radius * H.radius;
+    if (rows <= 0) return FRNN_OK;
+    if (H.path == FRNN_PATH_BRUTE_TC)
+        return tc_query_tiles(e, pts, N, dim, K, H.radius, oi, od, lo / 128, (hi + 127) / 128);
+    if (H.path == FRNN_PATH_BRUTE) {
+        FRNN_CHECK(e, launch_bruteforce(pts, N, dim, K, r2, lo, hi, oi, od, rows, s), "bruteforce launch");
+        e->launches++;
+        return FRNN_OK;
+    }
+    // grid: the range's sorted positions, then the search in cell order with
+    // rows written in original order
+    const GridPlan& P = H.P;
+    const float* proj_s = H.principal ? e->proj_s.as<float>() : nullptr;
+    const int* ids = e->ids.as<int>();
+    int* qlist = sh->qlist.as<int>();
+    int st = range_queries(sh, ids, N, lo, hi, qlist);
+    if (st != FRNN_OK) return st;
+    if (uses_lists(e, P, K, H.principal != 0)) {
+        const int cap = K <= 16 ? 64 : 128;
+        FRNN_GROW(e, e->lists, (size_t)N * cap * 8);
+        FRNN_GROW(e, e->list_counts, (size_t)N * 4);
+        FRNN_GROW(e, e->overflow, (size_t)N * 4);
+        FRNN_GROW(e, e->n_overflow, 16);
+        FRNN_CHECK(e, cudaMemsetAsync(e->n_overflow.p, 0, 4, s), "memset overflow count");
+        const bool d3 = P.dim == 3 && P.g == 3 && !H.principal;
+        if (d3)
+            FRNN_CHECK(e, launch_collect_d3(e->rows.as<float>(), e->starts.as<int>(), P, r2, cap,
+                                            e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
+                                            e->overflow.as<int>(), e->n_overflow.as<int>(), 0, rows, s, nullptr, qlist),
+                       "collect launch");
+        else
+            FRNN_CHECK(e, launch_collect_nd(e->rows.as<float>(), ids, e->starts.as<int>(), P, r2, cap,
+                                            e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
+                                            e->overflow.as<int>(), e->n_overflow.as<int>(), 0, rows, s, nullptr,
+                                            proj_s, qlist),
+                       "collect launch");
+        // output row q - lo reads sorted position inv[q]
+        FRNN_CHECK(e, launch_emit_lists(e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
+                                        sh->inv.as<int>() + lo, 0, rows, K, cap, r2, oi, od, s, N),
+                   "emit launch");
+        FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), ids, e->starts.as<int>(), P, K, r2, 0, N, oi, od, rows,
+                                         ids, s, e->overflow.as<int>(), e->n_overflow.as<int>(), lo, proj_s),
+                   "overflow search launch");
+        e->launches += 3;
+        return FRNN_OK;
+    }
+    FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), ids, e->starts.as<int>(), P, K, r2, 0, rows, oi, od, rows,
+                                     ids, s, qlist, nullptr, lo, proj_s),
+               "grid search launch");
+    e->launches++;
     return FRNN_OK;
 }
 
@@ -323,7 +441,7 @@ int frnn_shard_partition(const uint64_t* tile_work, const int* tile_start, int64
     bounds[0] = 0;
     bounds[nparts] = N;
     // boundary r sits at the tile edge nearest to the r/nparts quantile of the
-    // cumulative work; tile edges are cell starts, so a slice never splits a cell
+    // cumulative work
     int64_t t = 0;
     unsigned long long before = 0;  // work of tiles [0, t)
     for (int r = 1; r < nparts; ++r) {
@@ -337,10 +455,6 @@ int frnn_shard_partition(const uint64_t* tile_work, const int* tile_start, int64
     }
     return FRNN_OK;
 }
-
-}  // extern "C"
-
-extern "C" {
 
 int frnn_shard_unique_id(unsigned char* id_out) {
     if (!id_out) return FRNN_ERR_INVALID_ARG;
@@ -378,7 +492,9 @@ int frnn_shard_create(frnn_engine* e, int nranks, int rank, const unsigned char*
         return st;
     }
     if (cudaMallocHost(&sh->h_hdr, sizeof(ShardHeader)) != cudaSuccess ||
-        cudaMallocHost(&sh->h_stat, 64) != cudaSuccess) {
+        cudaMallocHost(&sh->h_stat, 64) != cudaSuccess ||
+        cudaMallocHost(&sh->h_work, (size_t)kWorkBuckets * 8) != cudaSuccess ||
+        cudaMallocHost(&sh->h_wstart, (size_t)kWorkBuckets * 4) != cudaSuccess) {
         cudaGetLastError();
         frnn_shard_destroy(sh);
         return fail(e, FRNN_ERR_OOM, "pinned shard staging");
@@ -401,11 +517,13 @@ int frnn_shard_destroy(frnn_shard* sh) {
     {
         DeviceGuard g(sh->e->device);
         cudaStreamSynchronize(sh->e->stream);
+        if (sh->cs) cudaStreamSynchronize(sh->cs);
         const NcclApi* api = nccl_api();
         if (sh->comm && api) api->CommDestroy(sh->comm);
-        if (sh->cs) cudaStreamSynchronize(sh->cs);
-        for (DevBuf* b : {&sh->d_hdr, &sh->d_stat, &sh->work, &sh->pts, &sh->st_idx, &sh->st_dist, &sh->res_idx,
-                          &sh->res_dist})
+        if (sh->peer_idx) cudaIpcCloseMemHandle(sh->peer_idx);
+        if (sh->peer_dist) cudaIpcCloseMemHandle(sh->peer_dist);
+        for (DevBuf* b : {&sh->d_hdr, &sh->d_stat, &sh->work, &sh->pts, &sh->res_idx, &sh->res_dist, &sh->inv,
+                          &sh->flags, &sh->fpos, &sh->fstatus, &sh->qlist})
             if (b->p) cudaFree(b->p);
         if (sh->h_hdr) cudaFreeHost(sh->h_hdr);
         if (sh->h_stat) cudaFreeHost(sh->h_stat);
@@ -485,9 +603,8 @@ int frnn_search_sharded(frnn_shard* sh, int root, const float* d_points_soa, int
     int local = check_search_args(e, is_root ? (const void*)d_points_soa : (const void*)sh, N, dim, K, radius);
     if (local == FRNN_OK && is_root) local = check_device_ptr(e, d_points_soa);
 
-    // 1. root: plan, build, partition
+    // 1. root: plan, build, owners' ranges
     ShardHeader& H = *sh->h_hdr;
-    const size_t bounds_off = offsetof(ShardHeader, bounds);
     if (is_root) {
         std::memset(&H, 0, sizeof(H));
         H.N = N;
@@ -495,14 +612,13 @@ int frnn_search_sharded(frnn_shard* sh, int root, const float* d_points_soa, int
         H.K = K;
         H.radius = radius;
         H.nparts = parts;
-        sh_begin(sh, SH_BUILD);
+        sh_begin(sh, SH_BUILD, s);
         H.status = local == FRNN_OK ? root_plan(sh, d_points_soa, N, dim, K, radius) : local;
-        sh_end(sh, SH_BUILD);
+        sh_end(sh, SH_BUILD, s);
         FRNN_CHECK(e, cudaMemcpyAsync(sh->d_hdr.p, &H, sizeof(H), cudaMemcpyHostToDevice, s), "header upload");
     }
-    (void)bounds_off;
     // 2. header, then every rank's status
-    sh_begin(sh, SH_HEADER);
+    sh_begin(sh, SH_HEADER, s);
     SH_NCCL(sh, api->Broadcast(sh->d_hdr.p, sh->d_hdr.p, sizeof(ShardHeader), ncclUint8, root, sh->comm, s),
             "header broadcast");
     FRNN_CHECK(e, cudaMemcpyAsync(&H, sh->d_hdr.p, sizeof(H), cudaMemcpyDeviceToHost, s), "header readback");
@@ -514,7 +630,7 @@ int frnn_search_sharded(frnn_shard* sh, int root, const float* d_points_soa, int
     }
     if (local == FRNN_OK && (H.N != N || H.dim != dim || H.K != K || H.radius != radius || H.nparts != parts))
         local = fail(e, FRNN_ERR_INVALID_ARG, "N, dim, K and radius must be the same on every rank");
-    const int b0 = H.bounds[sh->rank], b1 = H.bounds[sh->rank + 1], rows = b1 - b0;
+    const int lo = H.bounds[sh->rank], hi = H.bounds[sh->rank + 1], rows = hi - lo;
     const int path = H.path;
     const GridPlan& P = H.P;
     // buffers this rank needs (the root's build made its own)
@@ -530,12 +646,11 @@ int frnn_search_sharded(frnn_shard* sh, int root, const float* d_points_soa, int
     }
     if (local == FRNN_OK) local = grow(e, e->out_idx, (size_t)std::max(rows, 1) * K * 4, "out_idx");
     if (local == FRNN_OK) local = grow(e, e->out_dist, (size_t)std::max(rows, 1) * K * 4, "out_dist");
-    if (local == FRNN_OK && is_root) {
-        if ((local = grow(e, sh->st_idx, (size_t)N * K * 4, "staging")) == FRNN_OK &&
-            (local = grow(e, sh->st_dist, (size_t)N * K * 4, "staging")) == FRNN_OK &&
-            (local = grow(e, sh->res_idx, (size_t)N * K * 4, "results")) == FRNN_OK)
-            local = grow(e, sh->res_dist, (size_t)N * K * 4, "results");
+    if (local == FRNN_OK && path == FRNN_PATH_GRID) {
+        if ((local = grow(e, sh->inv, (size_t)N * 4, "inv")) == FRNN_OK)
+            local = grow(e, sh->qlist, (size_t)std::max(rows, 1) * 4, "qlist");
     }
+    if (local == FRNN_OK && !is_root) local = map_root_results(sh, H);
     sh->h_stat[0] = local;
     FRNN_CHECK(e, cudaMemcpyAsync(sh->d_stat.p, sh->h_stat, sizeof(int), cudaMemcpyHostToDevice, s),
                "status upload");
@@ -544,14 +659,14 @@ int frnn_search_sharded(frnn_shard* sh, int root, const float* d_points_soa, int
                "status readback");
     st = wait_stream(sh, "status all-reduce");
     if (st != FRNN_OK) return st;
-    sh_end(sh, SH_HEADER);
+    sh_end(sh, SH_HEADER, s);
     if (sh->h_stat[1] != FRNN_OK) {
         if (local == FRNN_OK) fail(e, sh->h_stat[1], "another rank could not take part in the sharded search");
         return sh->h_stat[1];
     }
 
     // 3. the data every rank searches
-    sh_begin(sh, SH_BCAST);
+    sh_begin(sh, SH_BCAST, s);
     const float* pts = is_root ? d_points_soa : sh->pts.as<float>();
     SH_NCCL(sh, api->GroupStart(), "group start");
     if (path == FRNN_PATH_GRID) {
@@ -572,115 +687,55 @@ int frnn_search_sharded(frnn_shard* sh, int root, const float* d_points_soa, int
         sh->bcast_bytes = (long long)N * dim * 4;
     }
     SH_NCCL(sh, api->GroupEnd(), "group end");
-    sh_end(sh, SH_BCAST);
+    sh_end(sh, SH_BCAST, s);
 
-    // 4 and 5. this rank's slice, chunk by chunk; every finished chunk goes to
-    // the root on the communication stream while the next is searched, and
-    // the root scatters each arrived chunk
-    const float r2 = radius * radius;
-    const int* scatter_ids = path == FRNN_PATH_GRID ? e->ids.as<int>() : nullptr;
+    // 4 and 5. this rank's queries, chunk by chunk; each finished chunk is
+    // copied into the root's result block on the communication stream (a copy
+    // engine over NVLink) while the next chunk is searched
     if (path == FRNN_PATH_BRUTE_TC && rows > 0) {
         st = tc_prepare(e, pts, N, dim, H.tc);
         if (st != FRNN_OK) return st;
     }
+    if (path == FRNN_PATH_GRID && rows > 0) {
+        inv_kernel<<<(N + 255) / 256, 256, 0, s>>>(e->ids.as<int>(), N, sh->inv.as<int>());
+        FRNN_CHECK(e, cudaGetLastError(), "inv launch");
+        e->launches++;
+    }
+    int* dst_idx = is_root ? sh->res_idx.as<int>() : sh->peer_idx;
+    float* dst_dist = is_root ? sh->res_dist.as<float>() : sh->peer_dist;
     int cb[kMaxChunks + 1];
-    const int m = chunk_bounds(b0, b1, path, sh->chunks, cb);
-    sh_begin(sh, SH_SEARCH);
-    if (is_root && sh->e->timing) cudaEventRecord(sh->ev[2 * SH_GATHER], sh->cs);
-    for (int c = 0; c < m; ++c) {
-        const int q0 = cb[c], q1 = cb[c + 1], n_c = q1 - q0;
-        const size_t off = (size_t)K * (q0 - b0);  // chunk c's [K, n_c] block in this rank's output
+    const int m = chunk_bounds(lo, hi, path, sh->chunks, cb);
+    sh_begin(sh, SH_SEARCH, s);
+    sh_begin(sh, SH_GATHER, sh->cs);
+    for (int c = 0; c < m && rows > 0; ++c) {
+        const int c0 = cb[c], c1 = cb[c + 1], n_c = c1 - c0;
+        if (n_c <= 0) continue;
+        const size_t off = (size_t)K * (c0 - lo);  // chunk c's [K, n_c] block in this rank's output
         int* oi = e->out_idx.as<int>() + off;
         float* od = e->out_dist.as<float>() + off;
-        if (n_c > 0) {
-            if (path == FRNN_PATH_GRID)
-                st = search_built(e, P, H.principal != 0, K, r2, q0, q1, false, oi, od);
-            else if (path == FRNN_PATH_BRUTE_TC)
-                st = tc_query_tiles(e, pts, N, dim, K, radius, oi, od, q0 / 128, (q1 + 127) / 128);
-            else {
-                FRNN_CHECK(e, launch_bruteforce(pts, N, dim, K, r2, q0, q1, oi, od, n_c, s), "bruteforce launch");
-                e->launches++;
-            }
-            if (st != FRNN_OK) return st;
-        }
+        st = search_range(sh, H, pts, c0, c1, oi, od);
+        if (st != FRNN_OK) return st;
         FRNN_CHECK(e, cudaEventRecord(sh->chunk_ev[c], s), "chunk event");
         FRNN_CHECK(e, cudaStreamWaitEvent(sh->cs, sh->chunk_ev[c], 0), "chunk wait");
-        if (is_root) {
-            // chunk c of every other rank's slice, then this rank's own
-            SH_NCCL(sh, api->GroupStart(), "group start");
-            for (int r = 0; r < parts; ++r) {
-                int rc[kMaxChunks + 1];
-                const int mr = chunk_bounds(H.bounds[r], H.bounds[r + 1], path, sh->chunks, rc);
-                if (r == root || c >= mr || rc[c + 1] == rc[c]) continue;
-                const size_t o = (size_t)K * rc[c], cnt = (size_t)K * (rc[c + 1] - rc[c]);
-                SH_NCCL(sh, api->Recv(sh->st_idx.as<int>() + o, cnt, ncclInt32, r, sh->comm, sh->cs), "idx receive");
-                SH_NCCL(sh, api->Recv(sh->st_dist.as<float>() + o, cnt, ncclFloat32, r, sh->comm, sh->cs),
-                        "dist receive");
-                sh->gather_bytes += (long long)cnt * 8;
-            }
-            SH_NCCL(sh, api->GroupEnd(), "group end");
-            for (int r = 0; r < parts; ++r) {
-                int rc[kMaxChunks + 1];
-                const int mr = chunk_bounds(H.bounds[r], H.bounds[r + 1], path, sh->chunks, rc);
-                if (c >= mr) continue;
-                const int n_rc = rc[c + 1] - rc[c];
-                const int* si = r == root ? oi : sh->st_idx.as<int>() + (size_t)K * rc[c];
-                const float* sd = r == root ? od : sh->st_dist.as<float>() + (size_t)K * rc[c];
-                FRNN_CHECK(e, launch_shard_scatter(si, sd, rc[c], n_rc, K, scatter_ids, N, sh->res_idx.as<int>(),
-                                                   sh->res_dist.as<float>(), sh->cs),
-                           "scatter launch");
-                if (n_rc > 0) e->launches++;
-            }
-        } else if (n_c > 0) {
-            const size_t cnt = (size_t)K * n_c;
-            SH_NCCL(sh, api->GroupStart(), "group start");
-            SH_NCCL(sh, api->Send(oi, cnt, ncclInt32, root, sh->comm, sh->cs), "idx send");
-            SH_NCCL(sh, api->Send(od, cnt, ncclFloat32, root, sh->comm, sh->cs), "dist send");
-            SH_NCCL(sh, api->GroupEnd(), "group end");
-            sh->gather_bytes += (long long)cnt * 8;
-        }
+        // [K, n_c] -> columns [c0, c1) of the root's [K, N] results
+        FRNN_CHECK(e, cudaMemcpy2DAsync(dst_idx + c0, (size_t)N * 4, oi, (size_t)n_c * 4, (size_t)n_c * 4, (size_t)K,
+                                        cudaMemcpyDeviceToDevice, sh->cs),
+                   "result copy");
+        FRNN_CHECK(e, cudaMemcpy2DAsync(dst_dist + c0, (size_t)N * 4, od, (size_t)n_c * 4, (size_t)n_c * 4, (size_t)K,
+                                        cudaMemcpyDeviceToDevice, sh->cs),
+                   "result copy");
+        if (!is_root) sh->gather_bytes += (long long)n_c * K * 8;
     }
-    if (is_root) {
-        // chunks of other slices beyond this rank's own chunk count
-        int mmax = m;
-        for (int r = 0; r < parts; ++r) {
-            int rc[kMaxChunks + 1];
-            mmax = std::max(mmax, chunk_bounds(H.bounds[r], H.bounds[r + 1], path, sh->chunks, rc));
-        }
-        for (int c = m; c < mmax; ++c) {
-            SH_NCCL(sh, api->GroupStart(), "group start");
-            for (int r = 0; r < parts; ++r) {
-                int rc[kMaxChunks + 1];
-                const int mr = chunk_bounds(H.bounds[r], H.bounds[r + 1], path, sh->chunks, rc);
-                if (r == root || c >= mr || rc[c + 1] == rc[c]) continue;
-                const size_t o = (size_t)K * rc[c], cnt = (size_t)K * (rc[c + 1] - rc[c]);
-                SH_NCCL(sh, api->Recv(sh->st_idx.as<int>() + o, cnt, ncclInt32, r, sh->comm, sh->cs), "idx receive");
-                SH_NCCL(sh, api->Recv(sh->st_dist.as<float>() + o, cnt, ncclFloat32, r, sh->comm, sh->cs),
-                        "dist receive");
-                sh->gather_bytes += (long long)cnt * 8;
-            }
-            SH_NCCL(sh, api->GroupEnd(), "group end");
-            for (int r = 0; r < parts; ++r) {
-                int rc[kMaxChunks + 1];
-                const int mr = chunk_bounds(H.bounds[r], H.bounds[r + 1], path, sh->chunks, rc);
-                if (r == root || c >= mr) continue;
-                FRNN_CHECK(e, launch_shard_scatter(sh->st_idx.as<int>() + (size_t)K * rc[c],
-                                                   sh->st_dist.as<float>() + (size_t)K * rc[c], rc[c],
-                                                   rc[c + 1] - rc[c], K, scatter_ids, N, sh->res_idx.as<int>(),
-                                                   sh->res_dist.as<float>(), sh->cs),
-                           "scatter launch");
-                e->launches++;
-            }
-        }
-    }
-    sh_end(sh, SH_SEARCH);
-    if (is_root && sh->e->timing) {
-        cudaEventRecord(sh->ev[2 * SH_GATHER + 1], sh->cs);
-        sh->ev_used[SH_GATHER] = true;
-    }
-    // the engine stream waits for the communication stream's work
+    sh_end(sh, SH_SEARCH, s);
+    sh_end(sh, SH_GATHER, sh->cs);
+    // every rank's copies precede its part of one last all-reduce, so the
+    // root's all-reduce completes only when every block has landed
     FRNN_CHECK(e, cudaEventRecord(sh->comm_done, sh->cs), "comm event");
     FRNN_CHECK(e, cudaStreamWaitEvent(s, sh->comm_done, 0), "comm wait");
+    SH_NCCL(sh, api->AllReduce(sh->d_stat.p, sh->d_stat.p, 1, ncclInt32, ncclMax, sh->comm, s), "completion");
+    if (is_root)
+        for (int r = 0; r < parts; ++r)
+            if (r != root) sh->gather_bytes += (long long)(H.bounds[r + 1] - H.bounds[r]) * K * 8;
     FRNN_CHECK(e, cudaMemcpyAsync(sh->h_stat + 2, e->err_flag.p, sizeof(int), cudaMemcpyDeviceToHost, s),
                "error flag readback");
     st = wait_stream(sh, "sharded search");
