@@ -520,8 +520,10 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
                  "synthetic (seeded generator, seed 1234; rank r draws replica r of the same distribution)"),
         "config": config_dict(c, N, r, K),
         "parallelism": (f"one cloud, queries sharded over {world} ranks by the engine's NCCL path: "
-                        f"rank 0 builds once, broadcasts the built structure, every rank searches a "
-                        f"work-balanced slice, slices gathered to rank 0 -- all in every step") if strong
+                        f"rank 0 builds once and broadcasts the built structure, every rank searches "
+                        f"a work-balanced range of original query indices, and the copy engines move "
+                        f"each range's results into rank 0's buffers over NVLink -- all in every "
+                        f"step") if strong
                        else f"independent clouds x{world}",
         "queries_per_gpu": N // world if strong else N,
         "shard_options": {"chunks": a.shard_chunks, "comm_priority": a.shard_comm_priority} if strong else None,
@@ -537,8 +539,8 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
     if shard_ranks:
         # per rank: device ms of each protocol stage and the bytes it moved;
         # the limiting collective is the slower of the broadcast and the gather
-        # (the gather overlaps the search: its time is from the first receive
-        # to the last scatter on rank 0's communication stream)
+        # (the gather's time runs from the start of the rank's search to the
+        # end of its last copy into rank 0's buffers)
         root = shard_ranks[0]["stage_ms"]
         coll = {k: root.get(k, 0.0) for k in ("broadcast", "gather")}
         line["shard"] = {"ranks": shard_ranks, "limiting_collective": max(coll, key=coll.get),

@@ -401,6 +401,9 @@ int search_range(frnn_shard* sh, const ShardHeader& H, const float* pts, int lo,
         FRNN_GROW(e, e->n_overflow, 16);
         FRNN_CHECK(e, cudaMemsetAsync(e->n_overflow.p, 0, 4, s), "memset overflow count");
         const bool d3 = P.dim == 3 && P.g == 3 && !H.principal;
+        // engine stages as in a single-GPU search (with several chunks the
+        // last chunk's times remain)
+        stage_begin(e, ST_COLLECT);
         if (d3)
             FRNN_CHECK(e, launch_collect_d3(e->rows.as<float>(), e->starts.as<int>(), P, r2, cap,
                                             e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
@@ -412,6 +415,8 @@ int search_range(frnn_shard* sh, const ShardHeader& H, const float* pts, int lo,
                                             e->overflow.as<int>(), e->n_overflow.as<int>(), 0, rows, s, nullptr,
                                             proj_s, qlist),
                        "collect launch");
+        stage_end(e, ST_COLLECT);
+        stage_begin(e, ST_EMIT);
         // output row q - lo reads sorted position inv[q]
         FRNN_CHECK(e, launch_emit_lists(e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
                                         sh->inv.as<int>() + lo, 0, rows, K, cap, r2, oi, od, s, N),
@@ -419,12 +424,15 @@ int search_range(frnn_shard* sh, const ShardHeader& H, const float* pts, int lo,
         FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), ids, e->starts.as<int>(), P, K, r2, 0, N, oi, od, rows,
                                          ids, s, e->overflow.as<int>(), e->n_overflow.as<int>(), lo, proj_s),
                    "overflow search launch");
+        stage_end(e, ST_EMIT);
         e->launches += 3;
         return FRNN_OK;
     }
+    stage_begin(e, ST_SEARCH);
     FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), ids, e->starts.as<int>(), P, K, r2, 0, rows, oi, od, rows,
                                      ids, s, qlist, nullptr, lo, proj_s),
                "grid search launch");
+    stage_end(e, ST_SEARCH);
     e->launches++;
     return FRNN_OK;
 }
