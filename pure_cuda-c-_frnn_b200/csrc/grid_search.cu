@@ -14,6 +14,7 @@
 #include "frnn_device.cuh"
 #include "frnn_internal.h"
 #include "grid_coop.cuh"
+#include "grid_prj.cuh"
 
 namespace frnn {
 namespace {
@@ -94,6 +95,23 @@ cudaError_t launch_coop(const CoopArgs& a, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+// Principal-axis grids: the pair-queue kernel (grid_prj.cuh).
+template <int NV, int G>
+cudaError_t launch_prj(const CoopArgs& a, cudaStream_t s) {
+    constexpr int GR = coop::kGroupPrj;
+    const size_t smem = (size_t)coop::kWarps * coop::prj_warp_bytes<NV, GR>(a.K);
+    cudaError_t err = set_smem(coop::grid_prj_kernel<NV, G, GR>, smem);
+    if (err != cudaSuccess) return err;
+    const int per_block = coop::kWarps * 32;
+    const int blocks = (a.q1 - a.q0 + per_block - 1) / per_block;
+    coop::grid_prj_kernel<NV, G, GR><<<blocks, coop::kWarps * 32, smem, s>>>(
+        reinterpret_cast<const float4*>(a.rows), a.ids, a.starts, a.P, a.K, a.r2, a.q0, a.q1, a.oidx,
+        a.odist, a.ostride, a.scatter_ids, a.qlist, a.qcount, a.row_base,
+        reinterpret_cast<const float4*>(a.proj), reinterpret_cast<const float4*>(a.qrows ? a.qrows : a.rows),
+        reinterpret_cast<const float4*>(a.qrows ? a.qproj : a.proj));
+    return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_grid_search(const float* rows, const int* ids, const int* starts,
@@ -120,11 +138,11 @@ cudaError_t launch_grid_search(const float* rows, const int* ids, const int* sta
     // (P.pre_r2 > 0); leading coordinates: G = 4
 #define FRNN_COOP_G(NV)                                                   \
     switch (P.g) {                                                        \
-        case 2: return launch_coop<NV, 2, false, true>(a, s);             \
-        case 3: return launch_coop<NV, 3, false, true>(a, s);             \
-        case 4: return launch_coop<NV, 4, false, true>(a, s);             \
-        case 5: return launch_coop<NV, 5, false, true>(a, s);             \
-        case 6: return launch_coop<NV, 6, false, true>(a, s);             \
+        case 2: return launch_prj<NV, 2>(a, s);                           \
+        case 3: return launch_prj<NV, 3>(a, s);                           \
+        case 4: return launch_prj<NV, 4>(a, s);                           \
+        case 5: return launch_prj<NV, 5>(a, s);                           \
+        case 6: return launch_prj<NV, 6>(a, s);                           \
         default: return cudaErrorInvalidValue;                            \
     }
     if (!proj) {
