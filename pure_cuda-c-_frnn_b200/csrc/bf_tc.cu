@@ -73,12 +73,6 @@ constexpr int kThreads = (kEpiWarps + 2) * 32;
 constexpr int kProducerWarp = kEpiWarps;
 constexpr int kMmaWarp = kEpiWarps + 1;
 constexpr int kTmemCols = 512;        // 2 query blocks x 2 buffers x 128 columns
-// CTA pairs (tcgen05.mma.cta_group::2, filter_pair_kernel) or single CTAs
-// (filter_kernel).  Build-time knob.
-#ifndef FRNN_TC_CTA_PAIR
-#define FRNN_TC_CTA_PAIR 0
-#endif
-constexpr bool kCtaPair = FRNN_TC_CTA_PAIR != 0;
 constexpr uint32_t kWaitPolls = 1u << 26;
 constexpr unsigned long long kWaitNs = 2000000000ull;
 
@@ -578,349 +572,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-// ---- filter on CTA pairs ----------------------------------------------------
-//
-// The same filter with tcgen05.mma.cta_group::2: a cluster of two CTAs, each
-// holding one 128-query block (A) and one 128-point half of a 256-point step
-// (B) in its own shared memory.  The even CTA issues one M = 256 x N = 256
-// MMA per 16-dimension slice; each CTA's TMEM receives its 128 queries x 256
-// points.  Per SM this reads 8 KB of shared memory per 128 x 256 x 16
-// product, against 8 KB per 128 x 128 x 16 for the single-CTA kernel, and
-// each point tile is copied once per 256 queries as before.
-//
-// Synchronisation across the pair (all waits bounded as above):
-//   * each CTA's producer copies its own A block and B halves and waits on its
-//     own barriers; the odd CTA's otherwise idle MMA warp relays "A landed"
-//     and "stage s landed" to the even CTA's pafull / pfull(s) barriers;
-//   * the even CTA's MMA thread commits each step to empty(s) and tfull(b)
-//     in both CTAs (two commits, one to the peer's barrier address);
-//   * every epilogue warp of both CTAs arrives on the even CTA's tempty(b);
-//   * a give-up sets both CTAs' abort flags;
-//   * before TMEM is released, both CTAs wait for every commit addressed to
-//     them and meet at a cluster barrier.
-constexpr uint32_t kIdescPair = (1u << 4) | ((uint32_t)(256 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
-
-template <int KC>
-struct PairCfg {
-    static constexpr int kStages = KC == 2 ? 5 : 10;
-    static constexpr uint32_t kTileBytes = KC * kAtomBytes;
-    static constexpr size_t kBarOffset = (size_t)(1 + kStages) * kTileBytes;
-    // full[S], empty[S], pfull[S], tfull[2], tempty[2], afull, pafull, done
-    static constexpr int kBars = 3 * kStages + 7;
-    static constexpr size_t kSmem = 1024 /* alignment slack */ + kBarOffset + kBars * 8 +
-                                    16 /* tmem slot, abort */ + kRows * 4 /* per-query counters */ +
-                                    16 + kEpiWarps * kRows * 4 /* point terms */;
-};
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ uint32_t cluster_index() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-    return r;
-}
-// the shared::cluster address of this CTA's shared-memory address `a` in CTA `rank`
-__device__ __forceinline__ uint32_t map_to(uint32_t a, uint32_t rank) {
-    uint32_t d;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(rank));
-    return d;
-}
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait_cl(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Bounded wait with cluster-scope acquire (barriers the other CTA arrives on).
-__device__ __noinline__ bool mbar_wait_cl(uint32_t bar, uint32_t parity, const volatile int* abort) {
-    if (mbar_try_wait_cl(bar, parity)) return true;
-    const unsigned long long t0 = global_ns();
-    for (uint32_t i = 1; i < kWaitPolls; ++i) {
-        if (mbar_try_wait_cl(bar, parity)) return true;
-        if ((i & 255u) == 0) {
-            if (*abort) return false;
-            if (global_ns() - t0 > kWaitNs) return false;
-        }
-    }
-    return false;
-}
-// Bounded wait against a shared deadline (drains at exit).
-__device__ __noinline__ void drain_until(uint32_t bar, uint32_t parity, unsigned long long t_end) {
-    for (uint32_t i = 0; i < kWaitPolls; ++i) {
-        if (mbar_try_wait_cl(bar, parity)) return;
-        if ((i & 255u) == 255u && global_ns() > t_end) return;
-    }
-}
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(kIdescPair), "r"(acc)
-        : "memory");
-}
-// arrive (once) on the barrier at shared::cluster address `bar` when every
-// MMA this thread issued before has completed
-__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-                 : "memory");
-}
-
-template <int KC>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    filter_pair_kernel(const uint8_t* __restrict__ tiles, const float* __restrict__ qa,
-                       const float* __restrict__ pb, int n, int ntiles, int cap, int* __restrict__ lists,
-                       int* __restrict__ counts, int* __restrict__ overflow, int* __restrict__ n_overflow,
-                       int* __restrict__ err, int qb_begin, int qb_end, const uint8_t* __restrict__ qtiles,
-                       int skip_tile) {
-    static_assert(kEpiWarps == 16, "the pair kernel's epilogue is two groups of 8 warps");
-    using C = PairCfg<KC>;
-    constexpr int S = C::kStages;
-    constexpr uint32_t TB = C::kTileBytes;
-    constexpr int kChunks = 4;  // 32-column chunks per epilogue warp and step
-    extern __shared__ uint8_t smem_raw[];
-    // the same offsets in both CTAs: the MMA addresses the odd CTA's operands
-    // through the even CTA's descriptors
-    const uint32_t raw_addr = smem_u32(smem_raw);
-    uint8_t* base = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
-    const uint32_t sA = smem_u32(base);
-    const uint32_t sB = sA + TB;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(base + C::kBarOffset);
-    const uint32_t bar0 = smem_u32(bars);
-    auto full = [&](int s) { return bar0 + 8u * s; };
-    auto empty = [&](int s) { return bar0 + 8u * (S + s); };
-    auto pfull = [&](int s) { return bar0 + 8u * (2 * S + s); };
-    auto tfull = [&](int b) { return bar0 + 8u * (3 * S + b); };
-    auto tempty = [&](int b) { return bar0 + 8u * (3 * S + 2 + b); };
-    const uint32_t afull = bar0 + 8u * (3 * S + 4);
-    const uint32_t pafull = bar0 + 8u * (3 * S + 5);
-    const uint32_t done = bar0 + 8u * (3 * S + 6);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kBars);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    int* qcnt = reinterpret_cast<int*>(tmem_slot + 4);
-    // [kEpiWarps][kRows], 16-byte aligned (read as float4)
-    float* pbstage = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(qcnt + kRows) + 15) & ~uintptr_t(15));
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t rank = cluster_rank();
-    const bool even = rank == 0;
-    const uint32_t other = rank ^ 1u;
-    // this CTA's query block (a valid block is loaded in its place past the
-    // end; its rows are never reported) and the steps: step u covers point
-    // tiles 2u (even CTA) and 2u + 1 (odd CTA)
-    const int qb = qb_begin + 2 * (int)cluster_index() + (int)rank;
-    const bool qvalid = qb < qb_end;
-    const int qbl = qvalid ? qb : qb_end - 1;
-    const int nsteps = (ntiles + 1) / 2;
-
-    if (threadIdx.x < kRows) qcnt[threadIdx.x] = 0;
-    if (threadIdx.x == 0) {
-        *abort_flag = 0;
-        for (int s = 0; s < S; ++s) {
-            mbar_init(full(s), 1);
-            mbar_init(empty(s), 1);
-            mbar_init(pfull(s), 1);
-        }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(tfull(b), 1);
-            mbar_init(tempty(b), kEpiWarps);  // both CTAs' warps of the group
-        }
-        mbar_init(afull, 1);
-        mbar_init(pafull, 1);
-        mbar_init(done, 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    if (warp == kProducerWarp) {
-        // one warp of each CTA, the same warp in both, allocates the pair's columns
-        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                         smem_u32(tmem_slot)),
-                     "r"(kTmemCols)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-    }
-    fence_before();
-    __syncthreads();
-    // both CTAs' barriers exist before either addresses the other's
-    cluster_sync_all();
-    fence_after();
-    const uint32_t tmem = *tmem_slot;
-    const uint32_t other_abort = map_to(smem_u32((const void*)abort_flag), other);
-
-    auto give_up = [&]() {
-        *abort_flag = 1;
-        asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(other_abort), "r"(1) : "memory");
-        atomicExch(err, 1);
-    };
-
-    if (warp == kProducerWarp) {
-        if (lane == 0) {
-            mbar_expect_tx(afull, TB);
-            bulk_g2s(sA, qtiles + (size_t)qbl * TB, TB, afull);
-            int issued = 0;
-            for (int u = 0; u < nsteps; ++u) {
-                const int s = u % S;
-                if (!mbar_wait_cl(empty(s), ((uint32_t)(u / S) & 1u) ^ 1u, abort_flag)) {
-                    give_up();
-                    break;
-                }
-                const int t = 2 * u + (int)rank;
-                // past the last tile (odd tile count) a real tile fills the
-                // half; its columns are never read
-                const int tl = t < ntiles ? t : ntiles - 1;
-                // skip_tile (tests of the timeout path only): this half is
-                // never filled, so the waits for it give up
-                if (t != skip_tile) {
-                    mbar_expect_tx(full(s), TB);
-                    bulk_g2s(sB + (uint32_t)s * TB, tiles + (size_t)tl * TB, TB, full(s));
-                }
-                issued = u + 1;
-            }
-            // before the CTA exits: its copies have landed and every MMA
-            // commit addressed to its empty barriers has arrived
-            const unsigned long long t_end = global_ns() + kWaitNs;
-            drain_until(afull, 0, t_end);
-            for (int u = issued - S < 0 ? 0 : issued - S; u < issued; ++u) {
-                if (2 * u + (int)rank != skip_tile) drain_until(full(u % S), (uint32_t)(u / S) & 1u, t_end);
-                drain_until(empty(u % S), (uint32_t)(u / S) & 1u, t_end);
-            }
-        }
-    } else if (warp == kMmaWarp) {
-        if (lane == 0 && !even) {
-            // odd CTA: relay "A landed" and "stage landed" to the even CTA
-            if (mbar_wait(afull, 0, abort_flag)) {
-                mbar_arrive_cluster(map_to(pafull, 0));
-                for (int u = 0; u < nsteps; ++u) {
-                    if (!mbar_wait(full(u % S), (uint32_t)(u / S) & 1u, abort_flag)) {
-                        give_up();
-                        break;
-                    }
-                    mbar_arrive_cluster(map_to(pfull(u % S), 0));
-                }
-            } else {
-                give_up();
-            }
-        } else if (lane == 0) {
-            bool ok = mbar_wait(afull, 0, abort_flag) && mbar_wait_cl(pafull, 0, abort_flag);
-            if (!ok) give_up();
-            int committed = 0;
-            for (int u = 0; ok && u < nsteps; ++u) {
-                const int s = u % S, b = u & 1;
-                const uint32_t ph = (uint32_t)(u / S) & 1u, v = (uint32_t)(u >> 1);
-                if (!mbar_wait(full(s), ph, abort_flag) || !mbar_wait_cl(pfull(s), ph, abort_flag) ||
-                    !mbar_wait_cl(tempty(b), (v & 1u) ^ 1u, abort_flag)) {
-                    give_up();
-                    break;
-                }
-                fence_after();
-                const uint32_t bstage = sB + (uint32_t)s * TB;
-                const uint32_t d = tmem + (uint32_t)(b * 256);
-#pragma unroll
-                for (int k = 0; k < 4 * KC; ++k) {
-                    const uint32_t off = (uint32_t)((k >> 2) * kAtomBytes + (k & 3) * 32);
-                    mma_f16_pair(d, sw128_desc(sA + off), sw128_desc(bstage + off), k > 0 ? 1u : 0u);
-                }
-                mma_commit_pair(empty(s));
-                mma_commit_pair(map_to(empty(s), 1));
-                mma_commit_pair(tfull(b));
-                mma_commit_pair(map_to(tfull(b), 1));
-                committed = u + 1;
-            }
-            (void)committed;
-            // every MMA issued above completes before TMEM is released
-            mma_commit_pair(done);
-            drain_wait(done, 0);
-        }
-    } else {
-        // epilogue: group g takes the steps u = g (mod 2), TMEM buffer g; a
-        // warp reads the TMEM lanes of its subpartition and the 128 columns
-        // of half h (point tile 2u + h)
-        const int sp = warp & 3, g = (warp >> 2) & 1, h = warp >> 3;
-        const int row = sp * 32 + lane;
-        const float aq = qvalid ? __ldg(&qa[(size_t)qbl * kRows + row]) : __int_as_float(0x7f800000);
-        const int q = qbl * kRows + row;
-        const uint32_t lane_base = (uint32_t)(sp * 32) << 16;
-        const uint32_t release = map_to(tempty(g), 0);
-        // the point-side terms of this warp's 128 columns: loaded one step
-        // ahead into registers, staged in shared memory for the step being
-        // filtered
-        float* spb = pbstage + warp * kRows;
-        auto load_terms = [&](int u) {
-            const int t = 2 * u + h;
-            return u < nsteps && t < ntiles ? __ldg(reinterpret_cast<const float4*>(pb + (size_t)t * kRows) + lane)
-                                            : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        };
-        float4 terms = load_terms(g);
-        for (int u = g; u < nsteps; u += 2) {
-            const uint32_t v = (uint32_t)(u >> 1);
-            if (!__all_sync(0xffffffffu, mbar_wait_cl(tfull(g), v & 1u, abort_flag))) {
-                if (lane == 0) give_up();
-                break;
-            }
-            fence_after();
-            __syncwarp();
-            reinterpret_cast<float4*>(spb)[lane] = terms;
-            __syncwarp();
-            terms = load_terms(u + 2);
-            const int t = 2 * u + h;
-            if (t < ntiles) {
-#pragma unroll 1
-                for (int c = 0; c < kChunks; ++c) {
-                    float bq[32];
-                    const float4* b4 = reinterpret_cast<const float4*>(spb + c * 32);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const float4 bb = b4[i];
-                        bq[4 * i] = bb.x;
-                        bq[4 * i + 1] = bb.y;
-                        bq[4 * i + 2] = bb.z;
-                        bq[4 * i + 3] = bb.w;
-                    }
-                    uint32_t acc[32];
-                    __syncwarp();
-                    tmem_ld32(tmem + lane_base + (uint32_t)(g * 256 + h * kRows + c * 32), acc);
-                    tmem_wait_ld();
-                    filter_chunk(acc, bq, aq, &qcnt[row], lists, q, cap, t * kRows + c * 32);
-                }
-            }
-            fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(release);
-        }
-    }
-
-    fence_before();
-    __syncthreads();
-    if (threadIdx.x < kRows && qvalid) {
-        const int qq = qb * kRows + threadIdx.x;
-        if (qq < n) {
-            const int c = qcnt[threadIdx.x];
-            counts[qq] = c;
-            if (c > cap) overflow[atomicAdd(n_overflow, 1)] = qq;
-        }
-    }
-    // the other CTA is done with this CTA's shared memory and TMEM
-    cluster_sync_all();
-    if (warp == kProducerWarp) {
-        fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
-                     : "memory");
-    }
-}
-
 // ---- exact re-rank ----------------------------------------------------------
 
 constexpr int kRerankWarps = 8;
@@ -1005,17 +656,6 @@ template <int KC>
 cudaError_t launch_filter_kc(const uint8_t* tiles, const float* qa, const float* pb, int n, int ntiles,
                              int cap, int* lists, int* counts, int* overflow, int* n_overflow, int* err,
                              int qb_begin, int qb_end, cudaStream_t s, const uint8_t* qtiles, int skip_tile) {
-    if (kCtaPair) {
-        const size_t smem = PairCfg<KC>::kSmem;
-        cudaError_t e = cudaFuncSetAttribute(filter_pair_kernel<KC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
-        if (e != cudaSuccess) return e;
-        if (qb_end <= qb_begin) return cudaSuccess;
-        filter_pair_kernel<KC><<<2 * ((qb_end - qb_begin + 1) / 2), kThreads, smem, s>>>(
-            tiles, qa, pb, n, ntiles, cap, lists, counts, overflow, n_overflow, err, qb_begin, qb_end, qtiles,
-            skip_tile);
-        return cudaGetLastError();
-    }
     const size_t smem = Cfg<KC>::kSmem;
     cudaError_t e =
         cudaFuncSetAttribute(filter_kernel<KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

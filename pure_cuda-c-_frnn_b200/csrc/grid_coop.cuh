@@ -28,20 +28,19 @@ namespace coop {
 
 constexpr int kWarps = 4;    // warps per block
 constexpr int kGroup = 8;    // queries per group
-// Queries per group on principal-axis grids, where a cell rarely holds more
-// than one query (fewer group slots keep the screening loop in registers).
-// Build-time launch-policy knob.
+// Queries per group of the principal-axis search (grid_prj.cuh).  Build-time
+// launch-policy knob.
 #ifndef FRNN_COOP_PRJ_GROUP
 #define FRNN_COOP_PRJ_GROUP 8
 #endif
 constexpr int kGroupPrj = FRNN_COOP_PRJ_GROUP;
-static_assert(kGroupPrj >= 1 && kGroupPrj <= 8, "group slots fit the 8-bit candidate masks");
+static_assert(kGroupPrj >= 1 && kGroupPrj <= 8, "group slots fit the 8-bit pair masks");
 
 // Launch policy: minimum resident blocks per SM (which caps registers per
 // thread) for the D = 3 kernel and for the wider-row kernels; build-time
 // knobs like the reference's FRNN_GRID_*_MIN_BLOCKS cache variables
-// (CMakeLists.txt:17-22).  Defaults measured on B200 (cfg1/cfg2 for D = 3,
-// cfg3/cfg4 for the others).
+// (CMakeLists.txt:17-22); PRJ: the principal-axis search (grid_prj.cuh).
+// Defaults measured on B200 (cfg1/cfg2 for D = 3, cfg3/cfg4 for the others).
 #ifndef FRNN_COOP_D3_MIN_BLOCKS
 #define FRNN_COOP_D3_MIN_BLOCKS 6
 #endif
@@ -49,7 +48,7 @@ static_assert(kGroupPrj >= 1 && kGroupPrj <= 8, "group slots fit the 8-bit candi
 #define FRNN_COOP_ND_MIN_BLOCKS 4
 #endif
 #ifndef FRNN_COOP_PRJ_MIN_BLOCKS
-#define FRNN_COOP_PRJ_MIN_BLOCKS 4
+#define FRNN_COOP_PRJ_MIN_BLOCKS 5
 #endif
 
 // List capacity for K: room for a whole chunk of acceptances (32) on top of K,
@@ -57,11 +56,10 @@ static_assert(kGroupPrj >= 1 && kGroupPrj <= 8, "group slots fit the 8-bit candi
 __host__ __device__ constexpr int list_cap(int K) { return K <= 32 ? 64 : (K <= 96 ? 128 : 256); }
 
 // Per-warp shared memory: the group's query rows, its 64-bit acceptance
-// bounds, the group's projected query coordinates (principal-axis grids),
-// then the group's candidate lists.
+// bounds, then the group's candidate lists.
 template <int NV, bool D3, int GR = kGroup>
 __host__ __device__ constexpr size_t rows_bytes() {
-    return (size_t)GR * NV * 16 + (size_t)GR * 8 + (size_t)GR * kProjStride * 4;
+    return (size_t)GR * NV * 16 + (size_t)GR * 8;
 }
 template <int NV, bool D3, int GR = kGroup>
 __host__ __device__ constexpr size_t warp_bytes(int K) {
@@ -229,29 +227,22 @@ struct Shell<1> {
     static constexpr int rows = 1;
 };
 
-// NV float4 per sorted row; G grid axes; D3: rows are (x, y, z, index bits)
-// and the index comes from .w, otherwise from ids[].  PRJ: the grid is on
-// principal axes and every candidate is first tested on its projected
-// coordinates: a pair whose projected squared distance exceeds P.pre_r2 (the
-// radius widened by the projections' rounding bound) cannot be within r in
-// the full dimension, because projection onto orthonormal axes never
-// lengthens a distance -- so only candidates that pass load their full row.
+// NV float4 per sorted row; G grid axes (the leading coordinates); D3: rows
+// are (x, y, z, index bits) and the index comes from .w, otherwise from
+// ids[].  Grids on principal axes use grid_prj_kernel (grid_prj.cuh).
 //
 // Group state (query rows, bounds, list lengths) is warp-uniform and lives in
 // registers of every lane; the group loop is unrolled over GR slots.
-template <int NV, int G, bool D3, bool PRJ, int GR = kGroup>
-__global__ void __launch_bounds__(kWarps * 32, D3    ? FRNN_COOP_D3_MIN_BLOCKS
-                                               : PRJ ? FRNN_COOP_PRJ_MIN_BLOCKS
-                                                     : FRNN_COOP_ND_MIN_BLOCKS)
+template <int NV, int G, bool D3, int GR = kGroup>
+__global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FRNN_COOP_ND_MIN_BLOCKS)
     grid_coop_kernel(const float4* __restrict__ rows, const int* __restrict__ ids,
                      const int* __restrict__ starts, GridPlan P, int K, float r2, int q0, int q1,
                      int* __restrict__ oidx, float* __restrict__ odist, long long ostride,
                      const int* __restrict__ scatter_ids, const int* __restrict__ qlist,
                      const int* __restrict__ qcount, long long row_base,
-                     const float4* __restrict__ proj, const float4* __restrict__ queries,
-                     const float4* __restrict__ qproj) {
-    // queries / qproj: the queries' rows and projected coordinates (a
-    // separate query set in the same grid's cell order, or the points' own)
+                     const float4* __restrict__ queries) {
+    // queries: the queries' rows (a separate query set in the same grid's
+    // cell order, or the points' own)
     extern __shared__ __align__(16) unsigned char smem[];
     if (qcount) q1 = min(q1, q0 + __ldg(qcount));  // list length known only on the device
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -260,7 +251,6 @@ __global__ void __launch_bounds__(kWarps * 32, D3    ? FRNN_COOP_D3_MIN_BLOCKS
     float4* qrows = reinterpret_cast<float4*>(wbase);  // [GR][NV]
     unsigned long long* gthr =
         reinterpret_cast<unsigned long long*>(wbase + (size_t)GR * NV * 16);  // [GR]
-    float4* qprj = reinterpret_cast<float4*>(wbase + (size_t)GR * NV * 16 + (size_t)GR * 8);
     unsigned long long* lists = reinterpret_cast<unsigned long long*>(wbase + rows_bytes<NV, D3, GR>());
 
     const int base = q0 + (blockIdx.x * kWarps + warp) * 32;
@@ -277,12 +267,11 @@ __global__ void __launch_bounds__(kWarps * 32, D3    ? FRNN_COOP_D3_MIN_BLOCKS
     for (int v = 0; v < NV; ++v)
         myq[v] = lane < nq ? __ldg(&queries[mysq * NV + v]) : make_float4(0, 0, 0, 0);
     {
-        // grid coordinates: the leading coordinates of the row, or the
-        // query's projected (principal-axis) coordinates
+        // grid coordinates: the leading coordinates of the row
         long long c = 0;
 #pragma unroll
         for (int a = 0; a < G; ++a) {
-            const float4 f = qproj ? __ldg(&qproj[mysq * (kProjStride / 4) + (a >> 2)]) : myq[a >> 2];
+            const float4 f = myq[a >> 2];
             const float x = (a & 3) == 0 ? f.x : (a & 3) == 1 ? f.y : (a & 3) == 2 ? f.z : f.w;
             mygc[a] = cell_coord(x, P.origin[a], P.inv_cell, P.res[a]);
             c += (long long)mygc[a] * P.stride[a];
@@ -316,11 +305,6 @@ __global__ void __launch_bounds__(kWarps * 32, D3    ? FRNN_COOP_D3_MIN_BLOCKS
 #pragma unroll
                 for (int v = 0; v < NV; ++v) qrows[g * NV + v] = myq[v];
                 gthr[g] = make_key(r2, 0);
-                if constexpr (PRJ) {
-#pragma unroll
-                    for (int v = 0; v < kProjStride / 4; ++v)
-                        qprj[g * (kProjStride / 4) + v] = __ldg(&qproj[mysq * (kProjStride / 4) + v]);
-                }
             }
             __syncwarp();
         }
@@ -373,40 +357,11 @@ __global__ void __launch_bounds__(kWarps * 32, D3    ? FRNN_COOP_D3_MIN_BLOCKS
             const int js = __shfl_sync(0xffffffffu, sstart, k);
             const int je = __shfl_sync(0xffffffffu, excl, k);
             const int j = valid ? js + (t - je) : 0;
-            // PRJ: which group queries this candidate can be a neighbour of,
-            // from the projected coordinates alone (bit g)
-            unsigned near = valid ? (1u << GR) - 1u : 0u;
-            if constexpr (PRJ) {
-                near = 0u;
-                if (valid) {
-                    float4 pp[kProjStride / 4];
-#pragma unroll
-                    for (int v = 0; v < kProjStride / 4; ++v) pp[v] = __ldg(&proj[(long long)j * (kProjStride / 4) + v]);
-#pragma unroll
-                    for (int g = 0; g < GR; ++g) {
-                        if (g < gq) {
-                            float d2p = 0.0f;
-#pragma unroll
-                            for (int a = 0; a < G; ++a) {
-                                const float4 qv = qprj[g * (kProjStride / 4) + (a >> 2)];
-                                const float4 pv = pp[a >> 2];
-                                const float qa = (a & 3) == 0 ? qv.x : (a & 3) == 1 ? qv.y : (a & 3) == 2 ? qv.z : qv.w;
-                                const float pa = (a & 3) == 0 ? pv.x : (a & 3) == 1 ? pv.y : (a & 3) == 2 ? pv.z : pv.w;
-                                const float df = qa - pa;
-                                d2p = __fmaf_rn(df, df, d2p);
-                            }
-                            near |= (d2p <= P.pre_r2 ? 1u : 0u) << g;
-                        }
-                    }
-                }
-                // no lane's candidate is near any query of the group: next chunk
-                if (!__any_sync(0xffffffffu, near != 0u)) continue;
-            }
             float4 p[NV];
 #pragma unroll
             for (int v = 0; v < NV; ++v)
-                p[v] = near ? __ldg(&rows[(long long)j * NV + v]) : make_float4(0, 0, 0, 0);
-            const int pid = D3 ? __float_as_int(p[0].w) : (near ? __ldg(&ids[j]) : 0);
+                p[v] = valid ? __ldg(&rows[(long long)j * NV + v]) : make_float4(0, 0, 0, 0);
+            const int pid = D3 ? __float_as_int(p[0].w) : (valid ? __ldg(&ids[j]) : 0);
 
 #pragma unroll
             for (int g = 0; g < GR; ++g) {
@@ -418,7 +373,7 @@ __global__ void __launch_bounds__(kWarps * 32, D3    ? FRNN_COOP_D3_MIN_BLOCKS
                     } else {
                         d2 = chain_dist2<NV>(qrows + g * NV, p);
                     }
-                    const bool cand = valid && ((near >> g) & 1u);
+                    const bool cand = valid;
                     bool acc = cand && d2 < glim[g];
                     const bool tie = cand && d2 == glim[g];
                     if (__any_sync(0xffffffffu, tie)) acc |= tie && make_key(d2, pid) < gthr[g];

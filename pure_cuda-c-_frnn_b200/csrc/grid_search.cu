@@ -5,12 +5,15 @@
 //   FindNbrsNDKernel<CAP,DIM> :116-214  -> grid_coop_kernel<NV, G, false> (G = D <= 4)
 //   FindNbrsGridDimKernel     :243-353  -> grid_coop_kernel<NV, 4, false> (D > 4: grid on
 //                                          the first four coordinates, full-D ranking)
+//                                          or grid_prj_kernel<NV, G> (D > 4: grid on
+//                                          G principal axes, projected screening)
 //   ScatterToOrigKernel       :505-523  -> unpermute_kernel
 //
 // Every query visits the 3^G cell shell around its own cell; because axis 0
 // varies fastest in the dense cell index, the three axis-0 neighbours form one
 // contiguous span, so a shell is 3^(G-1) spans.  The search itself is the
-// warp-cooperative kernel of grid_coop.cuh.
+// warp-cooperative kernel of grid_coop.cuh, or on principal-axis grids the
+// pair-queue kernel of grid_prj.cuh.
 #include "frnn_device.cuh"
 #include "frnn_internal.h"
 #include "grid_coop.cuh"
@@ -79,19 +82,18 @@ struct CoopArgs {
     const float* qproj;
 };
 
-template <int NV, int G, bool D3, bool PRJ = false>
+template <int NV, int G, bool D3>
 cudaError_t launch_coop(const CoopArgs& a, cudaStream_t s) {
-    constexpr int GR = PRJ ? coop::kGroupPrj : coop::kGroup;
+    constexpr int GR = coop::kGroup;
     const size_t smem = (size_t)coop::kWarps * coop::warp_bytes<NV, D3, GR>(a.K);
-    cudaError_t err = set_smem(coop::grid_coop_kernel<NV, G, D3, PRJ, GR>, smem);
+    cudaError_t err = set_smem(coop::grid_coop_kernel<NV, G, D3, GR>, smem);
     if (err != cudaSuccess) return err;
     const int per_block = coop::kWarps * 32;
     const int blocks = (a.q1 - a.q0 + per_block - 1) / per_block;
-    coop::grid_coop_kernel<NV, G, D3, PRJ, GR><<<blocks, coop::kWarps * 32, smem, s>>>(
+    coop::grid_coop_kernel<NV, G, D3, GR><<<blocks, coop::kWarps * 32, smem, s>>>(
         reinterpret_cast<const float4*>(a.rows), a.ids, a.starts, a.P, a.K, a.r2, a.q0, a.q1, a.oidx,
         a.odist, a.ostride, a.scatter_ids, a.qlist, a.qcount, a.row_base,
-        reinterpret_cast<const float4*>(a.proj), reinterpret_cast<const float4*>(a.qrows ? a.qrows : a.rows),
-        reinterpret_cast<const float4*>(a.qrows ? a.qproj : a.proj));
+        reinterpret_cast<const float4*>(a.qrows ? a.qrows : a.rows));
     return cudaGetLastError();
 }
 
