@@ -198,7 +198,15 @@ enum frnn_option {
      * never copies one point tile, so the MMA thread's wait for it gives up
      * after 2 s.  Results of a stalled search are undefined; nothing is
      * written outside the engine's buffers.  Default OFF. */
-    FRNN_OPT_TEST_STALL = 4
+    FRNN_OPT_TEST_STALL = 4,
+    /* Blocking self-searches with D <= 4 on the grid (frnn_search_gpu and the
+     * host entry points): 1 (default) plans the grid on the GPU -- the
+     * bounding-box kernel runs the host planner's own code and every later
+     * kernel reads the plan from device memory, so no host round trip
+     * separates the box from the build and the search; 0 reads the box back
+     * and plans on the host, as the reference does (frnn_engine.cu:64-86,
+     * 142-156).  Results are the same either way.  No reference counterpart. */
+    FRNN_OPT_DEVICE_PLAN = 5
 };
 enum frnn_test_stall {
     FRNN_TEST_STALL_OFF = 0,

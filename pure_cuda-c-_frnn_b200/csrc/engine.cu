@@ -206,11 +206,13 @@ int grid_axes_for(int dim) { return dim <= 4 ? dim : 4; }
 // `cells_per_point` cells per point (at least 2^22): 12 bytes of build traffic
 // per cell, and sparse clouds such as Gaussian mixtures leave most cells
 // empty, while coarser cells would multiply the candidates of every query.
+long long cell_budget(int N, long long cells_per_point) {
+    return std::min<long long>(std::max<long long>(1LL << 22, cells_per_point * N), (1LL << 31) - 2);
+}
+
 bool make_plan_axes(const float* box, int g, int N, int dim, float radius, double extra, GridPlan& P,
                     long long cells_per_point = 32) {
-    const long long budget = std::min<long long>(std::max<long long>(1LL << 22, cells_per_point * N),
-                                                 (1LL << 31) - 2);
-    return plan_grid(box, g, N, dim, radius, extra, budget, P);
+    return plan_grid(box, g, N, dim, radius, extra, cell_budget(N, cells_per_point), P);
 }
 
 bool make_plan(const float* box, int N, int dim, float radius, GridPlan& P) {
@@ -491,7 +493,7 @@ int build_points(frnn_engine* e, const float* d_pts, const GridPlan& P, const fl
 }
 
 int search_built(frnn_engine* e, const GridPlan& P, bool principal, int K, float r2, int q0, int q1,
-                 bool whole, int* out_idx, float* out_dist) {
+                 bool whole, int* out_idx, float* out_dist, const GridPlan* Pd) {
     cudaStream_t s = e->stream;
     const int N = P.n;
     const float* proj_s = principal ? e->proj_s.as<float>() : nullptr;
@@ -513,24 +515,25 @@ int search_built(frnn_engine* e, const GridPlan& P, bool principal, int K, float
         if (d3)
             FRNN_CHECK(e, launch_collect_d3(e->rows.as<float>(), e->starts.as<int>(), P, r2, cap,
                                             e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
-                                            e->overflow.as<int>(), e->n_overflow.as<int>(), q0, q1, s),
+                                            e->overflow.as<int>(), e->n_overflow.as<int>(), q0, q1, s, nullptr,
+                                            nullptr, Pd),
                        "collect launch");
         else
             FRNN_CHECK(e, launch_collect_nd(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(), P, r2,
                                             cap, e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
                                             e->overflow.as<int>(), e->n_overflow.as<int>(), q0, q1, s, nullptr,
-                                            proj_s),
+                                            proj_s, nullptr, Pd),
                        "collect launch");
         stage_end(e, ST_COLLECT);
         stage_begin(e, ST_EMIT);
         FRNN_CHECK(e, launch_emit_lists(e->lists.as<unsigned long long>(), e->list_counts.as<int>(),
                                         whole ? e->inv.as<int>() : nullptr, q0, rows, K, cap, r2,
-                                        out_idx, out_dist, s),
+                                        out_idx, out_dist, s, -1, Pd),
                    "emit launch");
         FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(),
                                          P, K, r2, 0, N, out_idx, out_dist, rows,
                                          whole ? e->ids.as<int>() : nullptr, s, e->overflow.as<int>(),
-                                         e->n_overflow.as<int>(), q0, proj_s),
+                                         e->n_overflow.as<int>(), q0, proj_s, nullptr, nullptr, Pd),
                    "overflow search launch");
         stage_end(e, ST_EMIT);
         e->launches += 3;
@@ -544,7 +547,7 @@ int search_built(frnn_engine* e, const GridPlan& P, bool principal, int K, float
         stage_begin(e, ST_SEARCH);
         FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(), P, K,
                                          r2, q0, q1, out_idx, out_dist, rows, nullptr, s, nullptr,
-                                         nullptr, -1, proj_s),
+                                         nullptr, -1, proj_s, nullptr, nullptr, Pd),
                    "grid search launch");
         stage_end(e, ST_SEARCH);
         e->launches++;
@@ -554,7 +557,7 @@ int search_built(frnn_engine* e, const GridPlan& P, bool principal, int K, float
         stage_begin(e, ST_SEARCH);
         FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(), P, K,
                                          r2, 0, N, out_idx, out_dist, N, e->ids.as<int>(), s, nullptr,
-                                         nullptr, -1, proj_s),
+                                         nullptr, -1, proj_s, nullptr, nullptr, Pd),
                    "grid search launch");
         stage_end(e, ST_SEARCH);
         e->launches++;
@@ -564,12 +567,12 @@ int search_built(frnn_engine* e, const GridPlan& P, bool principal, int K, float
         stage_begin(e, ST_SEARCH);
         FRNN_CHECK(e, launch_grid_search(e->rows.as<float>(), e->ids.as<int>(), e->starts.as<int>(), P, K,
                                          r2, 0, N, e->tmp_idx.as<int>(), e->tmp_dist.as<float>(), N,
-                                         nullptr, s, nullptr, nullptr, -1, proj_s),
+                                         nullptr, s, nullptr, nullptr, -1, proj_s, nullptr, nullptr, Pd),
                    "grid search launch");
         stage_end(e, ST_SEARCH);
         stage_begin(e, ST_UNPERMUTE);
         FRNN_CHECK(e, launch_unpermute(e->tmp_idx.as<int>(), e->tmp_dist.as<float>(), e->ids.as<int>(),
-                                       N, K, out_idx, out_dist, s),
+                                       N, K, out_idx, out_dist, s, Pd),
                    "unpermute launch");
         stage_end(e, ST_UNPERMUTE);
         e->launches += 2;
@@ -602,6 +605,97 @@ int run_grid(frnn_engine* e, const float* d_pts, int N, int dim, int K, float r2
         s1 = s1 >= N ? N : h[1];
     }
     return search_built(e, P, principal, K, r2, part ? s0 : 0, part ? s1 : N, !part, out_idx, out_dist);
+}
+
+// Whether a self-search takes run_grid_dplan: whole, blocking, on the grid,
+// D <= 4 (the grid axes are the coordinates, so the host needs nothing from
+// the box to choose the kernels).
+bool uses_device_plan(const frnn_engine* e, int path, int dim, bool blocking, bool part) {
+    return e->device_plan && path == FRNN_PATH_GRID && dim <= 4 && blocking && !part;
+}
+
+// A whole self-search on the grid with D <= 4, planned on the device: the
+// bounding-box kernel's last block plans the grid (plan_grid, the same code
+// and arithmetic as the host planner) into e->dplan, and every later kernel
+// reads that plan, so box, build and search run back to back with no host
+// round trip.  What the host must size before the plan exists is sized for
+// the largest plan the cell budget allows: the cell tables and the scan's
+// tiles (those past the plan's table return at once); a kernel zeroes the
+// plan's own count table in place of the host path's memset.  The plan is
+// copied to e->h_plan with the search; after the caller's sync,
+// h_plan->cells == 0 means that no grid was built (finish_dplan).
+int run_grid_dplan(frnn_engine* e, const float* d_pts, int N, int dim, int K, float radius, int* out_idx,
+                   float* out_dist) {
+    cudaStream_t s = e->stream;
+    const int g = grid_axes_for(dim);
+    const long long budget = cell_budget(N, 32);
+    GridPlan P{};  // what the host knows: the kernels read the rest from Pd
+    P.g = g;
+    P.n = N;
+    P.dim = dim;
+    P.row = plan_row_floats(dim);
+    P.cells = budget;
+    const bool lists = uses_lists(e, P, K, false);
+    FRNN_GROW(e, e->counts, (size_t)budget * 4);
+    FRNN_GROW(e, e->starts, ((size_t)budget + 1) * 4);
+    {
+        const int st = grow_scan_status(e, (size_t)scan_tiles(budget) * 8);
+        if (st != FRNN_OK) return st;
+    }
+    FRNN_GROW(e, e->dplan, sizeof(GridPlan));
+    FRNN_GROW(e, e->cellrank, (size_t)N * 8);
+    FRNN_GROW(e, e->rows, ((size_t)N + kCollectRowPad) * P.row * 4);
+    FRNN_GROW(e, e->ids, (size_t)N * 4);
+    if (lists) FRNN_GROW(e, e->inv, (size_t)N * 4);
+    GridPlan* Pd = e->dplan.as<GridPlan>();
+
+    FRNN_CHECK(e, cudaMemsetAsync(e->scan_ticket.p, 0, 4, s), "memset scan ticket");
+    const int blocks = std::min(bbox_blocks(N, e->sms), kBoxMaxBlocks);
+    stage_begin(e, ST_BBOX);
+    FRNN_CHECK(e, launch_bbox(d_pts, N, g, e->box_partial.as<float>(), e->box_ticket.as<unsigned>(),
+                              e->box_out.as<float>(), blocks, s, Pd, dim, radius, budget),
+               "bbox launch");
+    stage_end(e, ST_BBOX);
+    FRNN_CHECK(e, launch_clear_counts(e->counts.as<int>(), budget, Pd, e->sms, s), "clear counts launch");
+    stage_begin(e, ST_HASH);
+    FRNN_CHECK(e, launch_hash_count(d_pts, P, e->counts.as<int>(), e->cellrank.as<int2>(), s, nullptr, Pd),
+               "hash_count launch");
+    stage_end(e, ST_HASH);
+    e->epoch = (e->epoch + 1) & 0x3fffffffu;
+    if (e->epoch == 0) {
+        FRNN_CHECK(e, cudaMemsetAsync(e->scan_status.p, 0, e->scan_status.bytes, s), "memset status");
+        e->epoch = 1;
+    }
+    stage_begin(e, ST_SCAN);
+    FRNN_CHECK(e, launch_scan(e->counts.as<int>(), e->starts.as<int>(), budget,
+                              e->scan_status.as<unsigned long long>(), e->scan_ticket.as<int>(), e->epoch,
+                              e->err_flag.as<int>(), s, e->test_stall == FRNN_TEST_STALL_SCAN ? 1 : -1, Pd),
+               "scan launch");
+    stage_end(e, ST_SCAN);
+    stage_begin(e, ST_SCATTER);
+    FRNN_CHECK(e, launch_scatter(d_pts, P, e->cellrank.as<int2>(), e->starts.as<int>(), e->rows.as<float>(),
+                                 e->ids.as<int>(), s, lists ? e->inv.as<int>() : nullptr, nullptr, nullptr, Pd),
+               "scatter launch");
+    stage_end(e, ST_SCATTER);
+    e->launches += 5;
+    const int st = search_built(e, P, false, K, radius * radius, 0, N, true, out_idx, out_dist, Pd);
+    if (st != FRNN_OK) return st;
+    FRNN_CHECK(e, cudaMemcpyAsync(e->h_plan, Pd, sizeof(GridPlan), cudaMemcpyDeviceToHost, s), "plan readback");
+    return FRNN_OK;
+}
+
+// After the sync that ends a device-planned search: the plan it used, or,
+// when the GPU found no grid, an error for non-finite data or *brute = true
+// (the caller then searches by brute force; every grid kernel returned at
+// once).
+int finish_dplan(frnn_engine* e, GridPlan* P, bool* brute) {
+    *brute = false;
+    *P = *static_cast<const GridPlan*>(e->h_plan);
+    if (P->cells == 0) {
+        if (P->pre_r2 != 0.0f) return fail(e, FRNN_ERR_INVALID_ARG, "points contain NaN or Inf coordinates");
+        *brute = true;
+    }
+    return FRNN_OK;
 }
 
 // Brute force with the tcgen05 distance filter (bf_tc.cu), in two halves.
@@ -1157,7 +1251,29 @@ int search_core(frnn_engine* e, const float* d_pts, int N, int dim, int K, float
 
     GridPlan P{};
     bool principal = false;
-    if (path == FRNN_PATH_GRID) {
+    const bool dplan = uses_device_plan(e, path, dim, blocking, is_part);
+    if (dplan) {
+        int st = run_grid_dplan(e, d_pts, N, dim, K, radius, out_idx, out_dist);
+        if (st != FRNN_OK) return st;
+        FRNN_CHECK(e, cudaMemcpyAsync(e->h_err, e->err_flag.p, sizeof(int), cudaMemcpyDeviceToHost, s),
+                   "error flag readback");
+        FRNN_CHECK(e, cudaStreamSynchronize(s), "search sync");
+        if (*e->h_err != 0) {
+            cudaMemsetAsync(e->err_flag.p, 0, sizeof(int), s);
+            cudaStreamSynchronize(s);
+            return fail(e, FRNN_ERR_TIMEOUT, "a bounded device-side wait gave up");
+        }
+        bool brute = false;
+        st = finish_dplan(e, &P, &brute);
+        if (st != FRNN_OK) return st;
+        if (!brute) {
+            e->last_g = P.g;
+            e->last_cells = P.cells;
+        }
+        // no useful grid: every grid kernel returned at once; brute force
+        // below, then the usual blocking tail
+        path = brute ? FRNN_PATH_BRUTE : FRNN_PATH_GRID;
+    } else if (path == FRNN_PATH_GRID) {
         int st = plan_grid_search(e, d_pts, N, dim, radius, &path, P, &principal);
         if (st != FRNN_OK) return st;
     }
@@ -1170,7 +1286,7 @@ int search_core(frnn_engine* e, const float* d_pts, int N, int dim, int K, float
         e->last_g = 0;
         e->last_cells = 0;
     }
-    if (path == FRNN_PATH_GRID) {
+    if (path == FRNN_PATH_GRID && !dplan) {
         int st = run_grid(e, d_pts, N, dim, K, r2, P, out_idx, out_dist, is_part, s0, s1,
                           principal ? e->proj_u.as<float>() : nullptr);
         if (st != FRNN_OK) return st;
@@ -1199,7 +1315,8 @@ int search_core(frnn_engine* e, const float* d_pts, int N, int dim, int K, float
     }
     e->last_path = path;
     e->last_principal = path == FRNN_PATH_GRID && principal;
-    if (blocking) {
+    // (a device-planned grid search has had its sync and its error check)
+    if (blocking && !(dplan && path == FRNN_PATH_GRID)) {
         FRNN_CHECK(e, cudaMemcpyAsync(e->h_err, e->err_flag.p, sizeof(int), cudaMemcpyDeviceToHost, s),
                    "error flag readback");
         FRNN_CHECK(e, cudaStreamSynchronize(s), "search sync");
@@ -1273,7 +1390,8 @@ int frnn_create(int max_points, int device, frnn_engine** out) {
         cudaMemset(e->err_flag.p, 0, e->err_flag.bytes) != cudaSuccess ||
         cudaMallocHost(&e->h_box, 64) != cudaSuccess || cudaMallocHost(&e->h_err, 64) != cudaSuccess ||
         cudaMallocHost(&e->h_tc, 512 * sizeof(float)) != cudaSuccess ||
-        cudaMallocHost(&e->h_pca, 32768) != cudaSuccess) {
+        cudaMallocHost(&e->h_pca, 32768) != cudaSuccess ||
+        cudaMallocHost(&e->h_plan, sizeof(GridPlan)) != cudaSuccess) {
         cudaGetLastError();
         frnn_destroy(e);
         return FRNN_ERR_OOM;
@@ -1299,7 +1417,7 @@ int frnn_destroy(frnn_engine* e) {
                           &e->proj_u, &e->proj_s, &e->pca_smp, &e->pca_h, &e->pca_counts,
                           &e->q_counts, &e->q_starts, &e->q_cellrank, &e->q_rows, &e->q_ids, &e->q_inv,
                           &e->q_proj_u, &e->q_proj_s, &e->q_proj_partial, &e->q_proj_out, &e->q_box_out,
-                          &e->q_tiles, &e->q_rows32, &e->q_qa, &e->q_pb, &e->ovf_ids};
+                          &e->q_tiles, &e->q_rows32, &e->q_qa, &e->q_pb, &e->ovf_ids, &e->dplan};
         for (DevBuf* b : bufs) free_buf(*b);
         for (cudaEvent_t& ev : e->ev)
             if (ev) cudaEventDestroy(ev);
@@ -1307,6 +1425,7 @@ int frnn_destroy(frnn_engine* e) {
         if (e->h_err) cudaFreeHost(e->h_err);
         if (e->h_tc) cudaFreeHost(e->h_tc);
         if (e->h_pca) cudaFreeHost(e->h_pca);
+        if (e->h_plan) cudaFreeHost(e->h_plan);
     }
     delete e;
     return FRNN_OK;
@@ -1353,6 +1472,10 @@ int frnn_set_option(frnn_engine* e, int option, int64_t value) {
             if (value < FRNN_TEST_STALL_OFF || value > FRNN_TEST_STALL_TC_FILTER)
                 return fail(e, FRNN_ERR_INVALID_ARG, "test stall must be OFF, SCAN or TC_FILTER");
             e->test_stall = (int)value;
+            return FRNN_OK;
+        case FRNN_OPT_DEVICE_PLAN:
+            if (value < 0 || value > 1) return fail(e, FRNN_ERR_INVALID_ARG, "device plan must be 0 or 1");
+            e->device_plan = (int)value;
             return FRNN_OK;
         default:
             return fail(e, FRNN_ERR_INVALID_ARG, "unknown option");

@@ -56,6 +56,11 @@ struct frnn_engine {
     int grid_axes_mode = 0;   // FRNN_OPT_GRID_AXES
     int list_search = 0;      // FRNN_OPT_LIST_SEARCH
     int test_stall = 0;       // FRNN_OPT_TEST_STALL (tests of the timeout path)
+    int device_plan = 1;      // FRNN_OPT_DEVICE_PLAN
+    // device-planned grids: the plan (written by the bounding-box kernel) and
+    // its pinned host copy
+    frnn::eng::DevBuf dplan;
+    void* h_plan = nullptr;   // pinned, one GridPlan
     // a point set kept for frnn_query_grid: on the grid path its sorted rows,
     // ids, cell starts (and projected coordinates) stay in the point buffers
     struct {
@@ -156,8 +161,10 @@ int build_points(frnn_engine* e, const float* d_pts, const frnn::GridPlan& P, co
 // Search the built points' sorted positions [q0, q1).  whole: every query,
 // out[k*N + q] in original order (needs inv when lists are used); otherwise
 // row j = sorted position q0 + j of out[k*(q1-q0) + j].
+// Pd (optional): the plan as the GPU made it (run_grid_dplan); P then
+// carries only what the host knows before the box (n, dim, g, row).
 int search_built(frnn_engine* e, const frnn::GridPlan& P, bool principal, int K, float r2, int q0, int q1,
-                 bool whole, int* out_idx, float* out_dist);
+                 bool whole, int* out_idx, float* out_dist, const frnn::GridPlan* Pd = nullptr);
 
 // Tensor-core brute force: the host-side plan (centre, scale, thresholds)
 // and the device work for query tiles [qb_begin, qb_end).

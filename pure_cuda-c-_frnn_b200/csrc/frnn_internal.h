@@ -11,24 +11,37 @@ namespace frnn {
 
 // grid_build.cu
 int bbox_blocks(int n, int sms);
+// plan_out (optional): the grid planned on the device from the box
+// (plan_grid with dim, radius and at most max_cells cells); a plan with
+// cells = 0 means no grid (pre_r2 = 1: the data hold NaN or Inf)
 cudaError_t launch_bbox(const float* pts, int n, int g, float* partial, unsigned int* ticket,
-                        float* out, int blocks, cudaStream_t s);
+                        float* out, int blocks, cudaStream_t s, GridPlan* plan_out = nullptr,
+                        int dim = 0, float radius = 0.0f, long long max_cells = 0);
 // proj (optional): the grid axes are proj[i*kProjStride + d] instead of the
-// leading coordinates of pts
+// leading coordinates of pts.  Pd (optional, every launcher below): the plan
+// made on the device, read by the kernel in place of P (the host's P then
+// only needs n, dim, g and row); a device plan with cells = 0 makes the
+// kernel do nothing.
 cudaError_t launch_hash_count(const float* pts, const GridPlan& P, int* counts, int2* cellrank,
-                              cudaStream_t s, const float* proj = nullptr);
+                              cudaStream_t s, const float* proj = nullptr, const GridPlan* Pd = nullptr);
 long long scan_tiles(long long cells);
 // withhold >= 0 makes that tile keep its status to itself, so the bounded
 // look-back of the next tile gives up (tests of the timeout path only).
+// With Pd, `cells` is the largest table the device plan may have and the
+// kernel scans Pd->cells of them.
 cudaError_t launch_scan(const int* counts, int* starts, long long cells,
                         unsigned long long* status, int* ticket, unsigned epoch, int* err,
-                        cudaStream_t s, int withhold = -1);
+                        cudaStream_t s, int withhold = -1, const GridPlan* Pd = nullptr);
+// counts[0, Pd->cells) = 0 for a plan made on the device (max_cells: the
+// largest table it may have, which sizes the launch)
+cudaError_t launch_clear_counts(int* counts, long long max_cells, const GridPlan* Pd, int sms,
+                                cudaStream_t s);
 // inv (optional): inv[original index] = sorted position; proj (optional, D > 3):
 // projected coordinates copied to proj_sorted in cell order
 cudaError_t launch_scatter(const float* pts, const GridPlan& P, const int2* cellrank,
                            const int* starts, float* rows, int* ids, cudaStream_t s,
                            int* inv = nullptr, const float* proj = nullptr,
-                           float* proj_sorted = nullptr);
+                           float* proj_sorted = nullptr, const GridPlan* Pd = nullptr);
 
 // grid_search.cu
 // Searches sorted query positions [q0, q1).  Results for sorted position sq go
@@ -48,7 +61,7 @@ cudaError_t launch_grid_search(const float* rows, const int* ids, const int* sta
                                cudaStream_t s, const int* qlist = nullptr,
                                const int* qcount = nullptr, long long row_base = -1,
                                const float* proj = nullptr, const float* qrows = nullptr,
-                               const float* qproj = nullptr);
+                               const float* qproj = nullptr, const GridPlan* Pd = nullptr);
 
 // grid_collect.cu -- D = 3 two-kernel search (K <= 32).
 constexpr int kCollectRowPad = 8;
@@ -63,7 +76,8 @@ constexpr int kCollectRowPad = 8;
 cudaError_t launch_collect_d3(const float* rows, const int* starts, const GridPlan& P, float r2,
                               int cap, unsigned long long* lists, int* counts, int* overflow,
                               int* n_overflow, int q0, int q1, cudaStream_t s,
-                              const float* qrows = nullptr, const int* qlist = nullptr);
+                              const float* qrows = nullptr, const int* qlist = nullptr,
+                              const GridPlan* Pd = nullptr);
 // collect for D != 3 (any grid the planner makes, K-independent): the same
 // lists as launch_collect_d3 from one thread per query over its 3^g shell;
 // qproj: the queries' projected coordinates on a principal-axis grid (the
@@ -71,17 +85,19 @@ cudaError_t launch_collect_d3(const float* rows, const int* starts, const GridPl
 cudaError_t launch_collect_nd(const float* rows, const int* ids, const int* starts, const GridPlan& P,
                               float r2, int cap, unsigned long long* lists, int* counts, int* overflow,
                               int* n_overflow, int q0, int q1, cudaStream_t s, const float* qrows = nullptr,
-                              const float* qproj = nullptr, const int* qlist = nullptr);
+                              const float* qproj = nullptr, const int* qlist = nullptr,
+                              const GridPlan* Pd = nullptr);
 // emit: for output rows q < n -- sorted position map[q] (map = inv: rows in
 // original order), or q0 + q without map -- whose count is at most cap, the K
 // smallest keys ascending to out[k*n + q], padded (-1, r2).  map_range: the
 // number of sorted positions map's entries index (default n).
 cudaError_t launch_emit_lists(const unsigned long long* lists, const int* counts, const int* map,
                               int q0, int n, int K, int cap, float r2, int* oidx, float* odist,
-                              cudaStream_t s, int map_range = -1);
+                              cudaStream_t s, int map_range = -1, const GridPlan* Pd = nullptr);
 // out[k*N + ids[sq]] = in[k*N + sq]
 cudaError_t launch_unpermute(const int* in_idx, const float* in_dist, const int* ids, int n,
-                             int K, int* out_idx, float* out_dist, cudaStream_t s);
+                             int K, int* out_idx, float* out_dist, cudaStream_t s,
+                             const GridPlan* Pd = nullptr);
 
 // bruteforce.cu
 // Queries [q0, q1) of the SoA cloud against all n points; results of query q

@@ -13,8 +13,11 @@
 //   * the scan is a single-pass decoupled-lookback scan whose waits are bounded;
 //   * sorted points are stored as rows (AoS, D rounded up to 4 floats, 16-byte
 //     vector stores); for D = 3 the fourth float carries the original index.
+#include <algorithm>
+
 #include "frnn_device.cuh"
 #include "frnn_internal.h"
+#include "grid_plan.cuh"
 
 namespace frnn {
 
@@ -30,10 +33,17 @@ constexpr int kBoxSlots = 2 * kBoxAxes + 1;     // (min,max) per axis + non-fini
 // flight per thread.  Each block writes a partial; the last block to finish
 // (atomic ticket) folds the partials with all its threads into out[0..8]:
 // out[2d] = min, out[2d+1] = max, out[8] = 1 if any coordinate is NaN or Inf.
+// With plan_out, that block's thread 0 then plans the grid from the box
+// (plan_grid, the host planner's own code) and writes it to *plan_out, so
+// no host round trip separates the box from the build; a plan with cells = 0
+// means "no grid" (non-finite data, or no useful grid) and every kernel given
+// the plan then does nothing.
 __global__ void __launch_bounds__(kBoxThreads) bbox_kernel(const float* __restrict__ pts, int n, int g,
                                                            float* __restrict__ partial,
                                                            unsigned int* __restrict__ ticket,
-                                                           float* __restrict__ out) {
+                                                           float* __restrict__ out,
+                                                           GridPlan* __restrict__ plan_out, int dim,
+                                                           float radius, long long max_cells) {
     float mn[kBoxAxes], mx[kBoxAxes];
     bool bad = false;
 #pragma unroll
@@ -69,6 +79,7 @@ __global__ void __launch_bounds__(kBoxThreads) bbox_kernel(const float* __restri
         }
     }
     __shared__ float sred[kBoxSlots][kBoxThreads / 32];
+    __shared__ float sbox[kBoxSlots];
     __shared__ bool last;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
@@ -127,20 +138,39 @@ __global__ void __launch_bounds__(kBoxThreads) bbox_kernel(const float* __restri
         float a = sred[t][0];
         for (int w = 1; w < kBoxThreads / 32; ++w) a = is_max ? fmaxf(a, sred[t][w]) : fminf(a, sred[t][w]);
         out[t] = a;
+        sbox[t] = a;
     }
     if (threadIdx.x == 0) *ticket = 0u;  // ready for the next launch
+    if (plan_out == nullptr) return;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        GridPlan P{};
+        const bool finite = sbox[kBoxSlots - 1] == 0.0f;
+        if (!(finite && plan_grid(sbox, g, n, dim, radius, 0.0, max_cells, P))) {
+            P = GridPlan{};
+            P.g = g;
+            P.n = n;
+            P.dim = dim;
+            P.cells = 0;
+            // pre_r2 carries the reason for the host: 1 = non-finite data
+            P.pre_r2 = finite ? 0.0f : 1.0f;
+        }
+        *plan_out = P;
+    }
 }
 
 // ---- histogram: cell of each point and its slot within the cell ------------
 
 // The grid axes are the leading coordinates of the SoA input, or, with proj,
 // the projected coordinates proj[i*kProjStride + d] (principal axes).
-__global__ void __launch_bounds__(256) hash_count_kernel(const float* __restrict__ pts, GridPlan P,
+__global__ void __launch_bounds__(256) hash_count_kernel(const float* __restrict__ pts, GridPlan Pv,
                                                          int* __restrict__ counts,
                                                          int2* __restrict__ cellrank,
-                                                         const float* __restrict__ proj) {
+                                                         const float* __restrict__ proj,
+                                                         const GridPlan* __restrict__ Pd) {
+    const GridPlan P = Pd ? *Pd : Pv;
     int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= P.n) return;
+    if (i >= P.n || P.cells == 0) return;
     long long c = 0;
 #pragma unroll
     for (int d = 0; d < kMaxGridAxes; ++d) {
@@ -167,17 +197,22 @@ __device__ __forceinline__ unsigned long long pack_status(unsigned epoch, unsign
     return ((unsigned long long)((epoch << 2) | flag) << 32) | value;
 }
 
+// cells_dev (optional): the cell count of a plan written on the device (the
+// launch then covers the largest table the plan may have; tiles past the
+// plan's table return at once).
 __global__ void __launch_bounds__(kScanThreads) scan_kernel(const int* __restrict__ counts,
                                                             int* __restrict__ starts,
                                                             long long cells,
                                                             unsigned long long* __restrict__ status,
                                                             int* __restrict__ ticket, unsigned epoch,
-                                                            int* __restrict__ err, int withhold) {
+                                                            int* __restrict__ err, int withhold,
+                                                            const long long* __restrict__ cells_dev) {
     // withhold >= 0 (a test of the bounded wait only): that tile never
     // publishes its status, so the tile after it must give up waiting
     __shared__ int s_tile;
     __shared__ int s_warp[kScanThreads / 32];
     __shared__ unsigned s_excl;
+    if (cells_dev) cells = *cells_dev;
     if (threadIdx.x == 0) s_tile = atomicAdd(ticket, 1);
     __syncthreads();
     const int tile = s_tile;
@@ -283,6 +318,22 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const int* __restric
     }
 }
 
+// ---- zeroed count table for a plan made on the device -------------------------
+
+// counts[0, Pd->cells) = 0: the memset of the host-planned build, for a table
+// whose size only the device knows.  Like that memset, it leaves the table in
+// L2 for the histogram's atomics that follow.
+__global__ void __launch_bounds__(256) clear_counts_kernel(int* __restrict__ counts,
+                                                           const GridPlan* __restrict__ Pd) {
+    const long long cells = Pd->cells;
+    const long long n4 = cells >> 2;
+    const long long step = (long long)gridDim.x * blockDim.x;
+    int4* c4 = reinterpret_cast<int4*>(counts);
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += step)
+        c4[i] = make_int4(0, 0, 0, 0);
+    if (blockIdx.x == 0 && threadIdx.x < (cells & 3)) counts[(n4 << 2) + threadIdx.x] = 0;
+}
+
 // ---- counting-sort scatter into cell order ------------------------------------
 
 __global__ void __launch_bounds__(256) scatter_d3_kernel(const float* __restrict__ pts, int n,
@@ -290,9 +341,10 @@ __global__ void __launch_bounds__(256) scatter_d3_kernel(const float* __restrict
                                                          const int* __restrict__ starts,
                                                          float4* __restrict__ rows,
                                                          int* __restrict__ ids,
-                                                         int* __restrict__ inv) {
+                                                         int* __restrict__ inv,
+                                                         const GridPlan* __restrict__ Pd) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
+    if (i >= n || (Pd && Pd->cells == 0)) return;
     int2 cr = cellrank[i];
     int pos = __ldg(&starts[cr.x]) + cr.y;
     if (pos < 0 || pos >= n) return;  // only reachable if the scan gave up (error flag set)
@@ -310,9 +362,10 @@ __global__ void __launch_bounds__(256) scatter_rows_kernel(const float* __restri
                                                            int* __restrict__ ids,
                                                            int* __restrict__ inv,
                                                            const float4* __restrict__ proj,
-                                                           float4* __restrict__ proj_sorted) {
+                                                           float4* __restrict__ proj_sorted,
+                                                           const GridPlan* __restrict__ Pd) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
+    if (i >= n || (Pd && Pd->cells == 0)) return;
     int2 cr = cellrank[i];
     long long pos = __ldg(&starts[cr.x]) + cr.y;
     if (pos < 0 || pos >= n) return;  // only reachable if the scan gave up (error flag set)
@@ -339,8 +392,10 @@ __global__ void __launch_bounds__(256) scatter_rows_kernel(const float* __restri
 // ---- launchers ----------------------------------------------------------------
 
 cudaError_t launch_bbox(const float* pts, int n, int g, float* partial, unsigned int* ticket,
-                        float* out, int blocks, cudaStream_t s) {
-    bbox_kernel<<<blocks, kBoxThreads, 0, s>>>(pts, n, g, partial, ticket, out);
+                        float* out, int blocks, cudaStream_t s, GridPlan* plan_out, int dim,
+                        float radius, long long max_cells) {
+    bbox_kernel<<<blocks, kBoxThreads, 0, s>>>(pts, n, g, partial, ticket, out, plan_out, dim, radius,
+                                                max_cells);
     return cudaGetLastError();
 }
 
@@ -350,8 +405,8 @@ int bbox_blocks(int n, int sms) {
 }
 
 cudaError_t launch_hash_count(const float* pts, const GridPlan& P, int* counts, int2* cellrank,
-                              cudaStream_t s, const float* proj) {
-    hash_count_kernel<<<(P.n + 255) / 256, 256, 0, s>>>(pts, P, counts, cellrank, proj);
+                              cudaStream_t s, const float* proj, const GridPlan* Pd) {
+    hash_count_kernel<<<(P.n + 255) / 256, 256, 0, s>>>(pts, P, counts, cellrank, proj, Pd);
     return cudaGetLastError();
 }
 
@@ -359,24 +414,33 @@ long long scan_tiles(long long cells) { return (cells + kScanTile - 1) / kScanTi
 
 cudaError_t launch_scan(const int* counts, int* starts, long long cells,
                         unsigned long long* status, int* ticket, unsigned epoch, int* err,
-                        cudaStream_t s, int withhold) {
+                        cudaStream_t s, int withhold, const GridPlan* Pd) {
     long long tiles = scan_tiles(cells);
     scan_kernel<<<(unsigned)tiles, kScanThreads, 0, s>>>(counts, starts, cells, status, ticket,
-                                                         epoch & 0x3fffffffu, err, withhold);
+                                                         epoch & 0x3fffffffu, err, withhold,
+                                                         Pd ? &Pd->cells : nullptr);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_clear_counts(int* counts, long long max_cells, const GridPlan* Pd, int sms,
+                                cudaStream_t s) {
+    const long long want = (max_cells / 4 + 255) / 256;
+    const int blocks = (int)std::max<long long>(1, std::min<long long>(want, 8LL * sms));
+    clear_counts_kernel<<<blocks, 256, 0, s>>>(counts, Pd);
     return cudaGetLastError();
 }
 
 cudaError_t launch_scatter(const float* pts, const GridPlan& P, const int2* cellrank,
                            const int* starts, float* rows, int* ids, cudaStream_t s, int* inv,
-                           const float* proj, float* proj_sorted) {
+                           const float* proj, float* proj_sorted, const GridPlan* Pd) {
     if (proj && P.dim == 3) return cudaErrorInvalidValue;  // principal axes are for D > 4
     if (P.dim == 3)
         scatter_d3_kernel<<<(P.n + 255) / 256, 256, 0, s>>>(pts, P.n, cellrank, starts,
-                                                            reinterpret_cast<float4*>(rows), ids, inv);
+                                                            reinterpret_cast<float4*>(rows), ids, inv, Pd);
     else
         scatter_rows_kernel<<<(P.n + 255) / 256, 256, 0, s>>>(
             pts, P.n, P.dim, P.row, cellrank, starts, rows, ids, inv,
-            reinterpret_cast<const float4*>(proj), reinterpret_cast<float4*>(proj_sorted));
+            reinterpret_cast<const float4*>(proj), reinterpret_cast<float4*>(proj_sorted), Pd);
     return cudaGetLastError();
 }
 

@@ -49,15 +49,18 @@ __device__ __forceinline__ void append_if(bool ok, unsigned long long* list, int
 }
 
 __global__ void __launch_bounds__(256)
-    collect_d3_kernel(const float4* __restrict__ rows, const int* __restrict__ starts, GridPlan P,
+    collect_d3_kernel(const float4* __restrict__ rows, const int* __restrict__ starts, GridPlan Pv,
                       float r2, int cap, unsigned long long* __restrict__ lists,
                       int* __restrict__ counts, int* __restrict__ overflow,
                       int* __restrict__ n_overflow, int q0, int q1,
-                      const float4* __restrict__ qrows, const int* __restrict__ qlist) {
+                      const float4* __restrict__ qrows, const int* __restrict__ qlist,
+                      const GridPlan* __restrict__ Pd) {
     // queries: the points themselves (qrows == rows) or a separate set in
     // the same grid's cell order; sorted positions [q0, q1), or qlist[q0..q1)
+    // Pd: the plan, when the GPU made it (cells = 0: no grid, nothing to do)
+    const GridPlan P = Pd ? *Pd : Pv;
     const int qi = q0 + blockIdx.x * blockDim.x + threadIdx.x;
-    if (qi >= q1) return;
+    if (qi >= q1 || P.cells == 0) return;
     const int sq = qlist ? __ldg(&qlist[qi]) : qi;
     const float4 q = __ldg(&qrows[sq]);
     const float cs = P.cell, eps = P.eps;
@@ -66,33 +69,36 @@ __global__ void __launch_bounds__(256)
     const int gz = cell_coord(q.z, P.origin[2], P.inv_cell, P.res[2]);
     unsigned long long* mine = lists + (long long)sq * cap;
     int n = 0;
-    for (int cz = max(gz - 1, 0); cz <= min(gz + 1, P.res[2] - 1); ++cz) {
-        const float bz = axis_gap(q.z, cz, P.origin[2], cs, eps);
-        if (bz * kPruneScale > r2) continue;
-        for (int cy = max(gy - 1, 0); cy <= min(gy + 1, P.res[1] - 1); ++cy) {
-            const float byz = bz + axis_gap(q.y, cy, P.origin[1], cs, eps);
-            if (byz * kPruneScale > r2) continue;
-            int xlo = max(gx - 1, 0), xhi = min(gx + 1, P.res[0] - 1);
-            if (xlo < gx && (byz + axis_gap(q.x, xlo, P.origin[0], cs, eps)) * kPruneScale > r2) xlo = gx;
-            if (xhi > gx && (byz + axis_gap(q.x, xhi, P.origin[0], cs, eps)) * kPruneScale > r2) xhi = gx;
-            const long long rb = (long long)cz * P.stride[2] + (long long)cy * P.stride[1];
-            // clamped to [0, n): a corrupt start table never reads out of bounds
-            int j = min(max(__ldg(&starts[rb + xlo]), 0), P.n);
-            const int e = min(max(__ldg(&starts[rb + xhi + 1]), j), P.n);
-            // one loop per span, eight row loads in flight per pass; the last pass
-            // reads up to seven rows past the span (the row array is padded by
-            // kCollectRowPad rows) and masks them.  Appends are predicated
-            // stores: no branch per candidate (B200, cfg2: 0.290 ms against
-            // 0.301 with 8/4/2/1-wide loops and branches around every append)
-            for (; j < e; j += kCollectRowPad) {
-                float4 p[kCollectRowPad];
+    // every row's span bounds loaded before the first span is walked: the
+    // 18 start-table loads of a query are in flight together
+    int js[9], es[9];
 #pragma unroll
-                for (int u = 0; u < kCollectRowPad; ++u) p[u] = __ldg(&rows[j + u]);
+    for (int rr = 0; rr < 9; ++rr) {
+        const int cz = gz - 1 + rr / 3, cy = gy - 1 + rr % 3;
+        js[rr] = 0;
+        es[rr] = 0;
+        if (cz < 0 || cz >= P.res[2] || cy < 0 || cy >= P.res[1]) continue;
+        const float byz = axis_gap(q.z, cz, P.origin[2], cs, eps) + axis_gap(q.y, cy, P.origin[1], cs, eps);
+        if (byz * kPruneScale > r2) continue;
+        int xlo = max(gx - 1, 0), xhi = min(gx + 1, P.res[0] - 1);
+        if (xlo < gx && (byz + axis_gap(q.x, xlo, P.origin[0], cs, eps)) * kPruneScale > r2) xlo = gx;
+        if (xhi > gx && (byz + axis_gap(q.x, xhi, P.origin[0], cs, eps)) * kPruneScale > r2) xhi = gx;
+        const long long rb = (long long)cz * P.stride[2] + (long long)cy * P.stride[1];
+        js[rr] = __ldg(&starts[rb + xlo]);
+        es[rr] = __ldg(&starts[rb + xhi + 1]);
+    }
 #pragma unroll
-                for (int u = 0; u < kCollectRowPad; ++u) {
-                    const float d = dist2_d3(q.x, q.y, q.z, p[u].x, p[u].y, p[u].z);
-                    append_if(j + u < e && d < r2, mine, n, cap, d, __float_as_int(p[u].w));
-                }
+    for (int rr = 0; rr < 9; ++rr) {
+        int j = min(max(js[rr], 0), P.n);
+        const int e = min(max(es[rr], j), P.n);
+        for (; j < e; j += kCollectRowPad) {
+            float4 p[kCollectRowPad];
+#pragma unroll
+            for (int u = 0; u < kCollectRowPad; ++u) p[u] = __ldg(&rows[j + u]);
+#pragma unroll
+            for (int u = 0; u < kCollectRowPad; ++u) {
+                const float d = dist2_d3(q.x, q.y, q.z, p[u].x, p[u].y, p[u].z);
+                append_if(j + u < e && d < r2, mine, n, cap, d, __float_as_int(p[u].w));
             }
         }
     }
@@ -112,11 +118,13 @@ __global__ void __launch_bounds__(256)
 template <int NV, int G>
 __global__ void __launch_bounds__(256)
     collect_nd_kernel(const float4* __restrict__ rows, const int* __restrict__ ids,
-                      const int* __restrict__ starts, GridPlan P, float r2, int cap,
+                      const int* __restrict__ starts, GridPlan Pv, float r2, int cap,
                       unsigned long long* __restrict__ lists, int* __restrict__ counts,
                       int* __restrict__ overflow, int* __restrict__ n_overflow, int q0, int q1,
                       const float4* __restrict__ qrows, const float4* __restrict__ qproj,
-                      const int* __restrict__ qlist) {
+                      const int* __restrict__ qlist, const GridPlan* __restrict__ Pd) {
+    const GridPlan P = Pd ? *Pd : Pv;
+    if (P.cells == 0) return;
     // the bound span gaps are tested against
     const float gap_r2 = qproj ? P.pre_r2 : r2;
     constexpr int W = NV == 1 ? 8 : (NV == 2 ? 4 : 2);  // rows in flight per pass
@@ -281,7 +289,9 @@ template <int KN>
 __global__ void __launch_bounds__(128, 5)
     emit_lists_kernel(const unsigned long long* __restrict__ lists, const int* __restrict__ counts,
                       const int* __restrict__ map, int q0, int n, int K, int cap, float r2,
-                      int* __restrict__ oidx, float* __restrict__ odist, int map_range) {
+                      int* __restrict__ oidx, float* __restrict__ odist, int map_range,
+                      const GridPlan* __restrict__ Pd) {
+    if (Pd && Pd->cells == 0) return;  // a plan made on the GPU found no grid
     // output row q: sorted position map[q] (original order), or q0 + q (a
     // slice of the sorted order).  The block's 128 rows are dealt to its
     // threads by the number of 16-key batches their lists need, so a warp's
@@ -331,11 +341,11 @@ __global__ void __launch_bounds__(128, 5)
 cudaError_t launch_collect_d3(const float* rows, const int* starts, const GridPlan& P, float r2,
                               int cap, unsigned long long* lists, int* counts, int* overflow,
                               int* n_overflow, int q0, int q1, cudaStream_t s, const float* qrows,
-                              const int* qlist) {
+                              const int* qlist, const GridPlan* Pd) {
     if (q1 <= q0) return cudaSuccess;
     collect_d3_kernel<<<(q1 - q0 + 255) / 256, 256, 0, s>>>(
         reinterpret_cast<const float4*>(rows), starts, P, r2, cap, lists, counts, overflow, n_overflow,
-        q0, q1, reinterpret_cast<const float4*>(qrows ? qrows : rows), qlist);
+        q0, q1, reinterpret_cast<const float4*>(qrows ? qrows : rows), qlist, Pd);
     return cudaGetLastError();
 }
 
@@ -343,11 +353,12 @@ namespace {
 template <int NV, int G>
 cudaError_t launch_nd(const float* rows, const int* ids, const int* starts, const GridPlan& P, float r2,
                       int cap, unsigned long long* lists, int* counts, int* overflow, int* n_overflow, int q0,
-                      int q1, cudaStream_t s, const float* qrows, const float* qproj, const int* qlist) {
+                      int q1, cudaStream_t s, const float* qrows, const float* qproj, const int* qlist,
+                      const GridPlan* Pd) {
     collect_nd_kernel<NV, G><<<(q1 - q0 + 255) / 256, 256, 0, s>>>(
         reinterpret_cast<const float4*>(rows), ids, starts, P, r2, cap, lists, counts, overflow, n_overflow,
         q0, q1, reinterpret_cast<const float4*>(qrows ? qrows : rows), reinterpret_cast<const float4*>(qproj),
-        qlist);
+        qlist, Pd);
     return cudaGetLastError();
 }
 }  // namespace
@@ -355,12 +366,12 @@ cudaError_t launch_nd(const float* rows, const int* ids, const int* starts, cons
 cudaError_t launch_collect_nd(const float* rows, const int* ids, const int* starts, const GridPlan& P,
                               float r2, int cap, unsigned long long* lists, int* counts, int* overflow,
                               int* n_overflow, int q0, int q1, cudaStream_t s, const float* qrows,
-                              const float* qproj, const int* qlist) {
+                              const float* qproj, const int* qlist, const GridPlan* Pd) {
     if (q1 <= q0) return cudaSuccess;
     if (qproj && !(P.pre_r2 > 0.0f)) return cudaErrorInvalidValue;  // a principal grid carries its bound
     const int nv = P.row / 4;
 #define FRNN_ND(NV, G) return launch_nd<NV, G>(rows, ids, starts, P, r2, cap, lists, counts, overflow, \
-                                                n_overflow, q0, q1, s, qrows, qproj, qlist)
+                                                n_overflow, q0, q1, s, qrows, qproj, qlist, Pd)
     if (nv == 1 && !qproj) {
         if (P.g == 1) FRNN_ND(1, 1);
         if (P.g == 2) FRNN_ND(1, 2);
@@ -391,16 +402,16 @@ cudaError_t launch_collect_nd(const float* rows, const int* ids, const int* star
 
 cudaError_t launch_emit_lists(const unsigned long long* lists, const int* counts, const int* map,
                               int q0, int n, int K, int cap, float r2, int* oidx, float* odist,
-                              cudaStream_t s, int map_range) {
+                              cudaStream_t s, int map_range, const GridPlan* Pd) {
     if (K > 32) return cudaErrorInvalidValue;  // the register top-K holds at most 32 keys
     if (n <= 0) return cudaSuccess;
     if (map_range < 0) map_range = n;
     if (K <= 16)
         emit_lists_kernel<16><<<(n + 127) / 128, 128, 0, s>>>(lists, counts, map, q0, n, K, cap, r2,
-                                                              oidx, odist, map_range);
+                                                              oidx, odist, map_range, Pd);
     else
         emit_lists_kernel<32><<<(n + 127) / 128, 128, 0, s>>>(lists, counts, map, q0, n, K, cap, r2,
-                                                              oidx, odist, map_range);
+                                                              oidx, odist, map_range, Pd);
     return cudaGetLastError();
 }
 

@@ -236,14 +236,17 @@ struct Shell<1> {
 template <int NV, int G, bool D3, int GR = kGroup>
 __global__ void __launch_bounds__(kWarps * 32, D3 ? FRNN_COOP_D3_MIN_BLOCKS : FRNN_COOP_ND_MIN_BLOCKS)
     grid_coop_kernel(const float4* __restrict__ rows, const int* __restrict__ ids,
-                     const int* __restrict__ starts, GridPlan P, int K, float r2, int q0, int q1,
+                     const int* __restrict__ starts, GridPlan Pv, int K, float r2, int q0, int q1,
                      int* __restrict__ oidx, float* __restrict__ odist, long long ostride,
                      const int* __restrict__ scatter_ids, const int* __restrict__ qlist,
                      const int* __restrict__ qcount, long long row_base,
-                     const float4* __restrict__ queries) {
+                     const float4* __restrict__ queries, const GridPlan* __restrict__ Pd) {
     // queries: the queries' rows (a separate query set in the same grid's
-    // cell order, or the points' own)
+    // cell order, or the points' own).  Pd: the plan, when the GPU made it
+    // (cells = 0: no grid, nothing to do)
     extern __shared__ __align__(16) unsigned char smem[];
+    const GridPlan P = Pd ? *Pd : Pv;
+    if (P.cells == 0) return;
     if (qcount) q1 = min(q1, q0 + __ldg(qcount));  // list length known only on the device
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int cap = list_cap(K);

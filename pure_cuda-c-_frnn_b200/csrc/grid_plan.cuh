@@ -25,6 +25,24 @@ __host__ __device__ inline int plan_row_floats(int dim) {
     return r;
 }
 
+// Double products and sums rounded one at a time on the host and on the GPU
+// alike: device code would otherwise fuse a*b+c into one FMA, and a plan made
+// on the GPU (the bounding-box kernel's planner) must equal the host's.
+__host__ __device__ inline double plan_mul(double a, double b) {
+#ifdef __CUDA_ARCH__
+    return __dmul_rn(a, b);
+#else
+    return a * b;
+#endif
+}
+__host__ __device__ inline double plan_add(double a, double b) {
+#ifdef __CUDA_ARCH__
+    return __dadd_rn(a, b);
+#else
+    return a + b;
+#endif
+}
+
 // Plan a grid on g axes whose bounding box is box[2d], box[2d+1] (d < g).
 // `extra` is an absolute allowance added to the cell edge (the rounding bound
 // of projected coordinates; 0 for the data's own coordinates).  At most
@@ -43,7 +61,8 @@ __host__ __device__ inline bool plan_grid(const float* box, int g, int N, int di
     // the query's 3^g shell despite float rounding of the cell assignment
     // (|error| of (x - origin) * inv_cell is a few ulps of the cell index).
     const double u = 1.0 / 16777216.0;
-    double cell = (double)radius * (1.0 + 1e-5 + 8.0 * u * (ext_max / radius + 2.0)) + extra;
+    const double slack = plan_mul(plan_mul(8.0, u), plan_add(ext_max / radius, 2.0));
+    double cell = plan_add(plan_mul((double)radius, plan_add(1.0 + 1e-5, slack)), extra);
     long long res[kMaxGridAxes];
     long long cells = 1;
     for (int iter = 0; iter < 200; ++iter) {

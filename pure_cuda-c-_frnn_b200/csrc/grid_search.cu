@@ -28,11 +28,12 @@ __global__ void __launch_bounds__(256) unpermute_kernel(const int* __restrict__ 
                                                         const float* __restrict__ in_dist,
                                                         const int* __restrict__ ids, int n, int K,
                                                         int* __restrict__ out_idx,
-                                                        float* __restrict__ out_dist) {
+                                                        float* __restrict__ out_dist,
+                                                        const GridPlan* __restrict__ Pd) {
     // blockIdx.y = a slab of kUnpermRows output rows: blocks of one slab run
     // together, so the scattered writes stay inside an L2-resident region.
     const int sq = blockIdx.x * blockDim.x + threadIdx.x;
-    if (sq >= n) return;
+    if (sq >= n || (Pd && Pd->cells == 0)) return;
     const int o = __ldg(&ids[sq]);
     // a permutation entry outside [0, n) only exists after a scan gave up
     // (the search then reports FRNN_ERR_TIMEOUT); never write through it
@@ -80,6 +81,7 @@ struct CoopArgs {
     const float* proj;
     const float* qrows;
     const float* qproj;
+    const GridPlan* Pd;
 };
 
 template <int NV, int G, bool D3>
@@ -93,7 +95,7 @@ cudaError_t launch_coop(const CoopArgs& a, cudaStream_t s) {
     coop::grid_coop_kernel<NV, G, D3, GR><<<blocks, coop::kWarps * 32, smem, s>>>(
         reinterpret_cast<const float4*>(a.rows), a.ids, a.starts, a.P, a.K, a.r2, a.q0, a.q1, a.oidx,
         a.odist, a.ostride, a.scatter_ids, a.qlist, a.qcount, a.row_base,
-        reinterpret_cast<const float4*>(a.qrows ? a.qrows : a.rows));
+        reinterpret_cast<const float4*>(a.qrows ? a.qrows : a.rows), a.Pd);
     return cudaGetLastError();
 }
 
@@ -121,11 +123,14 @@ cudaError_t launch_grid_search(const float* rows, const int* ids, const int* sta
                                float* odist, long long ostride, const int* scatter_ids,
                                cudaStream_t s, const int* qlist, const int* qcount,
                                long long row_base, const float* proj, const float* qrows,
-                               const float* qproj) {
+                               const float* qproj, const GridPlan* Pd) {
     if (q1 <= q0) return cudaSuccess;
+    // a plan made on the GPU: leading-coordinate grids only (the kernel
+    // template follows P.dim and P.g, which the host knows)
+    if (Pd && proj) return cudaErrorInvalidValue;
     const CoopArgs a{rows, ids, starts, P, K, r2, q0, q1, oidx, odist, ostride, scatter_ids,
                      qlist, qcount, row_base >= 0 ? row_base : (scatter_ids ? 0LL : (long long)q0), proj, qrows,
-                     qproj};
+                     qproj, Pd};
     if (P.dim == 3 && P.g == 3 && !proj) return launch_coop<1, 3, true>(a, s);
     // (row float4s, grid axes) pairs the planner produces: leading coordinates
     // G = min(D, 4); principal axes (D > 4) G in 2..6
@@ -169,9 +174,9 @@ cudaError_t launch_grid_search(const float* rows, const int* ids, const int* sta
 }
 
 cudaError_t launch_unpermute(const int* in_idx, const float* in_dist, const int* ids, int n,
-                             int K, int* out_idx, float* out_dist, cudaStream_t s) {
+                             int K, int* out_idx, float* out_dist, cudaStream_t s, const GridPlan* Pd) {
     dim3 grid((n + 255) / 256, (K + kUnpermRows - 1) / kUnpermRows);
-    unpermute_kernel<<<grid, 256, 0, s>>>(in_idx, in_dist, ids, n, K, out_idx, out_dist);
+    unpermute_kernel<<<grid, 256, 0, s>>>(in_idx, in_dist, ids, n, K, out_idx, out_dist, Pd);
     return cudaGetLastError();
 }
 
