@@ -12,11 +12,12 @@ one cloud.
 
 Multi-GPU (one process per GPU under torchrun), ``--mode strong`` (default):
 one cloud, its queries sharded over the ranks by the engine's own NCCL path
-(frnn_search_sharded: rank 0 plans and builds the grid once, broadcasts the
-built structure, every rank searches a work-balanced slice of the cell-sorted
-queries, the slices are gathered to rank 0 and scattered into [K, N] -- all
-inside every step); ``value`` = N / max-over-ranks step time, ``shard``
-reports every rank's stage times and bytes.  ``--mode weak``: every rank
+(frnn_search_sharded: rank 0 plans and builds the grid once and broadcasts the
+built structure; every rank searches the queries of one work-balanced range of
+original indices and its copy engines write that range's [K, rows] block
+straight into rank 0's result buffers over NVLink -- all inside every step);
+``value`` = N / max-over-ranks step time, ``shard`` reports every rank's stage
+times and bytes.  ``--mode weak``: every rank
 searches its own cloud -- replica ``rank`` of the configuration's
 distribution -- with no data-path collective; ``value`` = all ranks'
 queries / max-over-ranks step time.
