@@ -574,8 +574,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ---- exact re-rank ----------------------------------------------------------
 
-constexpr int kRerankWarps = 8;
+constexpr int kRerankWarps = 4;
 
+// Row stride of the staged candidate rows in shared memory, in floats: the
+// row plus 4 or 8 floats so that stride / 4 is odd, and the eight lanes of a
+// quarter warp, each reading 16 bytes at the same column of its own row, hit
+// distinct banks.
+__host__ __device__ inline int rerank_stride(int dp) { return dp + ((dp & 4) ? 8 : 4); }
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem) : "memory");
+}
+
+// One warp per query, one lane per candidate.  The candidates' fp32 rows are
+// random reads (512 bytes at D = 128); each pass of 32 candidates first
+// stages all 32 rows in shared memory, every row copied by the warp as one
+// coalesced run of 16-byte cp.async copies, so a warp has the whole pass's
+// rows in flight at once and holds no registers for them; then each lane
+// runs its candidate's chain from shared memory.
 template <int LCAP>
 __global__ void __launch_bounds__(kRerankWarps * 32)
     rerank_kernel(const float* __restrict__ rows32, int dim, int dp, const int* __restrict__ lists,
@@ -583,8 +600,11 @@ __global__ void __launch_bounds__(kRerankWarps * 32)
                   float* __restrict__ odist, int q0, int q1, const float* __restrict__ qrows32) {
     extern __shared__ unsigned long long rsmem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int stride = rerank_stride(dp);
     unsigned long long* keys = rsmem + (size_t)warp * LCAP;
-    float* qrow = reinterpret_cast<float*>(rsmem + (size_t)kRerankWarps * LCAP) + (size_t)warp * dp;
+    float* fbase = reinterpret_cast<float*>(rsmem + (size_t)kRerankWarps * LCAP);
+    float* qrow = fbase + (size_t)warp * dp;
+    float* stage = fbase + (size_t)kRerankWarps * dp + (size_t)warp * 32 * stride;
     const bool d3 = dp == 4 && dim == 3;
     const int q = q0 + blockIdx.x * kRerankWarps + warp;
     if (q >= q1) return;
@@ -592,35 +612,44 @@ __global__ void __launch_bounds__(kRerankWarps * 32)
     if (cnt > cap) return;  // searched by the fallback
     const float* qsrc = qrows32 + (size_t)q * dp;  // the query's own fp32 row
     for (int d = lane; d < dp; d += 32) qrow[d] = __ldg(&qsrc[d]);
-    __syncwarp();
     const int* mine = lists + (size_t)q * cap;
+    const float4* q4 = reinterpret_cast<const float4*>(qrow);
+    const int nv = dp / 4;
     unsigned long long thr = make_key(r2, 0);
     int nl = 0;
     for (int base = 0; base < cnt; base += 32) {
         const int j = base + lane;
+        const int nrow = min(32, cnt - base);
+        const int p = j < cnt ? __ldg(&mine[j]) : 0;
+        for (int r = 0; r < nrow; ++r) {
+            const int pr = __shfl_sync(0xffffffffu, p, r);
+            for (int c = lane; c < nv; c += 32)
+                cp_async16(stage + r * stride + 4 * c, rows32 + (size_t)pr * dp + 4 * c);
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncwarp();
         unsigned long long key = ~0ull;
         bool acc = false;
         if (j < cnt) {
-            const int p = __ldg(&mine[j]);
-            const float4* prow = reinterpret_cast<const float4*>(rows32 + (size_t)p * dp);
-            const float4* q4 = reinterpret_cast<const float4*>(qrow);
+            const float4* prow = reinterpret_cast<const float4*>(stage + lane * stride);
             float d2 = 0.0f;
             if (d3) {
-                const float4 pv = __ldg(&prow[0]);
+                const float4 pv = prow[0];
                 const float4 qv = q4[0];
                 d2 = dist2_d3(qv.x, qv.y, qv.z, pv.x, pv.y, pv.z);
-            } else
-            for (int v = 0; v < dp / 4; ++v) {
-                const float4 pv = __ldg(&prow[v]);
-                const float4 qv = q4[v];
-                float df = qv.x - pv.x;
-                d2 = __fmaf_rn(df, df, d2);
-                df = qv.y - pv.y;
-                d2 = __fmaf_rn(df, df, d2);
-                df = qv.z - pv.z;
-                d2 = __fmaf_rn(df, df, d2);
-                df = qv.w - pv.w;
-                d2 = __fmaf_rn(df, df, d2);
+            } else {
+                for (int v = 0; v < nv; ++v) {
+                    const float4 pv = prow[v];
+                    const float4 qv = q4[v];
+                    float df = qv.x - pv.x;
+                    d2 = __fmaf_rn(df, df, d2);
+                    df = qv.y - pv.y;
+                    d2 = __fmaf_rn(df, df, d2);
+                    df = qv.z - pv.z;
+                    d2 = __fmaf_rn(df, df, d2);
+                    df = qv.w - pv.w;
+                    d2 = __fmaf_rn(df, df, d2);
+                }
             }
             key = make_key(d2, p);
             acc = d2 < r2 && key < thr;
@@ -628,7 +657,7 @@ __global__ void __launch_bounds__(kRerankWarps * 32)
         const unsigned m = __ballot_sync(0xffffffffu, acc);
         if (acc) keys[nl + __popc(m & ((1u << lane) - 1u))] = key;
         nl += __popc(m);
-        __syncwarp();
+        __syncwarp();  // every lane is done with the staged rows and the list
         if (nl > LCAP - 32) {
             thr = coop::compact_list(keys, nl, K);
             nl = K;
@@ -642,7 +671,7 @@ template <int LCAP>
 cudaError_t launch_rerank(const float* rows32, int dim, int dp, const int* lists, const int* counts, int cap,
                           int K, float r2, int* oidx, float* odist, int q0, int q1, cudaStream_t s,
                           const float* qrows32) {
-    const size_t smem = (size_t)kRerankWarps * (LCAP * 8 + dp * 4);
+    const size_t smem = (size_t)kRerankWarps * (LCAP * 8 + dp * 4 + 32 * rerank_stride(dp) * 4);
     cudaError_t e = cudaFuncSetAttribute(rerank_kernel<LCAP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
