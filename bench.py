@@ -206,14 +206,23 @@ def config_dict(c, N: int, r: float, K: int | None = None) -> dict:
             "l2": "flushed before every timed step"}
 
 
-def search_roofline(N: int, D: int, K: int, cells: int, path: str, ms: float) -> dict:
+def tc_filter_flops(N: int, D: int, symmetric: bool) -> float:
+    """Flops the tensor-core filter must do: 2D per (query, point) pair, over
+    all N^2 pairs, or over the N(N+1)/2 unordered pairs when a whole
+    self-search filters each pair of tiles once (FRNN_OPT_TC_SYMMETRIC, the
+    default; a sharded search filters its query tiles against all points)."""
+    return float(N) * (N + 1) * D if symmetric else 2.0 * N * N * D
+
+
+def search_roofline(N: int, D: int, K: int, cells: int, path: str, ms: float,
+                    symmetric: bool = False) -> dict:
     """Whole-search roofline: the compulsory bytes B_alg = 4N(3D + 4 + 2K) + 12C
-    of a grid search against HBM, or the 2N^2 D flops of the tensor-core
-    filter against the sustained bf16 peak."""
+    of a grid search against HBM, or the tensor-core filter's flops
+    (tc_filter_flops) against the sustained bf16 peak."""
     hbm, _, bf16_sus, src = measured_peaks()
     t = ms / 1e3
     if path == "brute_tc":
-        f = 2.0 * N * N * D
+        f = tc_filter_flops(N, D, symmetric)
         return {"bound": "tensor", "alg_flops": f, "achieved": f / t / 1e12, "peak": bf16_sus,
                 "unit": "TFLOP/s", "frac": f / t / 1e12 / bf16_sus, "peak_source": src + " (bf16 sustained)"}
     b = 4 * N * (3 * D + 4 + 2 * K) + 12 * cells
@@ -246,7 +255,8 @@ def per_config_engine(torch, dev, flush, steps: int = 5, warmup: int = 3) -> dic
         med = statistics.median(ms)
         out[f"cfg{cfg}"] = {"workload": c.name, "steps": n, "ms_median": med, "ms": ms,
                             "queries_per_s": c.N / (med / 1e3), "stage_ms": stage_ms, "plan": plan,
-                            "roofline": search_roofline(c.N, c.D, c.K, plan["cells"], plan["path"], med)}
+                            "roofline": search_roofline(c.N, c.D, c.K, plan["cells"], plan["path"], med,
+                                                        symmetric=True)}
         del eng, x
         torch.cuda.empty_cache()
     return out
@@ -487,8 +497,9 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
             # writes K results
             "tc_prep": N * D * 4 + N * ((D + 63) // 64 * 64) * 2 + N * ((D + 3) // 4 * 4) * 4 + 8 * N,
             "tc_rerank": N * c.target * (((D + 3) // 4 * 4) * 4 + 4) + N * K * 8,
-            # the filter is a dense contraction: 2*N*N*D flops (below)
-            "tc_filter": 2.0 * N * N * D,
+            # the filter is a dense contraction over every pair, or over every
+            # unordered pair once in a whole self-search (tc_filter_flops)
+            "tc_filter": tc_filter_flops(N, D, not strong),
         }[dom]
         if dom in ("search", "collect", "emit", "tc_rerank", "tc_filter", "brute", "unpermute"):
             alg *= qf

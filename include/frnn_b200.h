@@ -206,7 +206,15 @@ enum frnn_option {
      * separates the box from the build and the search; 0 reads the box back
      * and plans on the host, as the reference does (frnn_engine.cu:64-86,
      * 142-156).  Results are the same either way.  No reference counterpart. */
-    FRNN_OPT_DEVICE_PLAN = 5
+    FRNN_OPT_DEVICE_PLAN = 5,
+    /* Whole self-searches on the tensor-core path: 1 (default) filters each
+     * unordered pair of 128-point tiles once and appends every passing pair
+     * to both points' candidate lists (the distance is symmetric), half the
+     * MMAs of the all-pairs filter; 0 filters every (query tile, point tile)
+     * pair, as the reference's brute force visits every pair
+     * (no_grid_frnn.cu:121-326).  Results are the same either way.  No
+     * reference counterpart. */
+    FRNN_OPT_TC_SYMMETRIC = 6
 };
 enum frnn_test_stall {
     FRNN_TEST_STALL_OFF = 0,

@@ -358,12 +358,59 @@ __device__ __forceinline__ void filter_chunk(const uint32_t (&acc)[32], const fl
     }
 }
 
+// The same for a symmetric search (a self-search that filters each pair of
+// tiles once): the query's appends take their slots from the global counter
+// counts[q], and with `both` (a tile off the diagonal) every passing column p
+// also gets q appended to its own list, the pair seen from p's side.  The
+// threshold test is symmetric in q and p (n_q + n_p - 2 q.p against margins
+// that add a term of each), so one test decides both lists.  Padding rows and
+// columns carry +inf terms and never pass.
+__device__ __forceinline__ void filter_chunk_sym(const uint32_t (&acc)[32], const float (&b)[32], float a,
+                                                 int* __restrict__ counts, int* __restrict__ lists, int q, int cap,
+                                                 int col0, bool both) {
+    float m[4];
+    group_max(acc, b, m);
+    if (fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])) > a) {
+        uint32_t mask = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if (m[j] > a) {
+#pragma unroll
+                for (int i = 8 * j; i < 8 * j + 8; ++i)
+                    mask |= (__uint_as_float(acc[i]) - b[i] > a ? 1u : 0u) << i;
+            }
+        }
+        if (mask == 0) return;
+        int slot = atomicAdd(&counts[q], __popc(mask));
+        int* dst = lists + (size_t)q * cap;
+        while (mask) {
+            const int i = __ffs(mask) - 1;
+            mask &= mask - 1;
+            if (slot < cap) dst[slot] = col0 + i;
+            ++slot;
+            if (both) {
+                const int p = col0 + i;
+                const int ps = atomicAdd(&counts[p], 1);
+                if (ps < cap) lists[(size_t)p * cap + ps] = q;
+            }
+        }
+    }
+}
+
+// sym (a whole self-search only): the CTA of query blocks qb0, qb0 + 1 filters
+// point tiles t >= qb0 only -- each unordered pair of tiles once, so half the
+// MMAs -- block qb0 + 1 skipping tile qb0 (its transpose, tile qb0 + 1 of
+// block qb0, is filtered); tiles off a block's diagonal append each passing
+// pair to both lists.  counts[] must be zero on entry and is final only when
+// the kernel has finished (appends come from every CTA), so the overflow
+// list is made afterwards by sym_overflow_kernel.  CTA 0 has the most tiles
+// and starts first.
 template <int KC>
 __global__ void __launch_bounds__(kThreads, 1)
     filter_kernel(const uint8_t* __restrict__ tiles, const float* __restrict__ qa, const float* __restrict__ pb,
                   int n, int ntiles, int cap, int* __restrict__ lists, int* __restrict__ counts,
                   int* __restrict__ overflow, int* __restrict__ n_overflow, int* __restrict__ err,
-                  int qb_begin, int qb_end, const uint8_t* __restrict__ qtiles, int skip_tile) {
+                  int qb_begin, int qb_end, const uint8_t* __restrict__ qtiles, int skip_tile, int sym) {
     // qtiles: the query blocks' tiles (the points' own tiles for a self-query)
     using C = Cfg<KC>;
     constexpr int S = C::kStages;
@@ -394,6 +441,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int qb0 = qb_begin + 2 * blockIdx.x;
     const bool has1 = qb0 + 1 < qb_end;
     const int qb1 = has1 ? qb0 + 1 : qb0;
+    // the point tiles filtered: t0 + i for i < ntl
+    const int t0 = sym ? qb0 : 0;
+    const int ntl = ntiles - t0;
 
     if (threadIdx.x < 2 * kRows) qcnt[threadIdx.x] = 0;
     if (threadIdx.x == 0) {
@@ -433,9 +483,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             bulk_g2s(sA, qtiles + (size_t)qb0 * TB, TB, afull);
             if (has1) bulk_g2s(sA + TB, qtiles + (size_t)qb1 * TB, TB, afull);
             int issued = 0;
-            for (int t = 0; t < ntiles; ++t) {
-                const int s = t % S;
-                const uint32_t u = (uint32_t)(t / S);
+            for (int i = 0; i < ntl; ++i) {
+                const int t = t0 + i, s = i % S;
+                const uint32_t u = (uint32_t)(i / S);
                 if (!mbar_wait(empty(s), (u & 1u) ^ 1u, abort_flag)) {
                     give_up();
                     break;
@@ -446,20 +496,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_expect_tx(full(s), TB);
                     bulk_g2s(sB + (uint32_t)s * TB, tiles + (size_t)t * TB, TB, full(s));
                 }
-                issued = t + 1;
+                issued = i + 1;
             }
             // copies still in flight land before the CTA may exit
             drain_wait(afull, 0);
-            for (int t = issued - S < 0 ? 0 : issued - S; t < issued; ++t)
-                if (t != skip_tile) drain_wait(full(t % S), (uint32_t)(t / S) & 1u);
+            for (int i = issued - S < 0 ? 0 : issued - S; i < issued; ++i)
+                if (t0 + i != skip_tile) drain_wait(full(i % S), (uint32_t)(i / S) & 1u);
         }
     } else if (warp == kMmaWarp) {
         if (lane == 0) {
             bool ok = mbar_wait(afull, 0, abort_flag);
             if (!ok) give_up();
-            for (int t = 0; ok && t < ntiles; ++t) {
-                const int s = t % S, b = t & 1;
-                const uint32_t u = (uint32_t)(t / S), v = (uint32_t)(t >> 1);
+            for (int i = 0; ok && i < ntl; ++i) {
+                const int t = t0 + i, s = i % S, b = i & 1;
+                const uint32_t u = (uint32_t)(i / S), v = (uint32_t)(i >> 1);
                 if (!mbar_wait(full(s), u & 1u, abort_flag) || !mbar_wait(tempty(b), (v & 1u) ^ 1u, abort_flag)) {
                     give_up();
                     break;
@@ -467,6 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 fence_after();
                 const uint32_t bstage = sB + (uint32_t)s * TB;
                 for (int a = 0; a < (has1 ? 2 : 1); ++a) {
+                    if (sym && a == 1 && t < qb1) continue;  // the transpose of a pair filtered by block 0
                     const uint32_t d = tmem + (uint32_t)((a * 2 + b) * kRows);
                     const uint32_t astage = sA + (uint32_t)a * TB;
 #pragma unroll
@@ -499,9 +550,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float* src = pb + (size_t)t * kRows + h * kCols + lane;
             return t < ntiles ? make_float2(__ldg(src), __ldg(src + 32)) : make_float2(0.0f, 0.0f);
         };
-        float2 terms = load_terms(g);
-        for (int t = g; t < ntiles; t += 2) {
-            const uint32_t v = (uint32_t)(t >> 1);
+        float2 terms = load_terms(t0 + g);
+        for (int i = g; i < ntl; i += 2) {
+            const int t = t0 + i;
+            const uint32_t v = (uint32_t)(i >> 1);
             // warp-uniform outcome: the TMEM loads below need the whole warp
             if (!__all_sync(0xffffffffu, mbar_wait(tfull(g), v & 1u, abort_flag))) {
                 if (lane == 0) give_up();
@@ -526,7 +578,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     bq[4 * i + 2] = bb.z;
                     bq[4 * i + 3] = bb.w;
                 }
-                if (kEpiWarps == 8) {
+                if (sym) {
+#pragma unroll 1
+                    for (int a = 0; a < (has1 ? 2 : 1); ++a) {
+                        const int qb = a ? qb1 : qb0;
+                        if (t < qb) continue;  // block 1 at tile qb0: filtered as its transpose
+                        uint32_t acc[32];
+                        __syncwarp();
+                        tmem_ld32(tmem + lane_base + (uint32_t)((2 * a + g) * kRows + c * 32), acc);
+                        tmem_wait_ld();
+                        filter_chunk_sym(acc, bq, a ? aq1 : aq0, counts, lists, a ? q1 : q0, cap,
+                                         t * kRows + c * 32, t != qb);
+                    }
+                } else if (kEpiWarps == 8) {
                     // both blocks' loads in flight before one wait
                     uint32_t acc0[32], acc1[32];
                     __syncwarp();
@@ -556,7 +620,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     fence_before();
     __syncthreads();
-    if (threadIdx.x < 2 * kRows) {
+    if (!sym && threadIdx.x < 2 * kRows) {
         const int a = threadIdx.x / kRows, row = threadIdx.x % kRows;
         const int q = (a ? qb1 : qb0) * kRows + row;
         if ((a == 0 || has1) && q < n) {
@@ -570,6 +634,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
                      : "memory");
     }
+}
+
+// After a symmetric filter: the queries whose candidates overflowed their list.
+__global__ void __launch_bounds__(256) sym_overflow_kernel(const int* __restrict__ counts, int n, int cap,
+                                                           int* __restrict__ overflow,
+                                                           int* __restrict__ n_overflow) {
+    const int q = blockIdx.x * blockDim.x + threadIdx.x;
+    if (q < n && __ldg(&counts[q]) > cap) overflow[atomicAdd(n_overflow, 1)] = q;
 }
 
 // ---- exact re-rank ----------------------------------------------------------
@@ -684,7 +756,8 @@ cudaError_t launch_rerank(const float* rows32, int dim, int dp, const int* lists
 template <int KC>
 cudaError_t launch_filter_kc(const uint8_t* tiles, const float* qa, const float* pb, int n, int ntiles,
                              int cap, int* lists, int* counts, int* overflow, int* n_overflow, int* err,
-                             int qb_begin, int qb_end, cudaStream_t s, const uint8_t* qtiles, int skip_tile) {
+                             int qb_begin, int qb_end, cudaStream_t s, const uint8_t* qtiles, int skip_tile,
+                             int sym) {
     const size_t smem = Cfg<KC>::kSmem;
     cudaError_t e =
         cudaFuncSetAttribute(filter_kernel<KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -692,7 +765,9 @@ cudaError_t launch_filter_kc(const uint8_t* tiles, const float* qa, const float*
     if (qb_end <= qb_begin) return cudaSuccess;
     filter_kernel<KC><<<(qb_end - qb_begin + 1) / 2, kThreads, smem, s>>>(
         tiles, qa, pb, n, ntiles, cap, lists, counts, overflow, n_overflow, err, qb_begin, qb_end, qtiles,
-        skip_tile);
+        skip_tile, sym);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if (sym) sym_overflow_kernel<<<(n + 255) / 256, 256, 0, s>>>(counts, n, cap, overflow, n_overflow);
     return cudaGetLastError();
 }
 
@@ -725,19 +800,21 @@ cudaError_t launch_tc_prep(const float* pts, int n, int dim, const float* center
 cudaError_t launch_tc_filter(const uint8_t* tiles, const float* qa, const float* pb, int n, int dim,
                              int cap, int* lists, int* counts, int* overflow, int* n_overflow, int* err,
                              int qb_begin, int qb_end, cudaStream_t s, const uint8_t* qtiles, int m,
-                             int skip_tile) {
+                             int skip_tile, bool sym) {
     const int ntiles = (n + tc::kRows - 1) / tc::kRows;
     const int qtiles_n = qtiles ? (m + tc::kRows - 1) / tc::kRows : ntiles;
     if (qb_begin < 0 || qb_end > qtiles_n) return cudaErrorInvalidValue;
+    // symmetric filtering: a whole self-search only
+    if (sym && (qtiles || qb_begin != 0 || qb_end != ntiles)) return cudaErrorInvalidValue;
     if (!qtiles) {
         qtiles = tiles;
         m = n;
     }
     if (tc_kc(dim) == 1)
         return tc::launch_filter_kc<1>(tiles, qa, pb, m, ntiles, cap, lists, counts, overflow, n_overflow, err,
-                                       qb_begin, qb_end, s, qtiles, skip_tile);
+                                       qb_begin, qb_end, s, qtiles, skip_tile, sym ? 1 : 0);
     return tc::launch_filter_kc<2>(tiles, qa, pb, m, ntiles, cap, lists, counts, overflow, n_overflow, err,
-                                   qb_begin, qb_end, s, qtiles, skip_tile);
+                                   qb_begin, qb_end, s, qtiles, skip_tile, sym ? 1 : 0);
 }
 
 cudaError_t launch_tc_rerank(const float* rows32, int dim, const int* lists, const int* counts, int cap,

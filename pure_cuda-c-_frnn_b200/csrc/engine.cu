@@ -825,12 +825,16 @@ int tc_query_tiles(frnn_engine* e, const float* d_pts, int N, int dim, int K, fl
     const int q0 = qb_begin * 128, q1 = std::min(Q, qb_end * 128), rows = q1 - q0;
     FRNN_CHECK(e, cudaMemsetAsync(e->n_overflow.p, 0, 4, s), "memset overflow count");
     e->last_overflow_map = 2;
+    // a whole self-search filters each unordered pair of tiles once (half the
+    // MMAs); its candidate counts are global counters, zeroed here
+    const bool sym = !sep && e->tc_symmetric && qb_begin == 0 && qb_end == (N + 127) / 128;
+    if (sym) FRNN_CHECK(e, cudaMemsetAsync(e->list_counts.p, 0, (size_t)Q * 4, s), "memset candidate counts");
     stage_begin(e, ST_TC_FILTER);
     FRNN_CHECK(e, launch_tc_filter(e->tc_tiles.as<uint8_t>(), qa, e->tc_pb.as<float>(), N, dim, cap,
                                    e->lists.as<int>(), e->list_counts.as<int>(), e->overflow.as<int>(),
                                    e->n_overflow.as<int>(), e->err_flag.as<int>(), qb_begin, qb_end, s,
                                    sep ? e->q_tiles.as<uint8_t>() : nullptr, Q,
-                                   e->test_stall == FRNN_TEST_STALL_TC_FILTER ? 1 : -1),
+                                   e->test_stall == FRNN_TEST_STALL_TC_FILTER ? 1 : -1, sym),
                "filter launch");
     stage_end(e, ST_TC_FILTER);
     stage_begin(e, ST_TC_RERANK);
@@ -1472,6 +1476,10 @@ int frnn_set_option(frnn_engine* e, int option, int64_t value) {
             if (value < FRNN_TEST_STALL_OFF || value > FRNN_TEST_STALL_TC_FILTER)
                 return fail(e, FRNN_ERR_INVALID_ARG, "test stall must be OFF, SCAN or TC_FILTER");
             e->test_stall = (int)value;
+            return FRNN_OK;
+        case FRNN_OPT_TC_SYMMETRIC:
+            if (value < 0 || value > 1) return fail(e, FRNN_ERR_INVALID_ARG, "tc symmetric must be 0 or 1");
+            e->tc_symmetric = (int)value;
             return FRNN_OK;
         case FRNN_OPT_DEVICE_PLAN:
             if (value < 0 || value > 1) return fail(e, FRNN_ERR_INVALID_ARG, "device plan must be 0 or 1");

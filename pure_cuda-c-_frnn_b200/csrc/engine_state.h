@@ -57,6 +57,7 @@ struct frnn_engine {
     int list_search = 0;      // FRNN_OPT_LIST_SEARCH
     int test_stall = 0;       // FRNN_OPT_TEST_STALL (tests of the timeout path)
     int device_plan = 1;      // FRNN_OPT_DEVICE_PLAN
+    int tc_symmetric = 1;     // FRNN_OPT_TC_SYMMETRIC
     // device-planned grids: the plan (written by the bounding-box kernel) and
     // its pinned host copy
     frnn::eng::DevBuf dplan;

@@ -148,10 +148,13 @@ cudaError_t launch_tc_prep(const float* pts, int n, int dim, const float* center
 // holds its terms), searched against the n points of tiles / pb
 // skip_tile >= 0: the producer never copies that point tile, so the MMA
 // thread's bounded wait for it gives up (tests of the timeout path only)
+// sym (a whole self-search: no qtiles, every query tile): each unordered pair
+// of tiles is filtered once and every passing pair goes to both lists; counts
+// must be zero on entry.
 cudaError_t launch_tc_filter(const uint8_t* tiles, const float* qa, const float* pb, int n, int dim,
                              int cap, int* lists, int* counts, int* overflow, int* n_overflow, int* err,
                              int qb_begin, int qb_end, cudaStream_t s, const uint8_t* qtiles = nullptr,
-                             int m = 0, int skip_tile = -1);
+                             int m = 0, int skip_tile = -1, bool sym = false);
 // exact results for the queries q in [q0, q1) with counts[q] <= cap, to row
 // q - q0 of out[k*(q1-q0) + row]
 // qrows32 (optional): the separate query set's fp32 rows (n = its size)

@@ -284,6 +284,7 @@ class FRNNEngine:
     OPT_LIST_SEARCH = 3
     OPT_TEST_STALL = 4
     OPT_DEVICE_PLAN = 5
+    OPT_TC_SYMMETRIC = 6
     TEST_STALL_OFF, TEST_STALL_SCAN, TEST_STALL_TC_FILTER = 0, 1, 2
     GRID_AXES_AUTO, GRID_AXES_LEADING, GRID_AXES_PRINCIPAL = 0, 1, 2
     LIST_SEARCH_AUTO, LIST_SEARCH_ALWAYS, LIST_SEARCH_NEVER = 0, 1, 2
