@@ -310,7 +310,15 @@ enum frnn_shard_option {
     FRNN_SHARD_OPT_CHUNKS = 1,
     /* 1: the gather's stream gets the device's highest priority; 0 (default)
      * normal priority. */
-    FRNN_SHARD_OPT_COMM_PRIORITY = 2
+    FRNN_SHARD_OPT_COMM_PRIORITY = 2,
+    /* Tensor-core path with 2..8 ranks: 1 (default) shares the symmetric
+     * filter (each unordered pair of tiles once; rank r filters its query
+     * blocks against the tiles at or above them and keeps every passing
+     * pair, then pulls the entries the other ranks listed for its own
+     * queries over NVLink); 0 filters each rank's query tiles against every
+     * point tile.  Results are the same either way.  No reference
+     * counterpart. */
+    FRNN_SHARD_OPT_TC_SYMMETRIC = 3
 };
 int frnn_shard_set_option(frnn_shard* sh, int option, int64_t value);
 

@@ -404,7 +404,9 @@ __device__ __forceinline__ void filter_chunk_sym(const uint32_t (&acc)[32], cons
 // pair to both lists.  counts[] must be zero on entry and is final only when
 // the kernel has finished (appends come from every CTA), so the overflow
 // list is made afterwards by sym_overflow_kernel.  CTA 0 has the most tiles
-// and starts first.
+// and starts first.  In a sharded search the CTAs cover this rank's query
+// blocks [qb_begin, qb_end) and the pairs seen from points other ranks own
+// stay in this rank's lists until those ranks pull them (tc_pull_kernel).
 template <int KC>
 __global__ void __launch_bounds__(kThreads, 1)
     filter_kernel(const uint8_t* __restrict__ tiles, const float* __restrict__ qa, const float* __restrict__ pb,
@@ -636,12 +638,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// A sharded symmetric filter leaves the pairs seen from a point in the lists
+// of the rank that filtered them.  One warp per query q of this rank's range
+// [q0, q1): from every other rank, its count for q and that many list entries
+// (plain loads from memory mapped through CUDA IPC, a warp's entries
+// contiguous), appended to q's own list.  A source list that overflowed its
+// capacity carries a count above cap, so q's merged count does too and q
+// goes to the overflow fallback.
+__global__ void __launch_bounds__(256) tc_pull_kernel(const TcPeers peers, int self, int* __restrict__ counts,
+                                                      int* __restrict__ lists, int q0, int q1, int cap) {
+    const int lane = threadIdx.x & 31;
+    const int q = q0 + (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+    if (q >= q1) return;
+    for (int r = 0; r < peers.n; ++r) {
+        if (r == self) continue;
+        const int c = peers.counts[r][q];
+        if (c == 0) continue;
+        int base = 0;
+        if (lane == 0) base = atomicAdd(&counts[q], c);
+        base = __shfl_sync(0xffffffffu, base, 0);
+        const int* src = peers.lists[r] + (size_t)q * cap;
+        int* dst = lists + (size_t)q * cap;
+        for (int j = lane; j < min(c, cap); j += 32)
+            if (base + j < cap) dst[base + j] = src[j];
+    }
+}
+
 // After a symmetric filter: the queries whose candidates overflowed their list.
-__global__ void __launch_bounds__(256) sym_overflow_kernel(const int* __restrict__ counts, int n, int cap,
+__global__ void __launch_bounds__(256) sym_overflow_kernel(const int* __restrict__ counts, int q0, int q1, int cap,
                                                            int* __restrict__ overflow,
                                                            int* __restrict__ n_overflow) {
-    const int q = blockIdx.x * blockDim.x + threadIdx.x;
-    if (q < n && __ldg(&counts[q]) > cap) overflow[atomicAdd(n_overflow, 1)] = q;
+    const int q = q0 + blockIdx.x * blockDim.x + threadIdx.x;
+    if (q < q1 && __ldg(&counts[q]) > cap) overflow[atomicAdd(n_overflow, 1)] = q;
 }
 
 // ---- exact re-rank ----------------------------------------------------------
@@ -757,7 +785,7 @@ template <int KC>
 cudaError_t launch_filter_kc(const uint8_t* tiles, const float* qa, const float* pb, int n, int ntiles,
                              int cap, int* lists, int* counts, int* overflow, int* n_overflow, int* err,
                              int qb_begin, int qb_end, cudaStream_t s, const uint8_t* qtiles, int skip_tile,
-                             int sym) {
+                             int sym, bool sym_part) {
     const size_t smem = Cfg<KC>::kSmem;
     cudaError_t e =
         cudaFuncSetAttribute(filter_kernel<KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -767,7 +795,9 @@ cudaError_t launch_filter_kc(const uint8_t* tiles, const float* qa, const float*
         tiles, qa, pb, n, ntiles, cap, lists, counts, overflow, n_overflow, err, qb_begin, qb_end, qtiles,
         skip_tile, sym);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    if (sym) sym_overflow_kernel<<<(n + 255) / 256, 256, 0, s>>>(counts, n, cap, overflow, n_overflow);
+    // a whole symmetric search lists its overflows here; a sharded one only
+    // once its queries' candidates from the other ranks are in (tc_pull)
+    if (sym && !sym_part) sym_overflow_kernel<<<(n + 255) / 256, 256, 0, s>>>(counts, 0, n, cap, overflow, n_overflow);
     return cudaGetLastError();
 }
 
@@ -800,21 +830,38 @@ cudaError_t launch_tc_prep(const float* pts, int n, int dim, const float* center
 cudaError_t launch_tc_filter(const uint8_t* tiles, const float* qa, const float* pb, int n, int dim,
                              int cap, int* lists, int* counts, int* overflow, int* n_overflow, int* err,
                              int qb_begin, int qb_end, cudaStream_t s, const uint8_t* qtiles, int m,
-                             int skip_tile, bool sym) {
+                             int skip_tile, bool sym, bool sym_part) {
     const int ntiles = (n + tc::kRows - 1) / tc::kRows;
     const int qtiles_n = qtiles ? (m + tc::kRows - 1) / tc::kRows : ntiles;
     if (qb_begin < 0 || qb_end > qtiles_n) return cudaErrorInvalidValue;
-    // symmetric filtering: a whole self-search only
-    if (sym && (qtiles || qb_begin != 0 || qb_end != ntiles)) return cudaErrorInvalidValue;
+    // symmetric filtering: a self-search; a part of one only when sharded
+    if (sym_part && !sym) return cudaErrorInvalidValue;
+    if (sym && (qtiles || (!sym_part && (qb_begin != 0 || qb_end != ntiles)))) return cudaErrorInvalidValue;
     if (!qtiles) {
         qtiles = tiles;
         m = n;
     }
     if (tc_kc(dim) == 1)
         return tc::launch_filter_kc<1>(tiles, qa, pb, m, ntiles, cap, lists, counts, overflow, n_overflow, err,
-                                       qb_begin, qb_end, s, qtiles, skip_tile, sym ? 1 : 0);
+                                       qb_begin, qb_end, s, qtiles, skip_tile, sym ? 1 : 0, sym_part);
     return tc::launch_filter_kc<2>(tiles, qa, pb, m, ntiles, cap, lists, counts, overflow, n_overflow, err,
-                                   qb_begin, qb_end, s, qtiles, skip_tile, sym ? 1 : 0);
+                                   qb_begin, qb_end, s, qtiles, skip_tile, sym ? 1 : 0, sym_part);
+}
+
+cudaError_t launch_tc_pull(const TcPeers& peers, int self, int* counts, int* lists, int q0, int q1, int cap,
+                           cudaStream_t s) {
+    if (q1 <= q0) return cudaSuccess;
+    if (peers.n < 1 || peers.n > kTcMaxPeers || self < 0 || self >= peers.n) return cudaErrorInvalidValue;
+    const long long threads = (long long)(q1 - q0) * 32;
+    tc::tc_pull_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(peers, self, counts, lists, q0, q1, cap);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_tc_sym_overflow(const int* counts, int q0, int q1, int cap, int* overflow, int* n_overflow,
+                                   cudaStream_t s) {
+    if (q1 <= q0) return cudaSuccess;
+    tc::sym_overflow_kernel<<<(q1 - q0 + 255) / 256, 256, 0, s>>>(counts, q0, q1, cap, overflow, n_overflow);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_tc_rerank(const float* rows32, int dim, const int* lists, const int* counts, int cap,

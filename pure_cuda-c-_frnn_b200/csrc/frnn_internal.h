@@ -131,6 +131,15 @@ cudaError_t launch_pca_estimate(const float* pts, int n, int dim, const float* p
                                 const float* h, int* counts, cudaStream_t s);
 
 // bf_tc.cu -- brute force with a tcgen05 distance filter, 33 <= dim <= 128.
+
+// The ranks of a sharded symmetric filter: every rank's candidate lists and
+// counters (this rank's own buffers, the others' mapped through CUDA IPC).
+constexpr int kTcMaxPeers = 8;
+struct TcPeers {
+    int n = 0;  // ranks
+    const int* counts[kTcMaxPeers] = {};
+    const int* lists[kTcMaxPeers] = {};
+};
 int tc_kc(int dim);                 // 64-dimension slabs per row (1 or 2)
 size_t tc_tile_bytes(int dim);      // bytes of one 128-row fp16 tile
 int tc_row_floats(int dim);         // floats per fp32 row (dim rounded up to 4)
@@ -148,13 +157,24 @@ cudaError_t launch_tc_prep(const float* pts, int n, int dim, const float* center
 // holds its terms), searched against the n points of tiles / pb
 // skip_tile >= 0: the producer never copies that point tile, so the MMA
 // thread's bounded wait for it gives up (tests of the timeout path only)
-// sym (a whole self-search: no qtiles, every query tile): each unordered pair
-// of tiles is filtered once and every passing pair goes to both lists; counts
-// must be zero on entry.
+// sym (a self-search, no qtiles): each unordered pair of tiles is filtered
+// once and every passing pair goes to both lists; counts must be zero on
+// entry.  Without sym_part the query tiles must be all of them, and the
+// overflow list is made at the end; with sym_part (a sharded search) the
+// query tiles are this rank's range, the pairs seen from other ranks' points
+// stay in this rank's lists for those ranks to pull (launch_tc_pull), and
+// launch_tc_sym_overflow makes the list after the pull.
 cudaError_t launch_tc_filter(const uint8_t* tiles, const float* qa, const float* pb, int n, int dim,
                              int cap, int* lists, int* counts, int* overflow, int* n_overflow, int* err,
                              int qb_begin, int qb_end, cudaStream_t s, const uint8_t* qtiles = nullptr,
-                             int m = 0, int skip_tile = -1, bool sym = false);
+                             int m = 0, int skip_tile = -1, bool sym = false, bool sym_part = false);
+// After every rank's symmetric filter: the entries the other ranks listed for
+// this rank's queries [q0, q1), appended to their own lists
+cudaError_t launch_tc_pull(const TcPeers& peers, int self, int* counts, int* lists, int q0, int q1, int cap,
+                           cudaStream_t s);
+// overflow[0..*n_overflow) = the queries q in [q0, q1) with counts[q] > cap
+cudaError_t launch_tc_sym_overflow(const int* counts, int q0, int q1, int cap, int* overflow, int* n_overflow,
+                                   cudaStream_t s);
 // exact results for the queries q in [q0, q1) with counts[q] <= cap, to row
 // q - q0 of out[k*(q1-q0) + row]
 // qrows32 (optional): the separate query set's fp32 rows (n = its size)

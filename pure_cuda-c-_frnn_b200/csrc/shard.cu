@@ -25,6 +25,12 @@
 //      prepares its own fp16 tiles from it);
 //   4. every rank searches its queries in cell order (the grid path lists
 //      their sorted positions with a scan), writing rows in original order;
+//      on the tensor-core path the ranks share the symmetric filter (each
+//      unordered pair of tiles once): rank r filters its query blocks
+//      against the tiles at or above them, keeping every passing pair, from
+//      either side, in its own lists; after a barrier each rank pulls the
+//      entries the other ranks listed for its queries (plain loads from
+//      their lists, mapped through CUDA IPC) and re-ranks its own queries;
 //   5. each rank's block goes straight into the root's result buffers with
 //      a 2-D copy over NVLink on a copy engine (the root's buffers are mapped
 //      through CUDA IPC); no SM takes part in the gather, so with several
@@ -35,8 +41,9 @@
 // Every wait on the host is bounded (FRNN_ERR_TIMEOUT after the shard's
 // timeout; the communicator is then aborted and the shard unusable); an NCCL
 // error reported by the communicator ends the call with FRNN_ERR_COMM.
-// No kernel here touches another GPU's memory; the gather's writes to the
-// root are copy-engine copies.
+// Apart from the symmetric filter's pull (loads only), no kernel here touches
+// another GPU's memory; the gather's writes to the root are copy-engine
+// copies.
 #include <algorithm>
 #include <chrono>
 #include <cstring>
@@ -65,6 +72,7 @@ struct ShardHeader {
     int nparts;
     GridPlan P;
     TcPlan tc;
+    int tc_sym;          // the tensor-core filter is shared symmetrically
     cudaIpcMemHandle_t res_idx, res_dist;  // the root's result buffers
     int bounds[kMaxShardRanks + 1];  // rank r owns original query indices [bounds[r], bounds[r+1])
 };
@@ -126,6 +134,15 @@ struct frnn_shard {
     cudaIpcMemHandle_t open_h_idx{}, open_h_dist{};
     int* peer_idx = nullptr;
     float* peer_dist = nullptr;
+    // the symmetric tensor-core filter (FRNN_SHARD_OPT_TC_SYMMETRIC): every
+    // rank's candidate lists and counters, exchanged as IPC handles (slot r
+    // of the exchange buffer is rank r's) and mapped here
+    int tc_sym = 1;
+    DevBuf d_handles;
+    unsigned char* h_handles = nullptr;  // pinned
+    cudaIpcMemHandle_t open_lists[kTcMaxPeers]{}, open_counts[kTcMaxPeers]{};
+    int* peer_lists[kTcMaxPeers] = {};
+    int* peer_counts[kTcMaxPeers] = {};
     long long bcast_bytes = 0, gather_bytes = 0;
     int last_rows = 0, last_path = 0;
 };
@@ -254,6 +271,31 @@ __global__ void compact_kernel(const int* __restrict__ flags, const int* __restr
     if ((unsigned)p < (unsigned)cap) qlist[p] = sq;
 }
 
+// Owners' ranges for the symmetric tensor-core filter: query block b filters
+// the tiles t >= b, so block b costs T - b tiles, and its re-rank about
+// kRerankTiles more (B200, cfg5: 15.5 ms of re-rank for 7,813 blocks against
+// 177 ms of filter for 30.5M tiles); ranges are cut at even blocks (the
+// filter's CTAs take blocks in pairs) so that every rank gets an equal share.
+constexpr double kRerankTiles = 0.35;
+void tc_sym_bounds(int N, int parts, int* bounds) {
+    const long long T = (N + 127) / 128, pairs = (T + 1) / 2;
+    auto pair_work = [&](long long j) {
+        return (long double)((T - 2 * j) + (2 * j + 1 < T ? T - 2 * j - 1 + kRerankTiles : 0.0)) + kRerankTiles;
+    };
+    long double total = 0.0L;
+    for (long long j = 0; j < pairs; ++j) total += (long double)pair_work(j);
+    bounds[0] = 0;
+    long long j = 0;
+    long double before = 0.0L;
+    for (int r = 1; r < parts; ++r) {
+        const long double target = total * r / parts;
+        while (j < pairs && before + pair_work(j) <= target) before += (long double)pair_work(j++);
+        if (j < pairs && target - before > 0.5L * (long double)pair_work(j)) before += (long double)pair_work(j++);
+        bounds[r] = (int)std::min<long long>(N, j * 256);
+    }
+    bounds[parts] = N;
+}
+
 // Step 1 on the root: plan, build and the owners' ranges into h_hdr.
 int root_plan(frnn_shard* sh, const float* d_pts, int N, int dim, int K, float radius) {
     frnn_engine* e = sh->e;
@@ -300,9 +342,14 @@ int root_plan(frnn_shard* sh, const float* d_pts, int N, int dim, int K, float r
                 return fail(e, FRNN_ERR_INVALID_ARG, "partition failed");
         }
     } else if (H.path == FRNN_PATH_BRUTE_TC) {
-        // whole 128-query tiles; every query costs the same
-        const int ntq = (N + 127) / 128;
-        for (int r = 0; r <= parts; ++r) H.bounds[r] = std::min(N, (int)((long long)ntq * r / parts) * 128);
+        H.tc_sym = sh->tc_sym && e->tc_symmetric && parts > 1 && parts <= kTcMaxPeers ? 1 : 0;
+        if (H.tc_sym) {
+            tc_sym_bounds(N, parts, H.bounds);
+        } else {
+            // whole 128-query tiles; every query costs the same
+            const int ntq = (N + 127) / 128;
+            for (int r = 0; r <= parts; ++r) H.bounds[r] = std::min(N, (int)((long long)ntq * r / parts) * 128);
+        }
     }
     // the results land in these buffers, on this GPU and (mapped) on the others
     FRNN_GROW(e, sh->res_idx, (size_t)N * K * 4);
@@ -367,6 +414,129 @@ int range_queries(frnn_shard* sh, const int* ids, int N, int lo, int hi, int* ql
     compact_kernel<<<(N + 255) / 256, 256, 0, s>>>(sh->flags.as<int>(), sh->fpos.as<int>(), N, hi - lo, qlist);
     FRNN_CHECK(e, cudaGetLastError(), "compact launch");
     e->launches += 3;
+    return FRNN_OK;
+}
+
+// The symmetric filter's set-up, on every rank: its candidate lists (all N
+// points: pairs seen from any point it owns may come from other ranks) and
+// counters, zeroed; every rank's IPC handles of both, exchanged with one
+// all-reduce (MAX over bytes, every rank filling its own slot) and mapped;
+// then an all-reduce of the ranks' status, so that every rank stops together
+// when one cannot take part.
+int tc_sym_setup(frnn_shard* sh, const ShardHeader& H, int cap) {
+    frnn_engine* e = sh->e;
+    cudaStream_t s = e->stream;
+    const NcclApi* api = nccl_api();
+    const size_t slot = 2 * sizeof(cudaIpcMemHandle_t), nbytes = slot * (size_t)sh->nranks;
+    int local = FRNN_OK;
+    if ((local = grow(e, e->lists, (size_t)H.N * cap * 4, "lists")) == FRNN_OK &&
+        (local = grow(e, e->list_counts, (size_t)H.N * 4, "list_counts")) == FRNN_OK &&
+        (local = grow(e, e->overflow, (size_t)H.N * 4, "overflow")) == FRNN_OK &&
+        (local = grow(e, e->n_overflow, 16, "n_overflow")) == FRNN_OK)
+        local = grow(e, sh->d_handles, slot * kTcMaxPeers, "handles");
+    std::memset(sh->h_handles, 0, slot * kTcMaxPeers);
+    if (local == FRNN_OK) {
+        cudaIpcMemHandle_t* mine = reinterpret_cast<cudaIpcMemHandle_t*>(sh->h_handles + slot * sh->rank);
+        if (cudaMemsetAsync(e->list_counts.p, 0, (size_t)H.N * 4, s) != cudaSuccess ||
+            cudaMemsetAsync(e->n_overflow.p, 0, 4, s) != cudaSuccess ||
+            cudaIpcGetMemHandle(&mine[0], e->lists.p) != cudaSuccess ||
+            cudaIpcGetMemHandle(&mine[1], e->list_counts.p) != cudaSuccess)
+            local = cuda_fail(e, cudaGetLastError(), "symmetric filter set-up");
+    }
+    if (sh->d_handles.p == nullptr) return local;  // cannot take part in the exchange at all
+    FRNN_CHECK(e, cudaMemcpyAsync(sh->d_handles.p, sh->h_handles, nbytes, cudaMemcpyHostToDevice, s), "handles upload");
+    SH_NCCL(sh, api->AllReduce(sh->d_handles.p, sh->d_handles.p, nbytes, ncclUint8, ncclMax, sh->comm, s),
+            "handle exchange");
+    FRNN_CHECK(e, cudaMemcpyAsync(sh->h_handles, sh->d_handles.p, nbytes, cudaMemcpyDeviceToHost, s),
+               "handles readback");
+    int st = wait_stream(sh, "handle exchange");
+    if (st != FRNN_OK) return st;
+    for (int r = 0; r < sh->nranks && local == FRNN_OK; ++r) {
+        if (r == sh->rank) continue;
+        const cudaIpcMemHandle_t* h = reinterpret_cast<const cudaIpcMemHandle_t*>(sh->h_handles + slot * r);
+        for (int b = 0; b < 2 && local == FRNN_OK; ++b) {
+            cudaIpcMemHandle_t& open = b ? sh->open_counts[r] : sh->open_lists[r];
+            int*& ptr = b ? sh->peer_counts[r] : sh->peer_lists[r];
+            if (ptr && !std::memcmp(&open, &h[b], sizeof(open))) continue;
+            if (ptr) cudaIpcCloseMemHandle(ptr);
+            ptr = nullptr;
+            void* p = nullptr;
+            const cudaError_t err = cudaIpcOpenMemHandle(&p, h[b], cudaIpcMemLazyEnablePeerAccess);
+            if (err != cudaSuccess) {
+                local = cuda_fail(e, err, "map another rank's candidate lists");
+                break;
+            }
+            ptr = static_cast<int*>(p);
+            open = h[b];
+        }
+    }
+    sh->h_stat[3] = local;
+    FRNN_CHECK(e, cudaMemcpyAsync(sh->d_stat.p, sh->h_stat + 3, sizeof(int), cudaMemcpyHostToDevice, s),
+               "status upload");
+    SH_NCCL(sh, api->AllReduce(sh->d_stat.p, sh->d_stat.p, 1, ncclInt32, ncclMax, sh->comm, s), "status all-reduce");
+    FRNN_CHECK(e, cudaMemcpyAsync(sh->h_stat + 4, sh->d_stat.p, sizeof(int), cudaMemcpyDeviceToHost, s),
+               "status readback");
+    st = wait_stream(sh, "symmetric filter set-up");
+    if (st != FRNN_OK) return st;
+    if (sh->h_stat[4] != FRNN_OK) {
+        if (local == FRNN_OK) fail(e, sh->h_stat[4], "another rank could not set up the symmetric filter");
+        return sh->h_stat[4];
+    }
+    return FRNN_OK;
+}
+
+// This rank's part of the symmetric filter over its query blocks, a barrier
+// (one all-reduce: every rank's filter has finished), then its own queries
+// [lo, hi): the other ranks' entries for them pulled in, the overflow list,
+// the exact re-rank and the SIMT brute force for overflowing lists.  Every
+// rank runs it, also one with no queries.
+int tc_sym_range(frnn_shard* sh, const ShardHeader& H, const float* pts, int lo, int hi, int cap, int* oi,
+                 float* od) {
+    frnn_engine* e = sh->e;
+    cudaStream_t s = e->stream;
+    const NcclApi* api = nccl_api();
+    const int N = H.N, K = H.K, dim = H.dim, rows = hi - lo;
+    const float r2 = H.radius * H.radius;
+    TcPeers peers;
+    peers.n = sh->nranks;
+    for (int r = 0; r < sh->nranks; ++r) {
+        peers.counts[r] = r == sh->rank ? e->list_counts.as<int>() : sh->peer_counts[r];
+        peers.lists[r] = r == sh->rank ? e->lists.as<int>() : sh->peer_lists[r];
+    }
+    if (rows > 0) {
+        stage_begin(e, ST_TC_FILTER);
+        FRNN_CHECK(e, launch_tc_filter(e->tc_tiles.as<uint8_t>(), e->tc_qa.as<float>(), e->tc_pb.as<float>(), N, dim,
+                                       cap, e->lists.as<int>(), e->list_counts.as<int>(), e->overflow.as<int>(),
+                                       e->n_overflow.as<int>(), e->err_flag.as<int>(), lo / 128, (hi + 127) / 128, s,
+                                       nullptr, N, -1, true, true),
+                   "filter launch");
+        stage_end(e, ST_TC_FILTER);
+        e->launches++;
+    }
+    SH_NCCL(sh, api->AllReduce(sh->d_stat.p, sh->d_stat.p, 1, ncclInt32, ncclMax, sh->comm, s), "filter barrier");
+    if (rows <= 0) return FRNN_OK;
+    FRNN_CHECK(e, launch_tc_pull(peers, sh->rank, e->list_counts.as<int>(), e->lists.as<int>(), lo, hi, cap, s),
+               "pull launch");
+    FRNN_CHECK(e, launch_tc_sym_overflow(e->list_counts.as<int>(), lo, hi, cap, e->overflow.as<int>(),
+                                         e->n_overflow.as<int>(), s),
+               "overflow launch");
+    stage_begin(e, ST_TC_RERANK);
+    FRNN_CHECK(e, launch_tc_rerank(e->tc_rows.as<float>(), dim, e->lists.as<int>(), e->list_counts.as<int>(), cap, N,
+                                   K, r2, oi, od, lo, hi, s),
+               "rerank launch");
+    stage_end(e, ST_TC_RERANK);
+    e->launches += 3;
+    int* h_nov = sh->h_stat + 5;
+    FRNN_CHECK(e, cudaMemcpyAsync(h_nov, e->n_overflow.p, sizeof(int), cudaMemcpyDeviceToHost, s),
+               "overflow count readback");
+    FRNN_CHECK(e, cudaStreamSynchronize(s), "overflow count sync");
+    if (*h_nov > 0) {
+        stage_begin(e, ST_BRUTE);
+        FRNN_CHECK(e, launch_bruteforce(pts, N, dim, K, r2, 0, *h_nov, oi, od, rows, s, e->overflow.as<int>(), lo),
+                   "overflow brute force launch");
+        stage_end(e, ST_BRUTE);
+        e->launches++;
+    }
     return FRNN_OK;
 }
 
@@ -502,7 +672,8 @@ int frnn_shard_create(frnn_engine* e, int nranks, int rank, const unsigned char*
     if (cudaMallocHost(&sh->h_hdr, sizeof(ShardHeader)) != cudaSuccess ||
         cudaMallocHost(&sh->h_stat, 64) != cudaSuccess ||
         cudaMallocHost(&sh->h_work, (size_t)kWorkBuckets * 8) != cudaSuccess ||
-        cudaMallocHost(&sh->h_wstart, (size_t)kWorkBuckets * 4) != cudaSuccess) {
+        cudaMallocHost(&sh->h_wstart, (size_t)kWorkBuckets * 4) != cudaSuccess ||
+        cudaMallocHost(&sh->h_handles, 2 * sizeof(cudaIpcMemHandle_t) * kTcMaxPeers) != cudaSuccess) {
         cudaGetLastError();
         frnn_shard_destroy(sh);
         return fail(e, FRNN_ERR_OOM, "pinned shard staging");
@@ -530,13 +701,18 @@ int frnn_shard_destroy(frnn_shard* sh) {
         if (sh->comm && api) api->CommDestroy(sh->comm);
         if (sh->peer_idx) cudaIpcCloseMemHandle(sh->peer_idx);
         if (sh->peer_dist) cudaIpcCloseMemHandle(sh->peer_dist);
-        for (DevBuf* b : {&sh->d_hdr, &sh->d_stat, &sh->work, &sh->pts, &sh->res_idx, &sh->res_dist, &sh->inv,
+        for (int r = 0; r < kTcMaxPeers; ++r) {
+            if (sh->peer_lists[r]) cudaIpcCloseMemHandle(sh->peer_lists[r]);
+            if (sh->peer_counts[r]) cudaIpcCloseMemHandle(sh->peer_counts[r]);
+        }
+        for (DevBuf* b : {&sh->d_handles, &sh->d_hdr, &sh->d_stat, &sh->work, &sh->pts, &sh->res_idx, &sh->res_dist, &sh->inv,
                           &sh->flags, &sh->fpos, &sh->fstatus, &sh->qlist})
             if (b->p) cudaFree(b->p);
         if (sh->h_hdr) cudaFreeHost(sh->h_hdr);
         if (sh->h_stat) cudaFreeHost(sh->h_stat);
         if (sh->h_work) cudaFreeHost(sh->h_work);
         if (sh->h_wstart) cudaFreeHost(sh->h_wstart);
+        if (sh->h_handles) cudaFreeHost(sh->h_handles);
         for (cudaEvent_t ev : sh->ev)
             if (ev) cudaEventDestroy(ev);
         for (cudaEvent_t ev : sh->chunk_ev)
@@ -578,6 +754,10 @@ int frnn_shard_set_option(frnn_shard* sh, int option, int64_t value) {
             sh->comm_priority = (int)value;
             return FRNN_OK;
         }
+        case FRNN_SHARD_OPT_TC_SYMMETRIC:
+            if (value != 0 && value != 1) return fail(sh->e, FRNN_ERR_INVALID_ARG, "tc symmetric must be 0 or 1");
+            sh->tc_sym = (int)value;
+            return FRNN_OK;
         default:
             return fail(sh->e, FRNN_ERR_INVALID_ARG, "unknown shard option");
     }
@@ -700,8 +880,14 @@ int frnn_search_sharded(frnn_shard* sh, int root, const float* d_points_soa, int
     // 4 and 5. this rank's queries, chunk by chunk; each finished chunk is
     // copied into the root's result block on the communication stream (a copy
     // engine over NVLink) while the next chunk is searched
+    const bool tc_sym = path == FRNN_PATH_BRUTE_TC && H.tc_sym;
+    const int tc_cap = tc_list_cap(K);
     if (path == FRNN_PATH_BRUTE_TC && rows > 0) {
         st = tc_prepare(e, pts, N, dim, H.tc);
+        if (st != FRNN_OK) return st;
+    }
+    if (tc_sym) {
+        st = tc_sym_setup(sh, H, tc_cap);
         if (st != FRNN_OK) return st;
     }
     if (path == FRNN_PATH_GRID && rows > 0) {
@@ -712,17 +898,23 @@ int frnn_search_sharded(frnn_shard* sh, int root, const float* d_points_soa, int
     int* dst_idx = is_root ? sh->res_idx.as<int>() : sh->peer_idx;
     float* dst_dist = is_root ? sh->res_dist.as<float>() : sh->peer_dist;
     int cb[kMaxChunks + 1];
-    const int m = chunk_bounds(lo, hi, path, sh->chunks, cb);
+    // the symmetric filter runs in one piece, on every rank (it holds barriers)
+    const int m = tc_sym ? 1 : chunk_bounds(lo, hi, path, sh->chunks, cb);
+    if (tc_sym) {
+        cb[0] = lo;
+        cb[1] = hi;
+    }
     sh_begin(sh, SH_SEARCH, s);
     sh_begin(sh, SH_GATHER, sh->cs);
-    for (int c = 0; c < m && rows > 0; ++c) {
+    for (int c = 0; c < m && (rows > 0 || tc_sym); ++c) {
         const int c0 = cb[c], c1 = cb[c + 1], n_c = c1 - c0;
-        if (n_c <= 0) continue;
+        if (n_c <= 0 && !tc_sym) continue;
         const size_t off = (size_t)K * (c0 - lo);  // chunk c's [K, n_c] block in this rank's output
         int* oi = e->out_idx.as<int>() + off;
         float* od = e->out_dist.as<float>() + off;
-        st = search_range(sh, H, pts, c0, c1, oi, od);
+        st = tc_sym ? tc_sym_range(sh, H, pts, c0, c1, tc_cap, oi, od) : search_range(sh, H, pts, c0, c1, oi, od);
         if (st != FRNN_OK) return st;
+        if (n_c <= 0) continue;
         FRNN_CHECK(e, cudaEventRecord(sh->chunk_ev[c], s), "chunk event");
         FRNN_CHECK(e, cudaStreamWaitEvent(sh->cs, sh->chunk_ev[c], 0), "chunk wait");
         // [K, n_c] -> columns [c0, c1) of the root's [K, N] results

@@ -398,7 +398,7 @@ class FRNNShard:
         if st != _OK:
             _raise(self._lib, self._engine._eng, st, "shard set_timeout")
 
-    OPT_CHUNKS, OPT_COMM_PRIORITY = 1, 2
+    OPT_CHUNKS, OPT_COMM_PRIORITY, OPT_TC_SYMMETRIC = 1, 2, 3
 
     def set_option(self, option: int, value: int) -> None:
         st = self._lib.frnn_shard_set_option(self._sh, int(option), int(value))

@@ -58,6 +58,33 @@ def main():
                 assert pi == 0 and pd == 0
             assert st["rows"] >= 0
         dist.barrier()
+    # the tensor-core path with the symmetric filter shared between the ranks
+    # (each rank appends into the others' lists) and without it, on a cloud
+    # whose last tile is partial and on one whose lists overflow
+    rng = np.random.default_rng(5)
+    clusters = rng.standard_normal((3000, 48)).astype(np.float32)
+    clusters[:1800] = clusters[np.arange(1800) % 6]
+    tc_cases = [("sphere", datagen.soa(datagen.generate("sphere", 9001, 128, seed=9)), 128, None),
+                ("clusters", datagen.soa(clusters), 16, 0.5)]
+    for name, soa, K, r in tc_cases:
+        D, N = soa.shape
+        if r is None:
+            r = datagen.calibrate_radius(np.ascontiguousarray(soa.T), 64, sample=512)
+        x = torch.from_numpy(np.ascontiguousarray(soa)).cuda()
+        for sym in (1, 0):
+            shard.set_option(shard.OPT_TC_SYMMETRIC, sym)
+            pi, pd = shard.search(0, x.data_ptr() if rank == 0 else 0, N, D, K, r)
+            if rank == 0:
+                got_i = torch.as_tensor(_DeviceArray(pi, (K, N), "<i4"), device="cuda").cpu()
+                got_d = torch.as_tensor(_DeviceArray(pd, (K, N), "<f4"), device="cuda").cpu()
+                ref.set_path("brute_tc")
+                ref.search_gpu(x.data_ptr(), N, D, K, r)
+                ref.set_path("auto")
+                ri, rd = ref.get_results_arrays(N, K)
+                assert_bit_exact(got_i.numpy(), got_d.numpy(), ri, rd, f"tc {name} sym={sym} world={world}")
+                print(f"rank {rank} tc {name} sym={sym} ok {eng.last_plan()} {shard.last_stats()}", flush=True)
+        shard.set_option(shard.OPT_TC_SYMMETRIC, 1)
+        dist.barrier()
     shard.close()
     dist.barrier()
     dist.destroy_process_group()
