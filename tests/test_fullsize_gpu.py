@@ -4,7 +4,7 @@ The configurations are measured at full size, and full size is where the
 paths differ from the small clouds the other files use (a 12M-cell table and
 overflowing candidate lists for configuration 2, a 6-axis principal grid of
 78M cells for configuration 4, the fp16 filter margin and its overflow pass
-for configuration 5).  So each one is searched here at its BASELINE size,
+for configuration 5).  So each one is searched here at its benchmark size,
 through frnn_search_gpu, and checked bit for bit against the CPU oracle:
 
 * configurations 1 and 2: every query (and configuration 2 once more with a
