@@ -497,11 +497,12 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
             # writes K results
             "tc_prep": N * D * 4 + N * ((D + 63) // 64 * 64) * 2 + N * ((D + 3) // 4 * 4) * 4 + 8 * N,
             "tc_rerank": N * c.target * (((D + 3) // 4 * 4) * 4 + 4) + N * K * 8,
-            # the filter is a dense contraction over every pair, or over every
-            # unordered pair once in a whole self-search (tc_filter_flops)
-            "tc_filter": tc_filter_flops(N, D, not strong),
+            # the filter is a dense contraction over every unordered pair once
+            # (tc_filter_flops); a sharded search on 2..8 ranks shares that
+            # triangle equally between the ranks
+            "tc_filter": tc_filter_flops(N, D, True) / (world if strong else 1),
         }[dom]
-        if dom in ("search", "collect", "emit", "tc_rerank", "tc_filter", "brute", "unpermute"):
+        if dom in ("search", "collect", "emit", "tc_rerank", "brute", "unpermute"):
             alg *= qf
         t = stage_ms[dom] / 1e3
         traffic = None
