@@ -500,7 +500,8 @@ def run_engine_arm(a, torch, dist, rank, world, dev):
             # the filter is a dense contraction over every unordered pair once
             # (tc_filter_flops); a sharded search on 2..8 ranks shares that
             # triangle equally between the ranks
-            "tc_filter": tc_filter_flops(N, D, True) / (world if strong else 1),
+            "tc_filter": (tc_filter_flops(N, D, True) / world if world <= 8 else 2.0 * N * N * D * qf)
+                         if strong else tc_filter_flops(N, D, True),
         }[dom]
         if dom in ("search", "collect", "emit", "tc_rerank", "brute", "unpermute"):
             alg *= qf
