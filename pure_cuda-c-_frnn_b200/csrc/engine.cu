@@ -509,7 +509,8 @@ int search_built(frnn_engine* e, const GridPlan& P, bool principal, int K, float
         FRNN_GROW(e, e->list_counts, (size_t)N * 4);
         FRNN_GROW(e, e->overflow, (size_t)N * 4);
         FRNN_GROW(e, e->n_overflow, 16);
-        FRNN_CHECK(e, cudaMemsetAsync(e->n_overflow.p, 0, 4, s), "memset overflow count");
+        // (a device-planned search zeroed it with its count table)
+        if (!Pd) FRNN_CHECK(e, cudaMemsetAsync(e->n_overflow.p, 0, 4, s), "memset overflow count");
         e->last_overflow_map = whole ? 1 : 0;
         stage_begin(e, ST_COLLECT);
         if (d3)
@@ -643,20 +644,23 @@ int run_grid_dplan(frnn_engine* e, const float* d_pts, int N, int dim, int K, fl
         if (st != FRNN_OK) return st;
     }
     FRNN_GROW(e, e->dplan, sizeof(GridPlan));
+    FRNN_GROW(e, e->n_overflow, 16);
     FRNN_GROW(e, e->cellrank, (size_t)N * 8);
     FRNN_GROW(e, e->rows, ((size_t)N + kCollectRowPad) * P.row * 4);
     FRNN_GROW(e, e->ids, (size_t)N * 4);
     if (lists) FRNN_GROW(e, e->inv, (size_t)N * 4);
     GridPlan* Pd = e->dplan.as<GridPlan>();
 
-    FRNN_CHECK(e, cudaMemsetAsync(e->scan_ticket.p, 0, 4, s), "memset scan ticket");
     const int blocks = std::min(bbox_blocks(N, e->sms), kBoxMaxBlocks);
     stage_begin(e, ST_BBOX);
     FRNN_CHECK(e, launch_bbox(d_pts, N, g, e->box_partial.as<float>(), e->box_ticket.as<unsigned>(),
                               e->box_out.as<float>(), blocks, s, Pd, dim, radius, budget),
                "bbox launch");
     stage_end(e, ST_BBOX);
-    FRNN_CHECK(e, launch_clear_counts(e->counts.as<int>(), budget, Pd, e->sms, s), "clear counts launch");
+    // the count table, the scan's ticket and the overflow count, in one kernel
+    FRNN_CHECK(e, launch_clear_counts(e->counts.as<int>(), budget, Pd, e->sms, s, e->scan_ticket.as<int>(),
+                                      e->n_overflow.as<int>()),
+               "clear counts launch");
     stage_begin(e, ST_HASH);
     FRNN_CHECK(e, launch_hash_count(d_pts, P, e->counts.as<int>(), e->cellrank.as<int2>(), s, nullptr, Pd),
                "hash_count launch");

@@ -33,9 +33,10 @@ cudaError_t launch_scan(const int* counts, int* starts, long long cells,
                         unsigned long long* status, int* ticket, unsigned epoch, int* err,
                         cudaStream_t s, int withhold = -1, const GridPlan* Pd = nullptr);
 // counts[0, Pd->cells) = 0 for a plan made on the device (max_cells: the
-// largest table it may have, which sizes the launch)
+// largest table it may have, which sizes the launch); zero0 / zero1
+// (optional): two more words set to 0
 cudaError_t launch_clear_counts(int* counts, long long max_cells, const GridPlan* Pd, int sms,
-                                cudaStream_t s);
+                                cudaStream_t s, int* zero0 = nullptr, int* zero1 = nullptr);
 // inv (optional): inv[original index] = sorted position; proj (optional, D > 3):
 // projected coordinates copied to proj_sorted in cell order
 cudaError_t launch_scatter(const float* pts, const GridPlan& P, const int2* cellrank,

@@ -322,9 +322,16 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const int* __restric
 
 // counts[0, Pd->cells) = 0: the memset of the host-planned build, for a table
 // whose size only the device knows.  Like that memset, it leaves the table in
-// L2 for the histogram's atomics that follow.
+// L2 for the histogram's atomics that follow.  zero0 / zero1 (optional): two
+// more words to clear (the scan's ticket, the overflow count), so the
+// device-planned search needs no separate memsets between its kernels.
 __global__ void __launch_bounds__(256) clear_counts_kernel(int* __restrict__ counts,
-                                                           const GridPlan* __restrict__ Pd) {
+                                                           const GridPlan* __restrict__ Pd,
+                                                           int* __restrict__ zero0, int* __restrict__ zero1) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        if (zero0) *zero0 = 0;
+        if (zero1) *zero1 = 0;
+    }
     const long long cells = Pd->cells;
     const long long n4 = cells >> 2;
     const long long step = (long long)gridDim.x * blockDim.x;
@@ -423,10 +430,10 @@ cudaError_t launch_scan(const int* counts, int* starts, long long cells,
 }
 
 cudaError_t launch_clear_counts(int* counts, long long max_cells, const GridPlan* Pd, int sms,
-                                cudaStream_t s) {
+                                cudaStream_t s, int* zero0, int* zero1) {
     const long long want = (max_cells / 4 + 255) / 256;
     const int blocks = (int)std::max<long long>(1, std::min<long long>(want, 8LL * sms));
-    clear_counts_kernel<<<blocks, 256, 0, s>>>(counts, Pd);
+    clear_counts_kernel<<<blocks, 256, 0, s>>>(counts, Pd, zero0, zero1);
     return cudaGetLastError();
 }
 
