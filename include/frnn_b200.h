@@ -345,6 +345,15 @@ int frnn_shard_last_stats(frnn_shard* sh, float* stage_ms, int n, int64_t* bcast
 int frnn_shard_partition(const uint64_t* tile_work, const int* tile_start, int64_t tiles, int N, int nparts,
                          int* bounds);
 
+/* The partition of a sharded tensor-core search that shares the symmetric
+ * filter (FRNN_SHARD_OPT_TC_SYMMETRIC, host code, no GPU): query block b
+ * (128 queries) filters the ceil(N/128) - b point tiles at or above it, plus
+ * about 0.35 tile's worth of re-rank, and bounds[0..nparts] cut the blocks,
+ * in pairs (multiples of 256 queries, or N), into equal shares of that work;
+ * rank r owns [bounds[r], bounds[r+1]).  The reference's brute force runs
+ * on one GPU (no_grid_frnn.cu:121-326); no counterpart. */
+int frnn_shard_tc_partition(int N, int nparts, int* bounds);
+
 /* Allocation-free search.  No counterpart in the reference: it is for callers
  * that cannot allocate device memory while they search (a framework whose own
  * pool owns all device memory, a real-time loop with a fixed budget, code that

@@ -271,31 +271,6 @@ __global__ void compact_kernel(const int* __restrict__ flags, const int* __restr
     if ((unsigned)p < (unsigned)cap) qlist[p] = sq;
 }
 
-// Owners' ranges for the symmetric tensor-core filter: query block b filters
-// the tiles t >= b, so block b costs T - b tiles, and its re-rank about
-// kRerankTiles more (B200, cfg5: 15.5 ms of re-rank for 7,813 blocks against
-// 177 ms of filter for 30.5M tiles); ranges are cut at even blocks (the
-// filter's CTAs take blocks in pairs) so that every rank gets an equal share.
-constexpr double kRerankTiles = 0.35;
-void tc_sym_bounds(int N, int parts, int* bounds) {
-    const long long T = (N + 127) / 128, pairs = (T + 1) / 2;
-    auto pair_work = [&](long long j) {
-        return (long double)((T - 2 * j) + (2 * j + 1 < T ? T - 2 * j - 1 + kRerankTiles : 0.0)) + kRerankTiles;
-    };
-    long double total = 0.0L;
-    for (long long j = 0; j < pairs; ++j) total += (long double)pair_work(j);
-    bounds[0] = 0;
-    long long j = 0;
-    long double before = 0.0L;
-    for (int r = 1; r < parts; ++r) {
-        const long double target = total * r / parts;
-        while (j < pairs && before + pair_work(j) <= target) before += (long double)pair_work(j++);
-        if (j < pairs && target - before > 0.5L * (long double)pair_work(j)) before += (long double)pair_work(j++);
-        bounds[r] = (int)std::min<long long>(N, j * 256);
-    }
-    bounds[parts] = N;
-}
-
 // Step 1 on the root: plan, build and the owners' ranges into h_hdr.
 int root_plan(frnn_shard* sh, const float* d_pts, int N, int dim, int K, float radius) {
     frnn_engine* e = sh->e;
@@ -344,7 +319,7 @@ int root_plan(frnn_shard* sh, const float* d_pts, int N, int dim, int K, float r
     } else if (H.path == FRNN_PATH_BRUTE_TC) {
         H.tc_sym = sh->tc_sym && e->tc_symmetric && parts > 1 && parts <= kTcMaxPeers ? 1 : 0;
         if (H.tc_sym) {
-            tc_sym_bounds(N, parts, H.bounds);
+            frnn_shard_tc_partition(N, parts, H.bounds);
         } else {
             // whole 128-query tiles; every query costs the same
             const int ntq = (N + 127) / 128;
@@ -610,6 +585,33 @@ int search_range(frnn_shard* sh, const ShardHeader& H, const float* pts, int lo,
 }  // namespace
 
 extern "C" {
+
+// Owners' ranges for the symmetric tensor-core filter: query block b filters
+// the tiles t >= b, so block b costs T - b tiles, and its re-rank about
+// kRerankTiles more (B200, cfg5: 15.5 ms of re-rank for 7,813 blocks against
+// 177 ms of filter for 30.5M tiles); ranges are cut at even blocks (the
+// filter's CTAs take blocks in pairs) so that every rank gets an equal share.
+int frnn_shard_tc_partition(int N, int nparts, int* bounds) {
+    if (!bounds || N < 0 || nparts < 1 || nparts > kMaxShardRanks) return FRNN_ERR_INVALID_ARG;
+    constexpr double kRerankTiles = 0.35;
+    const long long T = ((long long)N + 127) / 128, pairs = (T + 1) / 2;
+    auto pair_work = [&](long long j) {
+        return (long double)((T - 2 * j) + (2 * j + 1 < T ? T - 2 * j - 1 + kRerankTiles : 0.0)) + kRerankTiles;
+    };
+    long double total = 0.0L;
+    for (long long j = 0; j < pairs; ++j) total += pair_work(j);
+    bounds[0] = 0;
+    long long j = 0;
+    long double before = 0.0L;
+    for (int r = 1; r < nparts; ++r) {
+        const long double target = total * r / nparts;
+        while (j < pairs && before + pair_work(j) <= target) before += pair_work(j++);
+        if (j < pairs && target - before > 0.5L * pair_work(j)) before += pair_work(j++);
+        bounds[r] = (int)std::min<long long>(N, j * 256);
+    }
+    bounds[nparts] = N;
+    return FRNN_OK;
+}
 
 int frnn_shard_partition(const uint64_t* tile_work, const int* tile_start, int64_t tiles, int N, int nparts,
                          int* bounds) {

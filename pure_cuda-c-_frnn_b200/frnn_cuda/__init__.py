@@ -89,6 +89,7 @@ def load_library() -> ctypes.CDLL:
         "frnn_shard_last_stats": (I, [P, ctypes.POINTER(F), I, ctypes.POINTER(L), ctypes.POINTER(L),
                                       ctypes.POINTER(I)]),
         "frnn_shard_partition": (I, [P, P, L, I, I, P]),
+        "frnn_shard_tc_partition": (I, [I, I, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -346,6 +347,18 @@ def shard_partition(tile_work, tile_start, N: int, nparts: int) -> np.ndarray:
     st = lib.frnn_shard_partition(w.ctypes.data, t.ctypes.data, len(w), int(N), int(nparts), out.ctypes.data)
     if st != _OK:
         _raise(lib, None, st, "shard_partition")
+    return out
+
+
+def shard_tc_partition(N: int, nparts: int) -> np.ndarray:
+    """The cut points of a sharded tensor-core search that shares the
+    symmetric filter (frnn_shard_tc_partition, host code): bounds[0..nparts],
+    rank r owns queries [bounds[r], bounds[r+1])."""
+    lib = load_library()
+    out = np.empty(int(nparts) + 1, dtype=np.int32)
+    st = lib.frnn_shard_tc_partition(int(N), int(nparts), out.ctypes.data)
+    if st != _OK:
+        _raise(lib, None, st, "shard_tc_partition")
     return out
 
 

@@ -60,3 +60,34 @@ def test_rejects_bad_arguments():
         frnn_cuda.shard_partition([1, 2], [0], 10, 2)
     with pytest.raises(ValueError):
         frnn_cuda.shard_partition([1], [0], 10, 0)
+
+
+# The sharded tensor-core search that shares the symmetric filter: query
+# block b (128 queries) filters the T - b tiles at or above it plus about
+# 0.35 tile of re-rank; the ranks get equal shares, cut between pairs of
+# blocks (frnn_shard_tc_partition).
+def tc_block_work(N):
+    T = (N + 127) // 128
+    return (T - np.arange(T)) + 0.35
+
+
+@pytest.mark.parametrize("N,nparts", [(1_000_000, 2), (1_000_000, 4), (1_000_000, 8), (300_001, 3),
+                                      (65_536, 8), (9_001, 2), (1_000, 4), (0, 3), (5, 1)])
+def test_tc_partition_covers_and_balances(N, nparts):
+    b = frnn_cuda.shard_tc_partition(N, nparts)
+    assert b[0] == 0 and b[-1] == N and (np.diff(b) >= 0).all(), b
+    assert all(x % 256 == 0 for x in b[1:-1] if x < N), b
+    w = tc_block_work(N)
+    if N == 0 or nparts == 1:
+        return
+    blocks = [(lo // 128, (hi + 127) // 128) for lo, hi in zip(b[:-1], b[1:])]
+    share = np.array([w[a:z].sum() for a, z in blocks]) / w.sum()
+    # each cut is within one pair of blocks of its quantile
+    pair = 2 * w[0] / w.sum()
+    assert np.abs(np.cumsum(share)[:-1] - np.arange(1, nparts) / nparts).max() <= pair + 1e-12, share
+
+
+def test_tc_partition_rejects_bad_arguments():
+    for N, nparts in [(-1, 2), (100, 0), (100, 65)]:
+        with pytest.raises((ValueError, frnn_cuda.FRNNError)):
+            frnn_cuda.shard_tc_partition(N, nparts)
